@@ -1,0 +1,411 @@
+// ffn_capi.cu -- the extern "C" entry points declared in include/ffnerf.h.
+//
+// One ffn_ctx per device and model: it owns the parameter blob, the Adam moments, the hash
+// table, both occupancy grids, the gradient buffer and the per-CTA weight-gradient partials.
+// Callers own rays / targets / outputs (device pointers).  Every entry point is stream-ordered
+// and returns a status code; nothing synchronises the device except ffn_create/ffn_destroy.
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "ffn_common.cuh"
+#include "ffn_step.cu"
+
+using namespace ffn;
+
+struct ffn_ctx {
+    ffn_config cfg;
+    int device = 0;
+    DevConfig dc{};
+    ParamLayout lo{};
+    size_t table_floats = 0;
+    int Pw = 0;
+    float* params = nullptr;
+    float* adam_m = nullptr;
+    float* adam_v = nullptr;
+    float* table = nullptr;
+    float* table_m = nullptr;
+    float* table_v = nullptr;
+    uint32_t* occ_in = nullptr;
+    uint32_t* occ_st = nullptr;
+    float* grads = nullptr;      // [table_floats + Pw]
+    float* partials = nullptr;   // [max_grid * Pw]
+    int max_grid = 0;
+    int rows = 0;
+    size_t smem = 0;
+    void (*kernel)(StepArgs) = nullptr;
+    std::string err;
+};
+
+namespace {
+
+thread_local std::string g_create_err;
+
+int fail(ffn_ctx* ctx, int code, const std::string& msg) {
+    if (ctx) ctx->err = msg; else g_create_err = msg;
+    return code;
+}
+
+int cuda_fail(ffn_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, FFN_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <int F, int ND, int NC, int ROWS>
+void bind_kernel(ffn_ctx* c) {
+    c->kernel = fused_step_kernel<F, ND, NC, ROWS>;
+    c->rows = ROWS;
+    c->smem = (size_t)Smem<F, ND, NC, ROWS>::floats(c->Pw) * sizeof(float);
+}
+
+// The (F, ND, NC) combinations compiled into this library; the tile height is the largest of
+// 128 / 64 samples whose shared-memory footprint fits in one SM.
+bool select_kernel(ffn_ctx* c) {
+    const ffn_config& g = c->cfg;
+    if (g.NC != 2) return false;
+    if (g.F == 2 && g.ND == 1) { bind_kernel<2, 1, 2, 128>(c); return true; }
+    if (g.F == 4 && g.ND == 1) { bind_kernel<4, 1, 2, 128>(c); return true; }
+    if (g.F == 2 && g.ND == 2) { bind_kernel<2, 2, 2, 64>(c); return true; }
+    if (g.F == 4 && g.ND == 2) { bind_kernel<4, 2, 2, 64>(c); return true; }
+    return false;
+}
+
+int check_config(const ffn_config* g, std::string* why) {
+    if (g->F != 2 && g->F != 4) { *why = "F (features per level) must be 2 or 4"; return FFN_E_CONFIG; }
+    if (g->ND < 1 || g->ND > 3 || g->NC < 1 || g->NC > 4) { *why = "ND must be 1..3 and NC 1..4"; return FFN_E_CONFIG; }
+    if (g->spr != 16 && g->spr != 32 && g->spr != 64) {
+        *why = "samples_per_ray must be 16, 32 or 64 (power of two, <= S_MAX=64)";
+        return FFN_E_CONFIG;
+    }
+    if (g->G < 1 || g->G > 1024) { *why = "occupancy grid side must be 1..1024"; return FFN_E_CONFIG; }
+    if (g->background < 0 || g->background > 2) { *why = "background must be 0 (black), 1 (white) or 2 (random)"; return FFN_E_CONFIG; }
+    uint64_t expect = 0;
+    for (int l = 0; l < FFN_N_LEVELS; ++l) {
+        if (g->level_log2[l] < 1 || g->level_log2[l] > 24) { *why = "per-level table size must be 2^1..2^24"; return FFN_E_CONFIG; }
+        if (g->level_offset[l] != expect) { *why = "level offsets must be the running sum of the level sizes"; return FFN_E_CONFIG; }
+        if (g->level_res[l] < 2) { *why = "level resolution must be >= 2"; return FFN_E_CONFIG; }
+        expect += 1ull << g->level_log2[l];
+    }
+    if (expect * (uint64_t)g->F >= (1ull << 32)) { *why = "hash table too large (>= 2^32 floats)"; return FFN_E_CONFIG; }
+    for (int i = 0; i < 3; ++i)
+        if (!(g->box_max[i] > g->box_min[i])) { *why = "box_max must exceed box_min"; return FFN_E_CONFIG; }
+    return FFN_OK;
+}
+
+void fill_dev_config(ffn_ctx* c) {
+    DevConfig& d = c->dc;
+    const ffn_config& g = c->cfg;
+    d.F = g.F; d.ND = g.ND; d.NC = g.NC; d.spr = g.spr; d.G = g.G; d.background = g.background;
+    for (int l = 0; l < L; ++l) {
+        d.level_log2[l] = g.level_log2[l];
+        d.level_offset[l] = g.level_offset[l];
+        d.level_res[l] = g.level_res[l];
+        d.hash_lr_scale[l] = g.hash_lr_scale[l];
+    }
+    for (int i = 0; i < 3; ++i) { d.bmin[i] = g.box_min[i]; d.bmax[i] = g.box_max[i]; }
+    d.rho_min = g.rho_min; d.rho_max = g.rho_max; d.dt_min = g.dt_min; d.dt_max = g.dt_max;
+    d.t_near = g.t_near; d.t_far = g.t_far;
+}
+
+StepArgs base_args(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
+                   const ffn_step_scalars* s) {
+    StepArgs a{};
+    a.c = c->dc;
+    a.lo = c->lo;
+    a.params = c->params;
+    a.table = c->table;
+    a.occ_in = c->occ_in;
+    a.occ_st = c->occ_st;
+    a.rays = static_cast<const float4*>(rays);
+    a.targets = static_cast<const float4*>(targets);
+    a.out = static_cast<float4*>(out);
+    a.grad_table = c->grads;
+    a.partials = c->partials;
+    a.n_rays = n;
+    a.ray_offset = s->ray_offset;
+    a.sh_mult = s->sh_mult;
+    a.occ_strength = s->occ_strength;
+    a.seed = s->rng_u32;
+    return a;
+}
+
+int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) {
+    const int rpt = c->rows / c->cfg.spr;
+    const int n_tiles = (int)((a.n_rays + (uint32_t)rpt - 1) / (uint32_t)rpt);
+    const int grid = n_tiles < c->max_grid ? n_tiles : c->max_grid;
+    if (grid_out) *grid_out = grid;
+    if (grid == 0) return FFN_OK;
+    c->kernel<<<grid, c->rows, c->smem, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "fused step launch");
+    return FFN_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int ffn_abi_version(void) { return FFN_ABI_VERSION; }
+
+const char* ffn_last_error(const ffn_ctx* ctx) { return ctx ? ctx->err.c_str() : g_create_err.c_str(); }
+
+int ffn_param_layout(const ffn_config* cfg, int32_t* offsets18, int32_t* sizes18) {
+    if (!cfg) return FFN_E_CONFIG;
+    ParamLayout lo = make_param_layout(cfg->F, cfg->ND, cfg->NC);
+    for (int i = 0; i < P_COUNT; ++i) {
+        if (offsets18) offsets18[i] = lo.off[i];
+        if (sizes18) sizes18[i] = lo.size[i];
+    }
+    return lo.total;
+}
+
+int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
+    if (!cfg || !out) return fail(nullptr, FFN_E_CONFIG, "null argument");
+    *out = nullptr;
+    std::string why;
+    if (check_config(cfg, &why) != FFN_OK) return fail(nullptr, FFN_E_CONFIG, why);
+    ffn_ctx* c = new ffn_ctx();
+    c->cfg = *cfg;
+    c->device = device;
+    c->lo = make_param_layout(cfg->F, cfg->ND, cfg->NC);
+    c->Pw = c->lo.total;
+    uint64_t entries = 0;
+    for (int l = 0; l < L; ++l) entries += 1ull << cfg->level_log2[l];
+    c->table_floats = (size_t)entries * cfg->F;
+    fill_dev_config(c);
+    if (!select_kernel(c)) {
+        delete c;
+        return fail(nullptr, FFN_E_CONFIG, "this (F, ND, NC) combination is not compiled: supported are NC=2 with "
+                                           "(F, ND) in {(2,1), (4,1), (2,2), (4,2)}");
+    }
+    DeviceGuard guard(device);
+    cudaError_t e;
+    int sms = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) {
+        delete c;
+        return cuda_fail(nullptr, e, "device query");
+    }
+    int max_smem = 0;
+    cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if ((int)c->smem > max_smem) {
+        delete c;
+        return fail(nullptr, FFN_E_CONFIG, "configuration needs more shared memory than the device offers");
+    }
+    if ((e = cudaFuncSetAttribute(c->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->smem)) != cudaSuccess) {
+        delete c;
+        return cuda_fail(nullptr, e, "shared-memory attribute");
+    }
+    c->max_grid = sms;
+    const size_t Pb = (size_t)c->Pw * sizeof(float);
+    const size_t Tb = c->table_floats * sizeof(float);
+    const size_t Gb = (size_t)cfg->G * cfg->G * cfg->G * sizeof(uint32_t);
+    struct { void** p; size_t n; } allocs[] = {
+        {(void**)&c->params, Pb}, {(void**)&c->adam_m, Pb}, {(void**)&c->adam_v, Pb},
+        {(void**)&c->table, Tb}, {(void**)&c->occ_in, Gb}, {(void**)&c->occ_st, Gb},
+        {(void**)&c->grads, Tb + Pb}, {(void**)&c->partials, (size_t)c->max_grid * Pb}};
+    for (auto& al : allocs) {
+        if ((e = cudaMalloc(al.p, al.n)) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "device allocation"); }
+        cudaMemset(*al.p, 0, al.n);
+    }
+    if (cfg->table_optimizer == 1) {
+        if ((e = cudaMalloc((void**)&c->table_m, Tb)) != cudaSuccess || (e = cudaMalloc((void**)&c->table_v, Tb)) != cudaSuccess) {
+            ffn_destroy(c);
+            return cuda_fail(nullptr, e, "device allocation");
+        }
+        cudaMemset(c->table_m, 0, Tb);
+        cudaMemset(c->table_v, 0, Tb);
+    }
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "initialisation"); }
+    *out = c;
+    return FFN_OK;
+}
+
+int ffn_destroy(ffn_ctx* c) {
+    if (!c) return FFN_OK;
+    DeviceGuard guard(c->device);
+    cudaDeviceSynchronize();
+    void* ptrs[] = {c->params, c->adam_m, c->adam_v, c->table, c->table_m, c->table_v, c->occ_in,
+                    c->occ_st, c->grads, c->partials};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    delete c;
+    return FFN_OK;
+}
+
+int ffn_buffer(ffn_ctx* c, int id, void** dev, size_t* bytes) {
+    if (!c || !dev || !bytes) return fail(c, FFN_E_CONFIG, "null argument");
+    const size_t Pb = (size_t)c->Pw * sizeof(float), Tb = c->table_floats * sizeof(float);
+    const size_t Gb = (size_t)c->cfg.G * c->cfg.G * c->cfg.G * sizeof(uint32_t);
+    switch (id) {
+        case FFN_BUF_PARAMS: *dev = c->params; *bytes = Pb; break;
+        case FFN_BUF_ADAM_M: *dev = c->adam_m; *bytes = Pb; break;
+        case FFN_BUF_ADAM_V: *dev = c->adam_v; *bytes = Pb; break;
+        case FFN_BUF_TABLE: *dev = c->table; *bytes = Tb; break;
+        case FFN_BUF_OCC_IN: *dev = c->occ_in; *bytes = Gb; break;
+        case FFN_BUF_OCC_ST: *dev = c->occ_st; *bytes = Gb; break;
+        case FFN_BUF_GRADS: *dev = c->grads; *bytes = Tb + Pb; break;
+        case FFN_BUF_TABLE_M: *dev = c->table_m; *bytes = c->table_m ? Tb : 0; break;
+        case FFN_BUF_TABLE_V: *dev = c->table_v; *bytes = c->table_v ? Tb : 0; break;
+        default: return fail(c, FFN_E_NAME, "unknown buffer id");
+    }
+    return FFN_OK;
+}
+
+int ffn_grad_buffer(ffn_ctx* c, void** dev, size_t* n_floats) {
+    if (!c || !dev || !n_floats) return fail(c, FFN_E_CONFIG, "null argument");
+    *dev = c->grads;
+    *n_floats = c->table_floats + (size_t)c->Pw;
+    return FFN_OK;
+}
+
+static int check_io(ffn_ctx* c, const void* rays, const void* out, uint32_t n, const ffn_step_scalars* s) {
+    if (!c) return FFN_E_CONFIG;
+    if (!s) return fail(c, FFN_E_CONFIG, "null step scalars");
+    if (n == 0) return FFN_OK;
+    if (!rays || !out) return fail(c, FFN_E_CONFIG, "rays and out must be device pointers");
+    if (!aligned16(rays) || !aligned16(out)) return fail(c, FFN_E_CONFIG, "rays/out must be 16-byte aligned");
+    if ((uint64_t)n * (uint64_t)c->cfg.spr >= (1ull << 31)) return fail(c, FFN_E_CAPACITY, "too many samples in one call");
+    return FFN_OK;
+}
+
+int ffn_forward_backward(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
+                         const ffn_step_scalars* s, void* stream) {
+    int rc = check_io(c, rays, out, n, s);
+    if (rc != FFN_OK || n == 0) return rc;
+    if (!targets || !aligned16(targets)) return fail(c, FFN_E_CONFIG, "targets must be a 16-byte aligned device pointer");
+    DeviceGuard guard(c->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    StepArgs a = base_args(c, rays, targets, out, n, s);
+    a.do_train = 1;
+    a.grad_table = c->grads;
+    int grid = 0;
+    if ((rc = launch_fused(c, a, st, &grid)) != FFN_OK) return rc;
+    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "gradient reduction launch");
+}
+
+int ffn_apply_updates(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
+    if (!c || !s) return fail(c, FFN_E_CONFIG, "null argument");
+    DeviceGuard guard(c->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const ffn_config& g = c->cfg;
+    mlp_adam_kernel<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->params, c->grads + c->table_floats, c->adam_m,
+                                                         c->adam_v, c->Pw, c->lo.off[P_WC_IN], c->lo.off[P_BD_0],
+                                                         c->lo.off[P_BC_0], s->lr_t, s->color_rel_lr,
+                                                         g.adam_beta1, g.adam_beta2, g.adam_eps);
+    LevelCoef lc{};
+    for (int l = 0; l < L; ++l) {
+        lc.start[l] = g.level_offset[l] * (uint32_t)g.F;
+        lc.coef[l] = g.table_optimizer == 1 ? s->table_lr_t * g.hash_lr_scale[l]
+                                            : -(s->lr_f * g.hash_lr_scale[l]) * 0.5f;   // HASH_LR_RATE
+    }
+    lc.start[L] = (uint32_t)c->table_floats;
+    const uint32_t n4 = (uint32_t)(c->table_floats / 4);
+    const int blocks = (int)((n4 + 255) / 256 < 148u * 16u ? (n4 + 255) / 256 : 148u * 16u);
+    if (g.table_optimizer == 1)
+        table_adam_kernel<<<blocks, 256, 0, st>>>(c->table, c->grads, c->table_m, c->table_v, n4, lc,
+                                                   g.adam_beta1, g.adam_beta2, g.table_adam_eps);
+    else
+        table_sgd_kernel<<<blocks, 256, 0, st>>>(c->table, c->grads, n4, lc);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "update launch");
+}
+
+int ffn_train_step(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
+                   const ffn_step_scalars* s, void* stream) {
+    int rc = ffn_forward_backward(c, rays, targets, out, n, s, stream);
+    if (rc != FFN_OK) return rc;
+    return ffn_apply_updates(c, s, stream);
+}
+
+int ffn_render(ffn_ctx* c, const void* rays, void* out, uint32_t n, const ffn_step_scalars* s, void* stream) {
+    int rc = check_io(c, rays, out, n, s);
+    if (rc != FFN_OK || n == 0) return rc;
+    DeviceGuard guard(c->device);
+    StepArgs a = base_args(c, rays, nullptr, out, n, s);
+    a.do_train = 0;
+    a.partials = nullptr;
+    return launch_fused(c, a, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int ffn_probe(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
+              const ffn_step_scalars* s, const void* bypass, float* t, float* dt, int32_t* idx,
+              uint32_t* flags, float* sigma, float* rgb, float* trans, void* stream) {
+    int rc = check_io(c, rays, out, n, s);
+    if (rc != FFN_OK || n == 0) return rc;
+    if (bypass && !aligned16(bypass)) return fail(c, FFN_E_CONFIG, "bypass must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    StepArgs a = base_args(c, rays, targets, out, n, s);
+    a.do_train = 1;
+    a.partials = nullptr;
+    a.probe = 1;
+    a.bypass = static_cast<const float4*>(bypass);
+    a.dbg_t = t; a.dbg_dt = dt; a.dbg_idx = idx; a.dbg_flags = flags;
+    a.dbg_sigma = sigma; a.dbg_rgb = rgb; a.dbg_trans = trans;
+    return launch_fused(c, a, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int ffn_occ_maintenance(ffn_ctx* c, uint32_t decay_q24, uint32_t seed, void* stream) {
+    if (!c) return FFN_E_CONFIG;
+    if (decay_q24 > (1u << 24)) return fail(c, FFN_E_CONFIG, "decay_q24 must be in [0, 2^24]");
+    DeviceGuard guard(c->device);
+    const uint32_t n = (uint32_t)c->cfg.G * c->cfg.G * c->cfg.G;
+    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    occ_decay_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(c->occ_in, c->occ_st, n, decay_q24, seed);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "decay launch");
+}
+
+int ffn_hash_encode(ffn_ctx* c, const float* pts, float* enc, int64_t n, void* stream) {
+    if (!c || (n > 0 && (!pts || !enc))) return fail(c, FFN_E_CONFIG, "null argument");
+    if (n <= 0) return FFN_OK;
+    if (!aligned16(enc)) return fail(c, FFN_E_CONFIG, "enc must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    const int blocks = (int)((n + 255) / 256 < 148 * 32 ? (n + 255) / 256 : 148 * 32);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (c->cfg.F == 2) hash_fwd_kernel<2><<<blocks, 256, 0, st>>>(c->dc, c->table, pts, n, enc);
+    else hash_fwd_kernel<4><<<blocks, 256, 0, st>>>(c->dc, c->table, pts, n, enc);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "hash encode launch");
+}
+
+int ffn_hash_encode_bwd(ffn_ctx* c, const float* pts, const float* denc, int64_t n, void* stream) {
+    if (!c || (n > 0 && (!pts || !denc))) return fail(c, FFN_E_CONFIG, "null argument");
+    if (n <= 0) return FFN_OK;
+    if (!aligned16(denc)) return fail(c, FFN_E_CONFIG, "denc must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    const int blocks = (int)((n + 255) / 256 < 148 * 32 ? (n + 255) / 256 : 148 * 32);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (c->cfg.F == 2) hash_bwd_kernel<2><<<blocks, 256, 0, st>>>(c->dc, c->grads, pts, denc, n);
+    else hash_bwd_kernel<4><<<blocks, 256, 0, st>>>(c->dc, c->grads, pts, denc, n);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "hash scatter launch");
+}
+
+int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float b1, float b2,
+             float eps, void* stream) {
+    if (n <= 0) return FFN_OK;
+    if (!p || !g || !m || !v) return FFN_E_CONFIG;
+    if (!aligned16(p) || !aligned16(g) || !aligned16(m) || !aligned16(v)) return FFN_E_CONFIG;
+    const int64_t n4 = (n + 3) / 4;
+    const int blocks = (int)((n4 + 255) / 256 < 148 * 16 ? (n4 + 255) / 256 : 148 * 16);
+    adam_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p, g, m, v, n, lr_t, b1, b2, eps);
+    return cudaGetLastError() == cudaSuccess ? FFN_OK : FFN_E_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,148 @@
+/*
+ * ffnerf.h -- C ABI of the B200 fused NeRF training step (libffnerf.so).
+ *
+ * Drop-in for the device side of the reference's PyOpenCL path (MolSzabi/ffnerf-experimental):
+ * the host module ffnerf_tools.py binds these entry points with ctypes in place of the three
+ * OpenCL programs it builds and launches.  Plain pointers and sizes only; device pointers are
+ * CUDA global-memory addresses on the context's device, `stream` is a cudaStream_t (NULL = the
+ * legacy default stream).  Every function returns 0 on success or a negative FFN_E* code; the
+ * message of the last failure is available from ffn_last_error().
+ *
+ * Reference interfaces replaced (paths relative to the reference repository root):
+ *   ffn_create / ffn_destroy      Nerf.from_kernels + Nerf.setup_buffers (ffnerf_tools.py:583-671,
+ *                                 926-977): program build, parameter and scratch allocation
+ *   ffn_buffer                    Nerf.buf / Nerf.tmp device buffers (ffnerf_tools.py:939-977),
+ *                                 used for checkpoint I/O (Nerf.save/load_latest, :989-1189)
+ *   ffn_forward_backward          enqueue of ffnerf_train_step with do_train=1
+ *                                 (ffnerf_tools.py:1410-1445; kernel ffnerf_OG.cl:838-2174)
+ *   ffn_apply_updates             enqueue of update_ffnerf_oneWG (ffnerf_tools.py:1478-1518;
+ *                                 kernel weight_update.cl:346-577) plus the hash-table SGD step
+ *                                 that the reference applies inside ffnerf_train_step
+ *                                 (ffnerf_OG.cl:2090-2173)
+ *   ffn_train_step                Nerf.step(do_train=True) device work (ffnerf_tools.py:1357-1544)
+ *   ffn_render                    Nerf.step(do_train=False) (ffnerf_tools.py:1357-1544 with
+ *                                 do_train=0; kernel path ffnerf_OG.cl:1115-1134,1848)
+ *   ffn_occ_maintenance           enqueue of occ_nibble_decay_write_both_q24
+ *                                 (ffnerf_tools.py:1452-1476; decay_occ_grid_in-st.cl:13-113)
+ *   ffn_grad_buffer               (no reference counterpart: the reference has one device) the
+ *                                 contiguous gradient buffer all-reduced across data-parallel ranks
+ */
+#ifndef FFNERF_H
+#define FFNERF_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFN_N_LEVELS 16
+#define FFN_ABI_VERSION 1
+
+enum {
+    FFN_OK = 0,
+    FFN_E_CONFIG = -1,    /* invalid configuration or argument (reference: ValueError) */
+    FFN_E_CUDA = -2,      /* CUDA runtime / launch failure                             */
+    FFN_E_CAPACITY = -3,  /* more rays than the context was created for                */
+    FFN_E_NAME = -4,      /* unknown buffer name                                        */
+    FFN_E_STATE = -5      /* call order violated (e.g. apply without gradients)         */
+};
+
+/* Buffer ids for ffn_buffer(). */
+enum {
+    FFN_BUF_PARAMS = 0,     /* float32 MLP parameter blob (active layers, canonical order)      */
+    FFN_BUF_ADAM_M = 1,     /* float32, same layout                                             */
+    FFN_BUF_ADAM_V = 2,     /* float32, same layout                                             */
+    FFN_BUF_TABLE = 3,      /* float32 [table_entries * F], index (level_offset[l]+entry)*F+f   */
+    FFN_BUF_OCC_IN = 4,     /* uint32 [G^3], 8 nibbles per cell                                 */
+    FFN_BUF_OCC_ST = 5,     /* uint32 [G^3]                                                     */
+    FFN_BUF_GRADS = 6,      /* float32 [table_entries * F + params]: table grads, then MLP grads */
+    FFN_BUF_TABLE_M = 7,    /* float32 table Adam state (table_optimizer = 1 only)              */
+    FFN_BUF_TABLE_V = 8
+};
+
+typedef struct ffn_config {
+    int32_t F;               /* features per hash level: 2 or 4                         */
+    int32_t ND;              /* density hidden layers 1..3                              */
+    int32_t NC;              /* color hidden layers 1..4                                */
+    int32_t spr;             /* samples per ray: 16, 32 or 64                           */
+    int32_t G;               /* occupancy grid side                                     */
+    int32_t background;      /* 0 black, 1 white, 2 random per ray                      */
+    int32_t table_optimizer; /* 0: reference SGD (hash lr roll-off), 1: Adam            */
+    int32_t max_rays;        /* capacity: largest n_rays of any call                    */
+    uint32_t level_log2[FFN_N_LEVELS];
+    uint32_t level_offset[FFN_N_LEVELS];
+    int32_t level_res[FFN_N_LEVELS];
+    float hash_lr_scale[FFN_N_LEVELS];
+    float box_min[4], box_max[4];
+    float rho_min, rho_max, dt_min, dt_max, t_near, t_far;
+    float adam_beta1, adam_beta2, adam_eps;   /* MLP (and table) Adam */
+    float table_adam_eps;
+} ffn_config;
+
+typedef struct ffn_step_scalars {
+    float lr_f;            /* base learning rate of the step (hash SGD lr, kernel arg `lr`) */
+    float lr_t;            /* bias-corrected Adam step size for the MLP                     */
+    float sh_mult;         /* spherical-harmonics multiplier                                */
+    float color_rel_lr;    /* color-MLP learning-rate factor                                */
+    float occ_strength;    /* occupancy update strength (0 disables proposals)              */
+    uint32_t rng_u32;      /* per-step seed                                                 */
+    uint32_t ray_offset;   /* global index of the first ray (data-parallel shards)          */
+    float table_lr_t;      /* bias-corrected Adam step size for the table (optimizer 1)     */
+} ffn_step_scalars;
+
+typedef struct ffn_ctx ffn_ctx;
+
+int ffn_abi_version(void);
+const char* ffn_last_error(const ffn_ctx* ctx);   /* ctx may be NULL (creation errors) */
+
+int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out);
+int ffn_destroy(ffn_ctx* ctx);
+
+/* Device pointer and size in bytes of one context buffer (FFN_BUF_*). */
+int ffn_buffer(ffn_ctx* ctx, int id, void** dev_ptr, size_t* bytes);
+/* Offset (floats) and size of each active parameter in FFN_BUF_PARAMS, canonical order
+ * Wd_in Wd_01 Wd_12 Wd_out Wc_in Wc_01 Wc_12 Wc_23 Wc_out bd_0 bd_1 bd_2 bd_out bc_0 bc_1 bc_2
+ * bc_3 bc_out; returns the blob length in floats. */
+int ffn_param_layout(const ffn_config* cfg, int32_t* offsets18, int32_t* sizes18);
+
+/* Forward + backward for n_rays rays (rays: [n][8] float o.xyzw d.xyzw, targets/out: [n][4]).
+ * Accumulates into FFN_BUF_GRADS, proposes occupancy into FFN_BUF_OCC_ST, writes out. */
+int ffn_forward_backward(ffn_ctx* ctx, const void* rays, const void* targets, void* out,
+                         uint32_t n_rays, const ffn_step_scalars* s, void* stream);
+/* Applies the accumulated gradients (table SGD or Adam, MLP Adam) and clears them. */
+int ffn_apply_updates(ffn_ctx* ctx, const ffn_step_scalars* s, void* stream);
+/* ffn_forward_backward + ffn_apply_updates. */
+int ffn_train_step(ffn_ctx* ctx, const void* rays, const void* targets, void* out,
+                   uint32_t n_rays, const ffn_step_scalars* s, void* stream);
+/* Forward only (do_train = 0): occupancy-guided sampling with the inference rule, black
+ * background, no gradients. */
+int ffn_render(ffn_ctx* ctx, const void* rays, void* out, uint32_t n_rays,
+               const ffn_step_scalars* s, void* stream);
+/* Occupancy maintenance: decay unchanged nibbles, merge proposals, write both grids. */
+int ffn_occ_maintenance(ffn_ctx* ctx, uint32_t decay_q24, uint32_t seed, void* stream);
+/* The contiguous gradient buffer (table grads then MLP grads) for a data-parallel all-reduce. */
+int ffn_grad_buffer(ffn_ctx* ctx, void** dev_ptr, size_t* n_floats);
+
+/* Diagnostics of one forward pass (any pointer may be NULL): per sample t, dt, resampled
+ * candidate index, sigma, rgb[3], transmittance; per ray the 64-bit run-start set.  When
+ * bypass is non-NULL ([n*spr][4] sigma,r,g,b) it replaces the MLP output, and sampling,
+ * compositing and occupancy proposals run on it (do_train = 1 rules, no backward). */
+int ffn_probe(ffn_ctx* ctx, const void* rays, const void* targets, void* out, uint32_t n_rays,
+              const ffn_step_scalars* s, const void* bypass, float* t, float* dt, int32_t* idx,
+              uint32_t* flags, float* sigma, float* rgb, float* trans, void* stream);
+
+/* Hash-grid encoding on its own (microbenchmark of the encode/scatter kernels): points are
+ * normalized coordinates [n][3] in [0,1]^3; enc is [n][16*F]; the backward scatter-adds
+ * denc [n][16*F] weighted by the trilinear weights into FFN_BUF_GRADS (table part). */
+int ffn_hash_encode(ffn_ctx* ctx, const float* pts, float* enc, int64_t n, void* stream);
+int ffn_hash_encode_bwd(ffn_ctx* ctx, const float* pts, const float* denc, int64_t n,
+                        void* stream);
+/* Plain Adam over n float32 parameters (vectorised; beta/eps as given). */
+int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float beta1,
+             float beta2, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

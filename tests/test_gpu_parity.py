@@ -1,0 +1,295 @@
+"""CUDA path vs the CPU oracle, through the C ABI (libffnerf.so).
+
+Contracts (stated per test):
+  * bit-exact: sampler sample times / candidate indices / run-start bits, per-ray sample counts,
+    occupancy proposals given fixed per-sample sigma/rgb, compositing transmittance given sigma,
+    decay/merge, Adam given identical gradients;
+  * fp32 tolerance: MLP outputs (rel 1e-4), gradients (rel-L2 1e-4 for one step), and over a run
+    of training steps the per-step loss (rel 1e-3) and the parameters (rel-L2 1e-2).
+The oracle runs in math mode 0 (the exp/pow restatement the device uses) and deferred table mode
+(every ray reads the step-start table), the semantics the GPU implements.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from _helpers import init_blob, init_occ, init_table, rays_toward_box, rel_l2, targets
+from ffn_config import REFERENCE_LEVEL_LOG2, make_geometry
+from oracle import OrcStep, make_orc_config
+import ffn_native as fn
+
+GEOMS = {
+    "cfg1": dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0),
+    "refdefault": dict(F=4, ND=2, NC=2, spr=64, G=32, log2_entries=list(REFERENCE_LEVEL_LOG2), rmax=1024.0,
+                       box_min=(-3, -3, -3), box_max=(3, 3, 3)),
+    "spr32": dict(F=2, ND=1, NC=2, spr=32, G=64, log2_entries=12, rmax=512.0),
+}
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _make(name, seed=0, n_rays=96, n_miss=4):
+    g = make_geometry(**GEOMS[name])
+    ctx = fn.Context(g, device=0)
+    blob = init_blob(g, seed)
+    table = init_table(g, seed)
+    occ = init_occ(g, seed)
+    ctx.tensor(fn.BUF_PARAMS).copy_(_cuda(blob))
+    ctx.tensor(fn.BUF_TABLE).copy_(_cuda(table))
+    ctx.tensor(fn.BUF_OCC_IN).copy_(_cuda(occ.view(np.int32)))
+    ctx.tensor(fn.BUF_OCC_ST).copy_(_cuda(occ.view(np.int32)))
+    radius = 2.0 if name != "refdefault" else 6.0
+    rays = rays_toward_box(n_rays, seed, radius=radius, n_miss=n_miss)
+    tg = targets(n_rays, seed)
+    return g, ctx, blob, table, occ, rays, tg
+
+
+@pytest.fixture(autouse=True)
+def _sync():
+    yield
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("name", list(GEOMS))
+def test_sampler_bit_exact(oracle, name):
+    g, ctx, blob, table, occ, rays, tg = _make(name)
+    n, spr = rays.shape[0], g["spr"]
+    seed = 0x9E3779B9
+    # oracle
+    dbg = {k: np.zeros(n * spr, np.float32) for k in ("t", "dt", "sigma", "trans")}
+    dbg["idx"] = np.zeros(n * spr, np.int32)
+    dbg["flags"] = np.zeros(n * 2, np.uint32)
+    dbg["rgb"] = np.zeros(n * spr * 3, np.float32)
+    out_o = np.zeros((n, 4), np.float32)
+    oracle.forward_backward(make_orc_config(g), OrcStep(1e-3, 0.5, 0.0, seed, 1, 0), blob, table.copy(),
+                            occ.copy(), occ.copy(), rays, tg, out_o, None, None, dbg)
+    # device
+    dr, dtg, dout = _cuda(rays), _cuda(tg), torch.zeros((n, 4), device="cuda")
+    t = torch.zeros(n * spr, device="cuda"); dt = torch.zeros_like(t); sg = torch.zeros_like(t); tr = torch.zeros_like(t)
+    idx = torch.zeros(n * spr, dtype=torch.int32, device="cuda")
+    fl = torch.zeros(n * 2, dtype=torch.int32, device="cuda")
+    rgb = torch.zeros(n * spr * 3, device="cuda")
+    ctx.probe(dr, dtg, dout, n, fn.make_step(sh_mult=0.5, rng_u32=seed), t=t, dt=dt, idx=idx, flags=fl,
+              sigma=sg, rgb=rgb, trans=tr)
+    torch.cuda.synchronize()
+    assert np.array_equal(t.cpu().numpy(), dbg["t"]), "sample times differ"
+    assert np.array_equal(dt.cpu().numpy(), dbg["dt"])
+    assert np.array_equal(idx.cpu().numpy(), dbg["idx"]), "candidate indices differ"
+    assert np.array_equal(fl.cpu().numpy().view(np.uint32), dbg["flags"]), "run-start bits differ"
+    counts_o = (dbg["dt"].reshape(n, spr) > 0).sum(1)
+    counts_g = (dt.cpu().numpy().reshape(n, spr) > 0).sum(1)
+    assert np.array_equal(counts_o, counts_g)
+    assert (counts_o == 0).sum() >= 1 and (counts_o == spr).sum() >= 1   # misses and hits covered
+    hit = np.repeat(counts_o > 0, spr)
+    np.testing.assert_allclose(sg.cpu().numpy()[hit], dbg["sigma"][hit], rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(rgb.cpu().numpy().reshape(-1, 3)[hit], dbg["rgb"].reshape(-1, 3)[hit], rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(dout.cpu().numpy(), out_o, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", list(GEOMS))
+def test_occupancy_proposals_bit_exact(oracle, name):
+    """With sigma/rgb fixed per sample (MLP bypassed) the nibble-max proposals, the transmittance
+    and the composited colour are bit-identical."""
+    g, ctx, blob, table, occ, rays, tg = _make(name, seed=3, n_rays=160)
+    n, spr = rays.shape[0], g["spr"]
+    rng = np.random.default_rng(5)
+    bypass = np.zeros((n * spr, 4), np.float32)
+    bypass[:, 0] = rng.exponential(20.0, n * spr).astype(np.float32)
+    bypass[:, 1:] = rng.uniform(0, 1, (n * spr, 3)).astype(np.float32)
+    seed = 1234567
+    occ_st_o = occ.copy()
+    tr_o = np.zeros(n * spr, np.float32)
+    out_o = np.zeros((n, 4), np.float32)
+    oracle.forward_backward(make_orc_config(g), OrcStep(0.0, 1.0, 1.0, seed, 1, 0), blob, table.copy(), occ.copy(),
+                            occ_st_o, rays, tg, out_o, None, None, {"trans": tr_o}, bypass)
+    assert (occ_st_o != occ).sum() > 0, "test does not exercise the proposals"
+    dout = torch.zeros((n, 4), device="cuda")
+    tr = torch.zeros(n * spr, device="cuda")
+    ctx.probe(_cuda(rays), _cuda(tg), dout, n, fn.make_step(occ_strength=1.0, rng_u32=seed), bypass=_cuda(bypass),
+              trans=tr)
+    torch.cuda.synchronize()
+    occ_st_g = ctx.tensor(fn.BUF_OCC_ST).cpu().numpy().view(np.uint32)
+    assert np.array_equal(occ_st_g, occ_st_o), f"{(occ_st_g != occ_st_o).sum()} occupancy words differ"
+    assert np.array_equal(tr.cpu().numpy(), tr_o)
+    assert np.array_equal(dout.cpu().numpy(), out_o)
+
+
+@pytest.mark.parametrize("name", list(GEOMS))
+def test_forward_backward_gradients(oracle, name):
+    g, ctx, blob, table, occ, rays, tg = _make(name, seed=7)
+    n = rays.shape[0]
+    lay, total = ctx.layout, ctx.param_total
+    seed = 42
+    tgo = np.zeros(table.size, np.float32)
+    mgo = np.zeros(total, np.float32)
+    out_o = np.zeros((n, 4), np.float32)
+    occ_st_o = occ.copy()
+    oracle.forward_backward(make_orc_config(g), OrcStep(1e-2, 0.8, 0.0, seed, 1, 0), blob, table.copy(), occ.copy(),
+                            occ_st_o, rays, tg, out_o, tgo, mgo)
+    dout = torch.zeros((n, 4), device="cuda")
+    ctx.forward_backward(_cuda(rays), _cuda(tg), dout, n, fn.make_step(lr_f=1e-2, sh_mult=0.8, rng_u32=seed))
+    torch.cuda.synchronize()
+    grads = ctx.tensor(fn.BUF_GRADS).cpu().numpy()
+    tg_g, mg_g = grads[:table.size], grads[table.size:]
+    np.testing.assert_allclose(dout.cpu().numpy(), out_o, rtol=1e-4, atol=1e-5)
+    assert np.count_nonzero(tgo) > 1000
+    assert rel_l2(tg_g, tgo) < 1e-4, rel_l2(tg_g, tgo)
+    for pname, (off, sz) in lay.items():
+        if sz:
+            e = rel_l2(mg_g[off:off + sz], mgo[off:off + sz])
+            assert e < 1e-4, (pname, e)
+
+
+def _mse(out, tg):
+    return float(np.mean((out[:, :3] - tg[:, :3]) ** 2))
+
+
+@pytest.mark.parametrize("name", ["cfg1", "refdefault"])
+def test_training_run_parity(oracle, name):
+    """20 full steps (forward, backward, MLP Adam, hash SGD, one occupancy maintenance):
+    per-step loss rel <= 1e-3, parameters and table rel-L2 <= 1e-2 at the end."""
+    g, ctx, blob, table, occ, rays_all, tg_all = _make(name, seed=11, n_rays=128 * 20, n_miss=0)
+    cfg = make_orc_config(g)
+    n = 128
+    b1, b2 = np.float32(0.9), np.float32(0.999)
+    p_o, m_o, v_o = blob.copy(), np.zeros_like(blob), np.zeros_like(blob)
+    tab_o, occ_in_o, occ_st_o = table.copy(), occ.copy(), occ.copy()
+    losses_o, losses_g = [], []
+    for step in range(1, 21):
+        rays = rays_all[(step - 1) * n: step * n]
+        tg = tg_all[(step - 1) * n: step * n]
+        lr_f = np.float32(5e-3)
+        lr_t = np.float32(lr_f * np.sqrt(1.0 - b2 ** np.float32(step)) / (1.0 - b1 ** np.float32(step)))
+        occs = 1.0 if step > 10 else 0.0
+        seed = (step * 2654435761) & 0xFFFFFFFF
+        # oracle step
+        tgo = np.zeros(table.size, np.float32)
+        mgo = np.zeros(blob.size, np.float32)
+        out_o = np.zeros((n, 4), np.float32)
+        oracle.forward_backward(cfg, OrcStep(lr_f, 1.0, occs, seed, 1, 0), p_o, tab_o, occ_in_o, occ_st_o, rays, tg,
+                                out_o, tgo, mgo)
+        oracle.mlp_adam(cfg, p_o, mgo, m_o, v_o, lr_t, 0.5, b1, b2, np.float32(1e-6))
+        oracle.table_apply(cfg, tab_o, tgo, lr_f)
+        # device step
+        dout = torch.zeros((n, 4), device="cuda")
+        ctx.train_step(_cuda(rays), _cuda(tg), dout, n,
+                       fn.make_step(lr_f=lr_f, lr_t=lr_t, color_rel_lr=0.5, occ_strength=occs, rng_u32=seed))
+        if step == 16:
+            oracle.decay(occ_in_o, occ_st_o, 15099494, seed)
+            ctx.occ_maintenance(15099494, seed)
+        losses_o.append(_mse(out_o, tg))
+        losses_g.append(_mse(dout.cpu().numpy(), tg))
+    torch.cuda.synchronize()
+    lo, lg = np.array(losses_o), np.array(losses_g)
+    assert np.all(np.abs(lg - lo) <= 1e-3 * np.abs(lo)), np.abs(lg - lo) / lo
+    p_g = ctx.tensor(fn.BUF_PARAMS).cpu().numpy()
+    assert rel_l2(p_g, p_o) < 1e-2, rel_l2(p_g, p_o)
+    assert rel_l2(ctx.tensor(fn.BUF_TABLE).cpu().numpy(), tab_o) < 1e-2
+    assert rel_l2(p_g - blob, p_o - blob) < 1e-2          # the update itself, not just the start point
+    occ_g = ctx.tensor(fn.BUF_OCC_IN).cpu().numpy().view(np.uint32)
+    assert (occ_g != occ_in_o).mean() < 0.01   # proposals depend on fp sigma: nearly all words agree
+
+
+def test_decay_bit_exact(oracle):
+    g = make_geometry(**GEOMS["cfg1"])
+    ctx = fn.Context(g)
+    rng = np.random.default_rng(3)
+    occ_in = rng.integers(0, 2**32, g["G"] ** 3, dtype=np.uint64).astype(np.uint32)
+    occ_st = occ_in.copy()
+    change = rng.random(occ_in.size) < 0.3
+    occ_st[change] = rng.integers(0, 2**32, change.sum(), dtype=np.uint64).astype(np.uint32)
+    ctx.tensor(fn.BUF_OCC_IN).copy_(_cuda(occ_in.view(np.int32)))
+    ctx.tensor(fn.BUF_OCC_ST).copy_(_cuda(occ_st.view(np.int32)))
+    for dq, seed in ((15099494, 77), (1 << 24, 1), (0, 99), (8388608, 0xDEADBEEF)):
+        ctx.occ_maintenance(dq, seed)
+        oracle.decay(occ_in, occ_st, dq, seed)
+        torch.cuda.synchronize()
+        assert np.array_equal(ctx.tensor(fn.BUF_OCC_IN).cpu().numpy().view(np.uint32), occ_in)
+        assert np.array_equal(ctx.tensor(fn.BUF_OCC_ST).cpu().numpy().view(np.uint32), occ_st)
+
+
+@pytest.mark.parametrize("n", [1, 7, 4096 + 3])
+def test_adam_bit_exact(oracle, n):
+    rng = np.random.default_rng(n)
+    p = rng.normal(size=n).astype(np.float32)
+    g = rng.normal(0, 1e-3, n).astype(np.float32)
+    m = rng.normal(0, 1e-3, n).astype(np.float32)
+    v = np.abs(rng.normal(0, 1e-6, n)).astype(np.float32)
+    tp, tg, tm, tv = (_cuda(x) for x in (p, g, m, v))
+    fn.adam(tp, tg, tm, tv, n, 1e-2, 0.9, 0.99, 1e-15)
+    oracle.adam(p, g, m, v, np.float32(1e-2), np.float32(0.9), np.float32(0.99), np.float32(1e-15))
+    torch.cuda.synchronize()
+    assert np.array_equal(tp.cpu().numpy(), p)
+    assert np.array_equal(tm.cpu().numpy(), m)
+    assert np.array_equal(tv.cpu().numpy(), v)
+
+
+@pytest.mark.parametrize("F", [2, 4])
+def test_hash_encode_fwd_bwd(oracle, F):
+    g = make_geometry(F=F, ND=1, NC=2, log2_entries=12, rmax=2048.0)
+    ctx = fn.Context(g)
+    table = init_table(g, 1)
+    ctx.tensor(fn.BUF_TABLE).copy_(_cuda(table))
+    n = 20000
+    rng = np.random.default_rng(F)
+    pts = rng.random((n, 3), dtype=np.float32)
+    pts[:5] = [[0, 0, 0], [1, 1, 1], [0.999999, 0.5, 0], [1.5, -0.5, 0.5], [0.5, 0.5, 0.5]]  # edges, outside
+    enc_o = np.zeros((n, 16 * F), np.float32)
+    oracle.hash_fwd(make_orc_config(g), table, pts, enc_o)
+    enc = torch.zeros((n, 16 * F), device="cuda")
+    ctx.hash_encode(_cuda(pts), enc, n)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(enc.cpu().numpy(), enc_o, rtol=1e-5, atol=1e-7)
+    denc = rng.normal(size=(n, 16 * F)).astype(np.float32)
+    tg_o = np.zeros(table.size, np.float32)
+    oracle.hash_bwd(make_orc_config(g), pts, denc, tg_o)
+    ctx.hash_encode_bwd(_cuda(pts), _cuda(denc), n)
+    torch.cuda.synchronize()
+    tg_g = ctx.tensor(fn.BUF_GRADS).cpu().numpy()[:table.size]
+    assert rel_l2(tg_g, tg_o) < 1e-5
+
+
+def test_render_matches_oracle_inference(oracle):
+    g, ctx, blob, table, occ, rays, tg = _make("cfg1", seed=9)
+    n = rays.shape[0]
+    out_o = np.zeros((n, 4), np.float32)
+    oracle.forward_backward(make_orc_config(g), OrcStep(0.0, 1.0, 0.0, 5, 0, 0), blob, table.copy(), occ.copy(),
+                            occ.copy(), rays, np.zeros((n, 4), np.float32), out_o)
+    dout = torch.zeros((n, 4), device="cuda")
+    ctx.render(_cuda(rays), dout, n, fn.make_step(rng_u32=5))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(dout.cpu().numpy(), out_o, rtol=1e-4, atol=1e-5)
+    grads = ctx.tensor(fn.BUF_GRADS).cpu().numpy()
+    assert not grads.any(), "render must not produce gradients"
+
+
+def test_ray_offset_shards_equal_single_call(oracle):
+    """Data-parallel sharding: two half-batches with global ray offsets accumulate the same
+    gradients as one call over the whole batch (RNG streams keyed by global ray id)."""
+    g, ctx, blob, table, occ, rays, tg = _make("cfg1", seed=13, n_rays=128)
+    n = rays.shape[0]
+    step = fn.make_step(lr_f=1e-2, rng_u32=99)
+    out1 = torch.zeros((n, 4), device="cuda")
+    ctx.forward_backward(_cuda(rays), _cuda(tg), out1, n, step)
+    torch.cuda.synchronize()
+    g1 = ctx.tensor(fn.BUF_GRADS).clone()
+    ctx.tensor(fn.BUF_GRADS).zero_()
+    out2 = torch.zeros((n, 4), device="cuda")
+    h = n // 2
+    dr, dt_ = _cuda(rays), _cuda(tg)
+    ctx.forward_backward(dr[:h], dt_[:h], out2[:h], h, fn.make_step(lr_f=1e-2, rng_u32=99, ray_offset=0))
+    ctx.forward_backward(dr[h:], dt_[h:], out2[h:], n - h, fn.make_step(lr_f=1e-2, rng_u32=99, ray_offset=h))
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2)
+    assert rel_l2(ctx.tensor(fn.BUF_GRADS).cpu().numpy(), g1.cpu().numpy()) < 1e-5
+
+
+def test_invalid_config_rejected():
+    g = make_geometry(**GEOMS["cfg1"])
+    g["spr"] = 48
+    with pytest.raises(ValueError):
+        fn.Context(g)
