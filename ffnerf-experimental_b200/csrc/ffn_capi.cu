@@ -123,6 +123,7 @@ StepArgs base_args(ffn_ctx* c, const void* rays, const void* targets, void* out,
                    const ffn_step_scalars* s) {
     StepArgs a{};
     a.c = c->dc;
+    if (s->spr) a.c.spr = (int)s->spr;
     a.lo = c->lo;
     a.params = c->params;
     a.table = c->table;
@@ -142,7 +143,7 @@ StepArgs base_args(ffn_ctx* c, const void* rays, const void* targets, void* out,
 }
 
 int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) {
-    const int rpt = c->rows / c->cfg.spr;
+    const int rpt = c->rows / a.c.spr;
     const int n_tiles = (int)((a.n_rays + (uint32_t)rpt - 1) / (uint32_t)rpt);
     const int grid = n_tiles < c->max_grid ? n_tiles : c->max_grid;
     if (grid_out) *grid_out = grid;
@@ -275,10 +276,12 @@ int ffn_grad_buffer(ffn_ctx* c, void** dev, size_t* n_floats) {
 static int check_io(ffn_ctx* c, const void* rays, const void* out, uint32_t n, const ffn_step_scalars* s) {
     if (!c) return FFN_E_CONFIG;
     if (!s) return fail(c, FFN_E_CONFIG, "null step scalars");
+    if (s->spr != 0 && s->spr != 16 && s->spr != 32 && s->spr != 64)
+        return fail(c, FFN_E_CONFIG, "samples_per_ray must be 16, 32 or 64 (power of two, <= S_MAX=64)");
     if (n == 0) return FFN_OK;
     if (!rays || !out) return fail(c, FFN_E_CONFIG, "rays and out must be device pointers");
     if (!aligned16(rays) || !aligned16(out)) return fail(c, FFN_E_CONFIG, "rays/out must be 16-byte aligned");
-    if ((uint64_t)n * (uint64_t)c->cfg.spr >= (1ull << 31)) return fail(c, FFN_E_CAPACITY, "too many samples in one call");
+    if ((uint64_t)n * 64ull >= (1ull << 31)) return fail(c, FFN_E_CAPACITY, "too many rays in one call");
     return FFN_OK;
 }
 
@@ -358,6 +361,17 @@ int ffn_probe(ffn_ctx* c, const void* rays, const void* targets, void* out, uint
     a.dbg_t = t; a.dbg_dt = dt; a.dbg_idx = idx; a.dbg_flags = flags;
     a.dbg_sigma = sigma; a.dbg_rgb = rgb; a.dbg_trans = trans;
     return launch_fused(c, a, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int ffn_occ_st_bytes(ffn_ctx* c, uint8_t* bytes, int to_bytes, void* stream) {
+    if (!c || !bytes) return fail(c, FFN_E_CONFIG, "null argument");
+    if (!aligned16(bytes)) return fail(c, FFN_E_CONFIG, "bytes must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    const uint32_t n = (uint32_t)c->cfg.G * c->cfg.G * c->cfg.G;
+    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    occ_bytes_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(c->occ_st, bytes, n, to_bytes);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "occupancy byte conversion launch");
 }
 
 int ffn_occ_maintenance(ffn_ctx* c, uint32_t decay_q24, uint32_t seed, void* stream) {

@@ -1067,6 +1067,29 @@ __global__ void occ_decay_kernel(uint32_t* __restrict__ occ_in, uint32_t* __rest
     }
 }
 
+// One byte per nibble: expand (to_bytes = 1) or pack back (to_bytes = 0); 8 bytes per word.
+__global__ void occ_bytes_kernel(uint32_t* __restrict__ grid, uint8_t* __restrict__ bytes, uint32_t n, int to_bytes) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        uint2* b = reinterpret_cast<uint2*>(bytes) + i;
+        if (to_bytes) {
+            const uint32_t w = grid[i];
+            uint2 v;
+            v.x = (w & 0xFu) | ((w >> 4) & 0xFu) << 8 | ((w >> 8) & 0xFu) << 16 | ((w >> 12) & 0xFu) << 24;
+            v.y = ((w >> 16) & 0xFu) | ((w >> 20) & 0xFu) << 8 | ((w >> 24) & 0xFu) << 16 | ((w >> 28) & 0xFu) << 24;
+            *b = v;
+        } else {
+            const uint2 v = *b;
+            uint32_t w = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                w |= ((v.x >> (8 * k)) & 0xFu) << (4 * k);
+                w |= ((v.y >> (8 * k)) & 0xFu) << (4 * (k + 4));
+            }
+            grid[i] = w;
+        }
+    }
+}
+
 template <int F>
 __global__ void hash_fwd_kernel(const DevConfig c, const float* __restrict__ table, const float* __restrict__ pts,
                                 int64_t n, float* __restrict__ enc) {

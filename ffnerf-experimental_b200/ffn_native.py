@@ -40,7 +40,7 @@ class FfnConfig(C.Structure):
 class FfnStep(C.Structure):
     _fields_ = [("lr_f", C.c_float), ("lr_t", C.c_float), ("sh_mult", C.c_float),
                 ("color_rel_lr", C.c_float), ("occ_strength", C.c_float), ("rng_u32", C.c_uint32),
-                ("ray_offset", C.c_uint32), ("table_lr_t", C.c_float)]
+                ("ray_offset", C.c_uint32), ("table_lr_t", C.c_float), ("spr", C.c_uint32)]
 
 
 _VP = C.c_void_p
@@ -57,6 +57,7 @@ _SIGS = {
     "ffn_render": (C.c_int, [_VP, _VP, _VP, C.c_uint32, C.POINTER(FfnStep), _VP]),
     "ffn_occ_maintenance": (C.c_int, [_VP, C.c_uint32, C.c_uint32, _VP]),
     "ffn_grad_buffer": (C.c_int, [_VP, C.POINTER(_VP), C.POINTER(C.c_size_t)]),
+    "ffn_occ_st_bytes": (C.c_int, [_VP, _VP, C.c_int, _VP]),
     "ffn_probe": (C.c_int, [_VP, _VP, _VP, _VP, C.c_uint32, C.POINTER(FfnStep), _VP] + [_VP] * 7 + [_VP]),
     "ffn_hash_encode": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_hash_encode_bwd": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
@@ -107,10 +108,10 @@ def make_ffn_config(geom: dict, table_optimizer: int = 0, max_rays: int = 0, ada
 
 
 def make_step(lr_f=0.0, lr_t=0.0, sh_mult=1.0, color_rel_lr=1.0, occ_strength=0.0, rng_u32=0,
-              ray_offset=0, table_lr_t=0.0) -> FfnStep:
+              ray_offset=0, table_lr_t=0.0, spr=0) -> FfnStep:
     return FfnStep(float(np.float32(lr_f)), float(np.float32(lr_t)), float(np.float32(sh_mult)),
                    float(np.float32(color_rel_lr)), float(np.float32(occ_strength)), int(rng_u32) & 0xFFFFFFFF,
-                   int(ray_offset) & 0xFFFFFFFF, float(np.float32(table_lr_t)))
+                   int(ray_offset) & 0xFFFFFFFF, float(np.float32(table_lr_t)), int(spr))
 
 
 class _CudaArray:
@@ -231,6 +232,10 @@ class Context:
     def hash_encode_bwd(self, pts, denc, n: int, stream=None):
         self._check(self.lib.ffn_hash_encode_bwd(self.h, _ptr(pts), _ptr(denc), int(n), self._stream(stream)),
                     "ffn_hash_encode_bwd")
+
+    def occ_st_bytes(self, buf, to_bytes: bool, stream=None):
+        self._check(self.lib.ffn_occ_st_bytes(self.h, _ptr(buf), 1 if to_bytes else 0, self._stream(stream)),
+                    "ffn_occ_st_bytes")
 
     def grad_buffer(self):
         p, n = _VP(), C.c_size_t()

@@ -24,8 +24,9 @@
  *                                 do_train=0; kernel path ffnerf_OG.cl:1115-1134,1848)
  *   ffn_occ_maintenance           enqueue of occ_nibble_decay_write_both_q24
  *                                 (ffnerf_tools.py:1452-1476; decay_occ_grid_in-st.cl:13-113)
- *   ffn_grad_buffer               (no reference counterpart: the reference has one device) the
- *                                 contiguous gradient buffer all-reduced across data-parallel ranks
+ *   ffn_grad_buffer,              (no reference counterpart: the reference has one device) the
+ *   ffn_occ_st_bytes              gradient buffer and the occupancy proposals merged across
+ *                                 data-parallel ranks
  */
 #ifndef FFNERF_H
 #define FFNERF_H
@@ -89,6 +90,7 @@ typedef struct ffn_step_scalars {
     uint32_t rng_u32;      /* per-step seed                                                 */
     uint32_t ray_offset;   /* global index of the first ray (data-parallel shards)          */
     float table_lr_t;      /* bias-corrected Adam step size for the table (optimizer 1)     */
+    uint32_t spr;          /* samples per ray of this batch (16/32/64); 0 = ffn_config.spr  */
 } ffn_step_scalars;
 
 typedef struct ffn_ctx ffn_ctx;
@@ -123,6 +125,10 @@ int ffn_render(ffn_ctx* ctx, const void* rays, void* out, uint32_t n_rays,
 int ffn_occ_maintenance(ffn_ctx* ctx, uint32_t decay_q24, uint32_t seed, void* stream);
 /* The contiguous gradient buffer (table grads then MLP grads) for a data-parallel all-reduce. */
 int ffn_grad_buffer(ffn_ctx* ctx, void** dev_ptr, size_t* n_floats);
+/* Occupancy proposals as one byte per nibble ([G^3 * 8] uint8, value = nibble) so that ranks can
+ * merge them with a byte-wise MAX all-reduce: to_bytes = 1 expands FFN_BUF_OCC_ST into bytes,
+ * to_bytes = 0 packs bytes back into FFN_BUF_OCC_ST.  (No reference counterpart: one device.) */
+int ffn_occ_st_bytes(ffn_ctx* ctx, uint8_t* bytes, int to_bytes, void* stream);
 
 /* Diagnostics of one forward pass (any pointer may be NULL): per sample t, dt, resampled
  * candidate index, sigma, rgb[3], transmittance; per ray the 64-bit run-start set.  When

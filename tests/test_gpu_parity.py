@@ -87,7 +87,8 @@ def test_sampler_bit_exact(oracle, name):
     hit = np.repeat(counts_o > 0, spr)
     np.testing.assert_allclose(sg.cpu().numpy()[hit], dbg["sigma"][hit], rtol=1e-4, atol=1e-6)
     np.testing.assert_allclose(rgb.cpu().numpy().reshape(-1, 3)[hit], dbg["rgb"].reshape(-1, 3)[hit], rtol=1e-4, atol=1e-6)
-    np.testing.assert_allclose(dout.cpu().numpy(), out_o, rtol=1e-4, atol=1e-5)
+    # colour only: the oracle ran a training pass, which also sets the reference's out.w = 4 marker
+    np.testing.assert_allclose(dout.cpu().numpy()[:, :3], out_o[:, :3], rtol=1e-4, atol=1e-5)
 
 
 @pytest.mark.parametrize("name", list(GEOMS))
