@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark of the fused NeRF training step (BASELINE metric: trained samples/s, fwd+bwd+Adam).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg3|cfg2|cfg1] [--impl reference]
+
+Default workload cfg3: 16384 rays x 64 samples = 2^20 samples per step, split by ray across the
+N ranks (strong scaling), hash grid L=16 F=2 T=2^19 fp32, finest resolution 2048, density MLP
+32-64-16, colour MLP 32-64-64-3, occupancy grid 128^3 in a warmed-up state (~5% of sub-cells
+occupied, proposals on, maintenance every 32 steps), on the seeded 56-camera 450x800 Gaussian
+blob scene (synthetic data: rays through random pixels, targets rendered analytically and
+quantised to 8 bits).  Every step is the full training step: forward, backward, gradient
+all-reduce across ranks (NCCL), MLP Adam and the hash-table SGD update.
+
+For N > 1 run under torchrun (one process per GPU, NCCL).  Rank 0 prints one JSON line:
+  value       -- samples/s of the whole job, inputs resident on the device, CUDA events, max
+                 over ranks;
+  e2e         -- the same through the public API (ffnerf_tools.RayBatch uploads from pinned host
+                 memory, Nerf.step, download of the rendered colours) per step;
+  roofline    -- the fused forward/backward kernel: algorithmic bytes per launch / its average
+                 duration (CUDA events on its stream) against the measured HBM copy bandwidth;
+  cpu_baseline-- the reference kernels compiled for the CPU (oracle/_ref) on the host cores.
+``--impl reference`` times the reference's own CPU implementation of the step instead (rank 0
+only) and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "ffnerf-experimental_b200"))
+
+import numpy as np
+
+METRIC = "train samples/s (fwd+bwd+Adam)"
+WORKLOADS = {
+    "cfg3": dict(rays=16384, spr=64, F=2, ND=1, NC=2, log2T=19, rmax=2048.0, G=128, n_cams=56, W=800, H=450,
+                 maint=32, desc="cfg3: 16384 rays x 64 samples (2^20 samples/step) split by ray across GPUs; "
+                                "hash L=16 F=2 T=2^19 fp32 replicated, Rmax 2048; MLP 32-64-16 / 32-64-64-3 fp32; "
+                                "occupancy 128^3 ~5% occupied; 56-camera 450x800 synthetic blob scene"),
+    "cfg2": dict(rays=512, spr=64, F=2, ND=1, NC=2, log2T=19, rmax=2048.0, G=128, n_cams=56, W=800, H=450,
+                 maint=16, desc="cfg2: 512 rays x 64 samples; hash L=16 F=2 T=2^19, Rmax 2048; occupancy 128^3, "
+                                "maintenance every 16 steps; 56-camera 450x800 synthetic blob scene"),
+    "cfg1": dict(rays=512, spr=64, F=2, ND=1, NC=2, log2T=14, rmax=512.0, G=64, n_cams=8, W=64, H=64,
+                 maint=32, desc="cfg1: 512 rays x 64 samples; hash L=16 F=2 T=2^14, Rmax 512; occupancy 64^3; "
+                                "8 cameras at 64x64"),
+}
+# Algorithmic bytes per sample of the fused forward/backward kernel (F=2): trilinear gather
+# 16 levels x 8 corners x F x 4 B, atomic scatter read+write of the same, ray/target/colour I/O
+# (64 B per ray / spr) and one occupancy word per sample.
+def fused_bytes_per_sample(F: int, spr: int) -> float:
+    gather = 16 * 8 * F * 4
+    return gather + 2 * gather + 64.0 / spr + 4
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------ reference arm
+def run_reference_arm(args, wl) -> dict:
+    """The reference's own kernels, compiled for the CPU from their sources (oracle/_ref), timed on
+    all host cores; the oracle port stands in when that build is absent."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    sys.path.insert(0, str(ROOT / "tests"))
+    import oracle as orc
+    from ffn_config import make_geometry, param_layout, param_shapes
+    g = make_geometry(F=wl["F"], ND=wl["ND"], NC=wl["NC"], spr=wl["spr"], G=wl["G"], log2_entries=wl["log2T"],
+                      rmax=wl["rmax"])
+    cores = os.cpu_count() or 1
+    n_rays = min(1024, wl["rays"])            # bounded sample of the batch per step
+    rng = np.random.default_rng(0)
+    from synthetic_scene import BlobScene, cameras_ring, intrinsics, random_batch
+    scene = BlobScene(0)
+    cams = cameras_ring(wl["n_cams"], 2.5, 0)
+    K = intrinsics(wl["W"], wl["H"], 50.0)
+    rays, tg = random_batch(scene, cams, K, wl["W"], wl["H"], n_rays, 1, n_quad=96)
+    lay, total = param_layout(g["F"], g["ND"], g["NC"])
+    blob = (rng.normal(0, 0.1, total)).astype(np.float32)
+    table = rng.uniform(-1e-4, 1e-4, g["table_entries"] * g["F"]).astype(np.float32)
+    occ = np.full(g["G"] ** 3, 0xEEEEEEEE, np.uint32)
+    variant = {"cfg3": "cfg3", "cfg2": "cfg3", "cfg1": "cfg1"}[args.workload]
+    kind = "reference"
+    try:
+        ref = orc.RefKernels(variant)
+    except (FileNotFoundError, OSError):
+        ref, kind = None, "port"
+    out = np.zeros((n_rays, 4), np.float32)
+    if ref is not None:
+        shapes = param_shapes(g["F"], g["ND"], g["NC"])
+        params = {n: (blob[o:o + s].view(np.int32).copy() if n in shapes else np.zeros(0, np.int32))
+                  for n, (o, s) in lay.items()}
+        m = {k: np.zeros(v.size, np.float32) for k, v in params.items()}
+        v = {k: np.zeros(v.size, np.float32) for k, v in params.items()}
+        scr = ref.alloc_scratch(n_rays * g["spr"])
+
+        def step(i):
+            ref.train(params, table.view(np.int32), rays, tg, out, scr, occ, occ.copy(), g, 1e-3, 1.0, 1.0, i, True, cores)
+            ref.weight_update(params, m, v, scr, n_rays * g["spr"], 1e-3, 1.0, 0.9, 0.999, 1e-6, cores)
+    else:
+        o_ = orc.Oracle()
+        cfg = orc.make_orc_config(g)
+        m, v = np.zeros_like(blob), np.zeros_like(blob)
+        tgr, mg = np.zeros_like(table), np.zeros_like(blob)
+        cores = 1
+
+        def step(i):
+            tgr[:] = 0
+            o_.forward_backward(cfg, orc.OrcStep(1e-3, 1.0, 1.0, i, 1, 0), blob, table, occ, occ.copy(), rays, tg, out, tgr, mg)
+            o_.mlp_adam(cfg, blob, mg, m, v, 1e-3, 1.0, 0.9, 0.999, 1e-6)
+            o_.table_apply(cfg, table, tgr, 1e-3)
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    dt = time.perf_counter() - t0
+    samples = n_rays * g["spr"] * args.steps
+    val = samples / dt
+    sample_desc = (f"{n_rays} rays x {g['spr']} samples per step ({n_rays * g['spr']} of the workload's "
+                   f"{wl['rays'] * wl['spr']}), fused step + weight update + Adam")
+    return {"metric": METRIC, "value": val, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": {"workload": wl["desc"], "global_batch_rays": wl["rays"]},
+            "cpu_baseline": {"value": val, "unit": "samples/s", "cores": cores, "kind": kind, "sample": sample_desc},
+            "e2e": {"value": val, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_baseline_sample(wl) -> dict:
+    """A bounded run (~10-20 s) of the reference kernels compiled for the CPU."""
+    class A:
+        steps, warmup, gpus, workload = 6, 1, 1, None
+    a = A()
+    a.workload = next(k for k, v in WORKLOADS.items() if v["desc"] in wl["desc"])
+    r = run_reference_arm(a, WORKLOADS[a.workload])
+    return r["cpu_baseline"]
+
+
+# ------------------------------------------------------------------------------ our arm
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end loop (profiling runs)")
+    ap.add_argument("--rays", type=int, default=0, help="override the global batch (profiling a small case)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    wl = dict(WORKLOADS[args.workload])
+    if args.rays:
+        wl["rays"] = int(args.rays)
+        wl["desc"] += f" [reduced to {args.rays} rays per step]"
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and not (world == 1 and args.gpus == 1):
+        if world == 1:
+            sys.exit(f"--gpus {args.gpus} needs torchrun with {args.gpus} processes")
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference_arm(args, wl)), flush=True)
+        return
+
+    import torch
+    import ffnerf_tools as ft
+    from synthetic_scene import BlobScene, cameras_ring, cameras_sphere, intrinsics, pixel_rays
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    # ---- synthetic data: scene, cameras, a pool of global batches (same on every rank)
+    scene = BlobScene(0)
+    cams = cameras_ring(wl["n_cams"], 2.5, 0) if wl["n_cams"] > 8 else cameras_sphere(wl["n_cams"], 2.0, 0)
+    K = intrinsics(wl["W"], wl["H"], 50.0)
+    n_glob, spr = wl["rays"], wl["spr"]
+    n_loc = n_glob // world
+    pool = 4
+    rng = np.random.default_rng(1234)
+    pool_rays, pool_tg = [], []
+    for b in range(pool):
+        ci = rng.integers(0, cams.shape[0], n_glob)
+        u = rng.integers(0, wl["W"], n_glob)
+        v = rng.integers(0, wl["H"], n_glob)
+        rays = np.zeros((n_glob, 8), np.float32)
+        for c in np.unique(ci):
+            sel = ci == c
+            rays[sel] = pixel_rays(cams[c], K, u[sel], v[sel])
+        rays_t = torch.from_numpy(rays).to(dev)
+        rgb = scene.render_torch(rays_t, n_quad=192)
+        tg = torch.zeros((n_glob, 4), device=dev)
+        tg[:, :3] = torch.round(rgb * 255.0) / 255.0
+        sl = slice(rank * n_loc, (rank + 1) * n_loc)
+        pool_rays.append(rays_t[sl].contiguous())
+        pool_tg.append(tg[sl].contiguous())
+    occ_grid = scene.occupancy_grid_torch(wl["G"], dev)
+
+    # ---- the model through the public host API
+    ctx = ft.Context([ft.Device(local)])
+    queue = ft.CommandQueue(ctx)
+    occ = ft.OccParams(G_occ=wl["G"], box_min=np.array([-1, -1, -1], np.float32), box_max=np.array([1, 1, 1], np.float32),
+                       rho_min=np.float32(1.0), rho_max=np.float32(16.0), dt_min=np.float32(2.0 / 8192),
+                       dt_max=np.float32(12.8 / spr / 6 * 2.0), t_near_clip=np.float32(0.3),
+                       t_far_clip=np.float32(1e9), occ_update_strength0=np.float32(1.0)).finalize()
+    tmp = tempfile.mkdtemp(prefix="ffn_bench_")
+    nerf = ft.Nerf(ctx, queue, training_dir=tmp, model_id="bench", transfer_fmt="fp32",
+                   table_size_entries=16 << wl["log2T"], f_per_level=wl["F"], occ=occ, rng_seed=777,
+                   background="random", finest_resolution=wl["rmax"], nd=wl["ND"], nc=wl["NC"], verbose=False)
+    nerf.state_i32["occ_grid_in_u32"] = occ_grid.view(np.int32).copy()
+    nerf.state_i32["occ_grid_st_u32"] = occ_grid.view(np.int32).copy()
+    nerf.steps_trained = 3000                  # steady-state schedules (past the warm-up phases)
+    if world > 1:
+        nerf.enable_data_parallel(ray_offset=rank * n_loc)
+    io = ft.RayBatch.init(ctx, queue, n_loc, spr)
+    nerf.setup_buffers(n_loc, spr)
+    import schedules as sch
+    lmbda = sch.lr_lambda(1e-4, n_glob, spr)
+
+    def one_step(i, host=False):
+        b = i % pool
+        stp = nerf.steps_trained
+        lr_f = sch.lr_schedule(stp, 5e-5 * 8, lmbda, n_glob, spr)
+        if host:
+            io.upload_rays(host_rays[b])
+            io.upload_targets(host_tg[b])
+        else:
+            io.rays_buf, io.targets_buf = pool_rays[b], pool_tg[b]
+        out = nerf.step(io, lr_f=float(lr_f), do_train=True, return_output=host, sh_multiplier=1.0,
+                        color_MLP_rel_lr=1.0, occ_update_strength=1.0)[0]
+        return out
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing (value) + fused-kernel events (roofline)
+    for i in range(args.warmup):
+        one_step(i)
+    queue.finish()
+    barrier()
+    torch.cuda.synchronize()
+    nerf.fb_events = []
+    launches0 = nerf.native.launches
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(queue.stream)
+        for i in range(args.steps):
+            one_step(args.warmup + i)
+        e1.record(queue.stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms_total = max_over_ranks(e0.elapsed_time(e1))
+    launches = nerf.native.launches - launches0
+    fb_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in nerf.fb_events))
+    nerf.fb_events = None
+    clocks = clk.summary()
+
+    # ---- end to end through the public API: pinned-host uploads, Nerf.step, colour download
+    if args.no_e2e:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": n_glob * spr * args.steps / (ms_total * 1e-3),
+                              "unit": "samples/s", "note": "profiling run (no e2e, no baseline)",
+                              "gpu_launches": launches, "fused_ms": fb_ms}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    host_rays = [r.cpu().numpy().view(ft.ray_dtype).reshape(-1) for r in pool_rays]
+    host_tg = [t.cpu().numpy() for t in pool_tg]
+    io2 = ft.RayBatch.init(ctx, queue, n_loc, spr)
+    io_saved, io = io, io2
+    for i in range(3):
+        one_step(i, host=True)
+    queue.finish()
+    barrier()
+    t_e2e0 = torch.cuda.Event(enable_timing=True)
+    t_e2e1 = torch.cuda.Event(enable_timing=True)
+    t_e2e0.record(queue.stream)
+    losses = []
+    for i in range(args.steps):
+        out = one_step(i, host=True)
+        losses.append(float(np.mean((out[:, :3] - host_tg[i % pool][:, :3]) ** 2)))
+    t_e2e1.record(queue.stream)
+    t_e2e1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(t_e2e0.elapsed_time(t_e2e1))
+    io = io_saved
+
+    # ---- report (rank 0)
+    samples_per_step = n_glob * spr
+    value = samples_per_step * args.steps / (ms_total * 1e-3)
+    e2e_val = samples_per_step * args.steps / (e2e_ms * 1e-3)
+    hbm, bf16, peak_kind = peaks()
+    bytes_launch = fused_bytes_per_sample(wl["F"], spr) * n_loc * spr
+    achieved = bytes_launch / (fb_ms * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / f"fused_step_{args.workload}_traffic.json"
+    if tfile.exists():
+        t = json.loads(tfile.read_text())
+        traffic = t.get("bytes_per_launch_at_samples", {}).get(str(n_loc * spr))
+        if traffic is None and "bytes_per_sample" in t:
+            traffic = t["bytes_per_sample"] * n_loc * spr
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl["desc"], "global_batch_rays": n_glob, "samples_per_ray": spr,
+                       "samples_per_step": samples_per_step, "parallelism": f"dp{world}",
+                       "l2": "working set per step exceeds L2 (table 67 MB + table gradient 67 MB + occupancy 8 MB)"
+                             if wl["log2T"] >= 19 else "working set fits in L2 (small config)"},
+            "e2e": {"value": e2e_val, "unit": "samples/s", "h2d_bytes_per_step": n_loc * (32 + 16) * world,
+                    "d2h_bytes_per_step": n_loc * 16 * world, "final_mse": losses[-1]},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": "fused_step_kernel (+ partial-gradient reduce)",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": traffic, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_sample": fused_bytes_per_sample(wl["F"], spr),
+                         "launch_ms": fb_ms},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline_sample(wl)
+            except Exception as exc:   # the baseline is a side measurement; report why it is missing
+                line["cpu_baseline"] = {"value": None, "unit": "samples/s", "cores": os.cpu_count(),
+                                        "kind": "reference", "sample": f"not run: {exc}"}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -151,6 +151,7 @@ class Context:
         self.param_total = self.lib.ffn_param_layout(C.byref(self.cfg), off.ctypes.data, sz.ctypes.data)
         self.layout = {n: (int(o), int(s)) for n, o, s in zip(PARAM_NAMES, off, sz)}
         self._views = {}
+        self.launches = 0          # kernels this context has launched (for benchmark accounting)
 
     # -- lifetime
     def close(self):
@@ -203,39 +204,48 @@ class Context:
     def forward_backward(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_forward_backward(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                                   C.byref(step), self._stream(stream)), "ffn_forward_backward")
+        self.launches += 2
 
     def apply_updates(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_apply_updates(self.h, C.byref(step), self._stream(stream)), "ffn_apply_updates")
+        self.launches += 2
 
     def train_step(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_train_step(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                             C.byref(step), self._stream(stream)), "ffn_train_step")
+        self.launches += 4
 
     def render(self, rays, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_render(self.h, _ptr(rays), _ptr(out), int(n_rays), C.byref(step),
                                         self._stream(stream)), "ffn_render")
+        self.launches += 1
 
     def occ_maintenance(self, decay_q24: int, seed: int, stream=None):
         self._check(self.lib.ffn_occ_maintenance(self.h, int(decay_q24), int(seed) & 0xFFFFFFFF,
                                                  self._stream(stream)), "ffn_occ_maintenance")
+        self.launches += 1
 
     def probe(self, rays, targets, out, n_rays: int, step: FfnStep, bypass=None, t=None, dt=None, idx=None,
               flags=None, sigma=None, rgb=None, trans=None, stream=None):
         self._check(self.lib.ffn_probe(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays), C.byref(step),
                                        _ptr(bypass), _ptr(t), _ptr(dt), _ptr(idx), _ptr(flags), _ptr(sigma),
                                        _ptr(rgb), _ptr(trans), self._stream(stream)), "ffn_probe")
+        self.launches += 1
 
     def hash_encode(self, pts, enc, n: int, stream=None):
         self._check(self.lib.ffn_hash_encode(self.h, _ptr(pts), _ptr(enc), int(n), self._stream(stream)),
                     "ffn_hash_encode")
+        self.launches += 1
 
     def hash_encode_bwd(self, pts, denc, n: int, stream=None):
         self._check(self.lib.ffn_hash_encode_bwd(self.h, _ptr(pts), _ptr(denc), int(n), self._stream(stream)),
                     "ffn_hash_encode_bwd")
+        self.launches += 1
 
     def occ_st_bytes(self, buf, to_bytes: bool, stream=None):
         self._check(self.lib.ffn_occ_st_bytes(self.h, _ptr(buf), 1 if to_bytes else 0, self._stream(stream)),
                     "ffn_occ_st_bytes")
+        self.launches += 1
 
     def grad_buffer(self):
         p, n = _VP(), C.c_size_t()

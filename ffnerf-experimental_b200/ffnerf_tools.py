@@ -488,6 +488,7 @@ class Nerf:
         self.dp: DataParallel | None = None
         self.ray_offset = 0
         self._occ_bytes = None
+        self.fb_events = None      # list -> (start, end) CUDA events around every forward/backward launch
         self.buf, self.io, self.tmp = {}, {}, {}
         if load_id:
             self.load_latest(load_id)
@@ -854,8 +855,15 @@ class Nerf:
                 s = ffn_native.make_step(lr_f=lr_f, lr_t=lr_t, sh_mult=sh_multiplier, color_rel_lr=color_MLP_rel_lr,
                                          occ_strength=occ_update_strength, rng_u32=int(rng_u32), ray_offset=offset,
                                          table_lr_t=lr_t, spr=io.samples_per_ray)
+                if self.fb_events is not None:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record(q.stream)
                 nat.forward_backward(io.rays_buf, io.targets_buf, io.out_buf, io.num_rays, s, q.stream)
                 ev_ff = Event(q.stream, t_start)
+                if self.fb_events is not None:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record(q.stream)
+                    self.fb_events.append((e0, e1))
                 if self.dp is not None:
                     self.dp.allreduce_grads(self)
                 if do_maint:

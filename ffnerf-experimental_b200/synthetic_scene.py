@@ -63,6 +63,69 @@ class BlobScene:
             out[a:a + chunk] = np.where(hit[:, None], col, 0.0)
         return np.clip(out, 0.0, 1.0)
 
+    # -- the same computations on a torch device (data preparation for benchmarks)
+    def _t(self, device):
+        import torch
+        return (torch.as_tensor(self.centers, dtype=torch.float32, device=device),
+                torch.as_tensor(self.sigma, dtype=torch.float32, device=device),
+                torch.as_tensor(self.rgb, dtype=torch.float32, device=device))
+
+    def density_color_torch(self, x):
+        c, s, rgb = self._t(x.device)
+        d2 = ((x[..., None, :] - c) ** 2).sum(-1)
+        w = self.peak * (-d2 / (2.0 * s ** 2)).exp()
+        tot = w.sum(-1)
+        col = (w[..., None] * rgb).sum(-2) / tot.clamp_min(1e-12)[..., None]
+        return tot, col
+
+    def render_torch(self, rays, n_quad: int = 192, chunk: int = 16384):
+        """rays [n, 8] torch tensor -> rgb [n, 3] (black background), on the rays' device."""
+        import torch
+        out = torch.zeros((rays.shape[0], 3), dtype=torch.float32, device=rays.device)
+        bmin = torch.as_tensor(self.box_min, dtype=torch.float32, device=rays.device)
+        bmax = torch.as_tensor(self.box_max, dtype=torch.float32, device=rays.device)
+        u = (torch.arange(n_quad, device=rays.device, dtype=torch.float32) + 0.5) / n_quad
+        for a in range(0, rays.shape[0], chunk):
+            o, d = rays[a:a + chunk, :3], rays[a:a + chunk, 4:7]
+            inv = torch.where(d != 0, 1.0 / d, torch.full_like(d, float("inf")))
+            ta, tb = (bmin - o) * inv, (bmax - o) * inv
+            t0 = torch.nan_to_num(torch.minimum(ta, tb), nan=-float("inf")).amax(1).clamp_min(0.0)
+            t1 = torch.nan_to_num(torch.maximum(ta, tb), nan=float("inf")).amin(1)
+            hit = t1 > t0
+            t0 = torch.where(hit, t0, torch.zeros_like(t0))
+            t1 = torch.where(hit, t1, torch.zeros_like(t1))
+            t = t0[:, None] + (t1 - t0)[:, None] * u[None, :]
+            dt = ((t1 - t0) / n_quad)[:, None]
+            x = o[:, None, :] + t[..., None] * d[:, None, :]
+            sg, c = self.density_color_torch(x)
+            alpha = 1.0 - (-sg * dt).exp()
+            T = torch.cumprod(torch.cat([torch.ones_like(alpha[:, :1]), 1.0 - alpha[:, :-1]], 1), 1)
+            col = ((T * alpha)[..., None] * c).sum(1)
+            out[a:a + chunk] = torch.where(hit[:, None], col, torch.zeros_like(col))
+        return out.clamp(0.0, 1.0)
+
+    def occupancy_grid_torch(self, G: int, device, occupied_fraction: float = 0.05, q_occupied: int = 15) -> np.ndarray:
+        """occupancy_grid computed on a torch device."""
+        import torch
+        h = torch.as_tensor((self.box_max - self.box_min) / (2 * G), dtype=torch.float32, device=device)
+        lo = torch.as_tensor(self.box_min, dtype=torch.float32, device=device)
+        idx = torch.arange(2 * G, device=device, dtype=torch.float32) + 0.5
+        sub = torch.empty((2 * G, 2 * G, 2 * G), dtype=torch.float32, device=device)
+        yy, xx = torch.meshgrid(lo[1] + idx * h[1], lo[0] + idx * h[0], indexing="ij")
+        for zi in range(2 * G):
+            pts = torch.stack([xx, yy, torch.full_like(xx, float(lo[2] + (zi + 0.5) * h[2]))], -1)
+            sub[zi] = self.density_color_torch(pts)[0]
+        k = max(1, int(round(occupied_fraction * sub.numel())))
+        thr = torch.topk(sub.reshape(-1), k).values[-1]
+        occ4 = torch.where(sub >= thr, q_occupied - 1, 0).to(torch.int64).cpu().numpy().astype(np.uint32)
+        o = occ4.reshape(G, 2, G, 2, G, 2)
+        grid = np.zeros((G, G, G), np.uint32)
+        for sz in range(2):
+            for sy in range(2):
+                for sx in range(2):
+                    grid |= o[:, sz, :, sy, :, sx] << np.uint32(4 * (sx + 2 * sy + 4 * sz))
+        return grid.reshape(-1)
+
     def occupancy_grid(self, G: int, occupied_fraction: float = 0.05, q_occupied: int = 15) -> np.ndarray:
         """Packed nibble grid [G^3] uint32 (8 sub-cells per cell, value occ4 = q - 1): the densest
         `occupied_fraction` of sub-cells get occ4 = q_occupied - 1, the rest 0."""
