@@ -202,6 +202,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end loop (profiling runs)")
     ap.add_argument("--rays", type=int, default=0, help="override the global batch (profiling a small case)")
+    ap.add_argument("--mlp", choices=["fp16", "fp32"], default="fp16",
+                    help="MLP arithmetic: fp16 operands / fp32 accumulation on the tensor cores, or fp32 CUDA cores")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -268,7 +270,8 @@ def main():
     tmp = tempfile.mkdtemp(prefix="ffn_bench_")
     nerf = ft.Nerf(ctx, queue, training_dir=tmp, model_id="bench", transfer_fmt="fp32",
                    table_size_entries=16 << wl["log2T"], f_per_level=wl["F"], occ=occ, rng_seed=777,
-                   background="random", finest_resolution=wl["rmax"], nd=wl["ND"], nc=wl["NC"], verbose=False)
+                   background="random", finest_resolution=wl["rmax"], nd=wl["ND"], nc=wl["NC"],
+                   mlp_precision=args.mlp, verbose=False)
     nerf.state_i32["occ_grid_in_u32"] = occ_grid.view(np.int32).copy()
     nerf.state_i32["occ_grid_st_u32"] = occ_grid.view(np.int32).copy()
     nerf.steps_trained = 3000                  # steady-state schedules (past the warm-up phases)

@@ -10,6 +10,7 @@
 
 #include "ffn_common.cuh"
 #include "ffn_step.cu"
+#include "ffn_step_tc.cu"
 
 using namespace ffn;
 
@@ -30,8 +31,10 @@ struct ffn_ctx {
     uint32_t* occ_st = nullptr;
     float* grads = nullptr;      // [table_floats + Pw]
     float* partials = nullptr;   // [max_grid * Pw]
+    int* status = nullptr;       // device status word
     int max_grid = 0;
     int rows = 0;
+    int ctas_per_sm = 1;
     size_t smem = 0;
     void (*kernel)(StepArgs) = nullptr;
     std::string err;
@@ -63,11 +66,22 @@ struct DeviceGuard {
     }
 };
 
+int g_sms = 0;
+
 template <int F, int ND, int NC, int ROWS>
 void bind_kernel(ffn_ctx* c) {
+    if (c->cfg.mlp_precision == 1) {
+        using PL = TcPlan<F, ND>;
+        c->kernel = fused_step_tc_kernel<F, ND>;
+        c->rows = PL::ROWS;
+        c->smem = PL::BYTES;
+        c->ctas_per_sm = PL::CTAS_PER_SM;
+        return;
+    }
     c->kernel = fused_step_kernel<F, ND, NC, ROWS>;
     c->rows = ROWS;
     c->smem = (size_t)Smem<F, ND, NC, ROWS>::floats(c->Pw) * sizeof(float);
+    c->ctas_per_sm = 1;
 }
 
 // The (F, ND, NC) combinations compiled into this library; the tile height is the largest of
@@ -91,6 +105,7 @@ int check_config(const ffn_config* g, std::string* why) {
     }
     if (g->G < 1 || g->G > 1024) { *why = "occupancy grid side must be 1..1024"; return FFN_E_CONFIG; }
     if (g->background < 0 || g->background > 2) { *why = "background must be 0 (black), 1 (white) or 2 (random)"; return FFN_E_CONFIG; }
+    if (g->mlp_precision != 0 && g->mlp_precision != 1) { *why = "mlp_precision must be 0 (fp32) or 1 (fp16 tensor cores)"; return FFN_E_CONFIG; }
     uint64_t expect = 0;
     for (int l = 0; l < FFN_N_LEVELS; ++l) {
         if (g->level_log2[l] < 1 || g->level_log2[l] > 24) { *why = "per-level table size must be 2^1..2^24"; return FFN_E_CONFIG; }
@@ -134,6 +149,7 @@ StepArgs base_args(ffn_ctx* c, const void* rays, const void* targets, void* out,
     a.out = static_cast<float4*>(out);
     a.grad_table = c->grads;
     a.partials = c->partials;
+    a.status = c->status;
     a.n_rays = n;
     a.ray_offset = s->ray_offset;
     a.sh_mult = s->sh_mult;
@@ -210,14 +226,15 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
         delete c;
         return cuda_fail(nullptr, e, "shared-memory attribute");
     }
-    c->max_grid = sms;
+    c->max_grid = sms * c->ctas_per_sm;
     const size_t Pb = (size_t)c->Pw * sizeof(float);
     const size_t Tb = c->table_floats * sizeof(float);
     const size_t Gb = (size_t)cfg->G * cfg->G * cfg->G * sizeof(uint32_t);
     struct { void** p; size_t n; } allocs[] = {
         {(void**)&c->params, Pb}, {(void**)&c->adam_m, Pb}, {(void**)&c->adam_v, Pb},
         {(void**)&c->table, Tb}, {(void**)&c->occ_in, Gb}, {(void**)&c->occ_st, Gb},
-        {(void**)&c->grads, Tb + Pb}, {(void**)&c->partials, (size_t)c->max_grid * Pb}};
+        {(void**)&c->grads, Tb + Pb}, {(void**)&c->partials, (size_t)c->max_grid * Pb},
+        {(void**)&c->status, sizeof(int)}};
     for (auto& al : allocs) {
         if ((e = cudaMalloc(al.p, al.n)) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "device allocation"); }
         cudaMemset(*al.p, 0, al.n);
@@ -240,7 +257,7 @@ int ffn_destroy(ffn_ctx* c) {
     DeviceGuard guard(c->device);
     cudaDeviceSynchronize();
     void* ptrs[] = {c->params, c->adam_m, c->adam_v, c->table, c->table_m, c->table_v, c->occ_in,
-                    c->occ_st, c->grads, c->partials};
+                    c->occ_st, c->grads, c->partials, c->status};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -409,6 +426,17 @@ int ffn_hash_encode_bwd(ffn_ctx* c, const float* pts, const float* denc, int64_t
     else hash_bwd_kernel<4><<<blocks, 256, 0, st>>>(c->dc, c->grads, pts, denc, n);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "hash scatter launch");
+}
+
+int ffn_status(ffn_ctx* c, uint32_t* status) {
+    if (!c || !status) return fail(c, FFN_E_CONFIG, "null argument");
+    DeviceGuard guard(c->device);
+    int h = 0;
+    cudaError_t e = cudaMemcpy(&h, c->status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(c, e, "status read");
+    cudaMemset(c->status, 0, sizeof(int));
+    *status = (uint32_t)h;
+    return FFN_OK;
 }
 
 int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float b1, float b2,

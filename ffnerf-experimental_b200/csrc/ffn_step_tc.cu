@@ -1,0 +1,586 @@
+// ffn_step_tc.cu -- the fused training step with the MLPs on the 5th-generation tensor cores.
+//
+// Same tile structure as fused_step_kernel (one CTA = 128 samples, thread t = sample t), with
+// every dense layer of ffnerf_train_step (ffnerf_OG.cl:1378-1466, 1930-2082) and every per-layer
+// reduction of update_ffnerf_oneWG (weight_update.cl:210-314) issued as tcgen05.mma:
+//
+//   forward       ACC[128 x N] = X[128 x K] * W^T         X K-major, W K-major (fp16 in, fp32 acc)
+//   backward      ACC[128 x N] = D[128 x K] * W           D K-major, W read MN-major
+//   weight grad   dW[64 x N]  += D^T[64 x 128] * X[128 x N]   both read MN-major, accumulated in
+//                 TMEM over every tile the CTA processes; bias grads as D^T * e_0 with a constant
+//                 one-hot tile.
+//
+// Accumulators live in tensor memory; the epilogues (bias, ReLU, masks, fp16 packing) run in the
+// thread that owns the row (TMEM lane t = sample t).  Deltas are stored scaled by DELTA_SCALE in
+// fp16 and unscaled on the way out.  All operand tiles use the core-matrix interleaved layout
+// of ffn_tcgen05.cuh.  Shared memory ~100 KB and 256 TMEM columns (F=2, ND=1) let two CTAs share
+// an SM.  Every mbarrier wait is bounded; on a timeout the CTA flags the status word, stops issuing
+// work and releases its tensor memory.
+#include "ffn_common.cuh"
+#include "ffn_hashgrid.cuh"
+#include "ffn_raymarch.cuh"
+#include "ffn_tcgen05.cuh"
+
+namespace ffn {
+
+constexpr float DELTA_SCALE = 1024.0f;
+constexpr uint32_t WAIT_LIMIT = 1u << 26;   // polls of an mbarrier before a wait is declared failed
+
+template <int F, int ND>
+struct TcPlan {
+    static constexpr int ROWS = 128;
+    static constexpr int LPOS = 16 * F;
+    // fp16 operand tiles (bytes), each a multiple of 1 KB
+    static constexpr int X0 = 0;
+    static constexpr int HD = X0 + ROWS * LPOS * 2;           // ND density hidden tiles [128 x 64]
+    static constexpr int XC = HD + ND * ROWS * 64 * 2;        // colour input [128 x 32]
+    static constexpr int C1 = XC + ROWS * 32 * 2;             // colour hidden 1 [128 x 64]
+    static constexpr int C2 = C1 + ROWS * 64 * 2;             // colour hidden 2 [128 x 64]
+    static constexpr int DC = C2 + ROWS * 64 * 2;             // output delta [128 x 16]
+    static constexpr int ONES = DC + ROWS * 16 * 2;           // one-hot [128 x 8]
+    // fp16 weights, rows = outputs, columns = inputs
+    static constexpr int W_DIN = ONES + ROWS * 8 * 2;         // [64 x LPOS]
+    static constexpr int W_D01 = W_DIN + 64 * LPOS * 2;       // [64 x 64] (ND = 2)
+    static constexpr int W_DOUT = W_D01 + (ND >= 2 ? 64 * 64 * 2 : 0);   // [16 x 64]
+    static constexpr int W_CIN = W_DOUT + 16 * 64 * 2;        // [64 x 32]
+    static constexpr int W_C01 = W_CIN + 64 * 32 * 2;         // [64 x 64]
+    static constexpr int W_COUT = W_C01 + 64 * 64 * 2;        // [16 x 64], rows 3..15 zero
+    // fp32 biases and output-layer bias-gradient accumulators
+    static constexpr int BIAS = W_COUT + 16 * 64 * 2;         // bd_0[64] bd_1[64] bd_out[16] bc_0[64] bc_1[64] bc_out[16]
+    static constexpr int BGRAD = BIAS + (64 * 2 + 16 + 64 * 2 + 16) * 4;   // bd_out[16], bc_out[16]
+    // ray-phase arrays
+    static constexpr int RAY = BGRAD + 32 * 4;
+    static constexpr int RAY_BYTES = ROWS * 6 * 4 + ROWS * 16 + ROWS * 16 + 8 * 2 * 4 + 8 * 16 * 4;
+    static constexpr int MISC = RAY + RAY_BYTES;               // mbarrier (8), tmem base (4), abort (4)
+    static constexpr int BYTES = MISC + 64;
+    // tensor-memory columns
+    static constexpr uint32_t ACC = 0;                         // per-tile accumulator (64 cols)
+    static constexpr uint32_t DW_C01 = 64;
+    static constexpr uint32_t DW_DIN = 128;
+    static constexpr uint32_t DW_CIN = DW_DIN + LPOS;
+    static constexpr uint32_t DW_COUT_T = DW_CIN + 32;         // [64 in x 16 out]
+    static constexpr uint32_t DW_DOUT_T = DW_COUT_T + 16;      // [64 in x 16 out]
+    static constexpr uint32_t B_D0 = DW_DOUT_T + 16;
+    static constexpr uint32_t B_C0 = B_D0 + 8;
+    static constexpr uint32_t B_C1 = B_C0 + 8;
+    static constexpr uint32_t DW_D01 = B_C1 + 8;               // ND = 2
+    static constexpr uint32_t B_D1 = DW_D01 + 64;
+    static constexpr uint32_t USED = ND >= 2 ? B_D1 + 8 : B_C1 + 8;
+    static constexpr uint32_t TMEM_COLS = USED <= 256 ? 256 : 512;
+    static constexpr int CTAS_PER_SM = (TMEM_COLS == 256 && BYTES <= 110 * 1024) ? 2 : 1;
+};
+
+// Converts one fp32 weight matrix [rows x cols] (row-major, from the parameter blob) into an
+// interleaved fp16 tile; rows beyond `rows` up to `pad_rows` are zero.
+__device__ __forceinline__ void stage_weight(unsigned char* tile, const float* W, int rows, int pad_rows, int cols) {
+    for (int e = threadIdx.x; e < pad_rows * (cols / 8); e += blockDim.x) {
+        const int r = e / (cols / 8), c0 = (e - r * (cols / 8)) * 8;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = r < rows ? W[r * cols + c0 + i] : 0.0f;
+        tc::st_chunk8(tile, r, c0, cols, v);
+    }
+}
+
+// Issues ACC (+)= A * B for a K range in steps of 16 (one thread).
+__device__ __forceinline__ void gemm(uint32_t d, uint32_t a, int a_cols, bool a_mn, uint32_t b, int b_cols, bool b_mn,
+                                     int M, int N, int K, uint32_t accumulate) {
+    const uint32_t idesc = tc::idesc_f16(M, N, a_mn, b_mn);
+    const uint32_t a_step = a_mn ? 2u * (uint32_t)(a_cols / 8) * 128u : 256u;
+    const uint32_t b_step = b_mn ? 2u * (uint32_t)(b_cols / 8) * 128u : 256u;
+    for (int k = 0; k < K / 16; ++k) {
+        const uint64_t ad = a_mn ? tc::desc_mnmajor(a + k * a_step, a_cols) : tc::desc_kmajor(a + k * a_step, a_cols);
+        const uint64_t bd = b_mn ? tc::desc_mnmajor(b + k * b_step, b_cols) : tc::desc_kmajor(b + k * b_step, b_cols);
+        tc::mma_f16(d, ad, bd, idesc, (k > 0 || accumulate) ? 1u : 0u);
+    }
+}
+
+// One row (this thread's sample) of an ACC region into registers.
+template <int N>
+__device__ __forceinline__ void acc_row(uint32_t tmem, uint32_t col, float (&v)[N]) {
+    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+#pragma unroll
+    for (int j = 0; j < N; j += 16) {
+        float t[16];
+        tc::tmem_ld16(tmem + lane + col + j, t);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[j + i] = t[i];
+    }
+    tc::tmem_wait_ld();
+}
+
+template <int N>
+__device__ __forceinline__ void store_row(unsigned char* tile, int cols, const float (&v)[N]) {
+#pragma unroll
+    for (int c = 0; c < N; c += 8) tc::st_chunk8(tile, threadIdx.x, c, cols, v + c);
+}
+template <int N>
+__device__ __forceinline__ void load_row_h(const unsigned char* tile, int cols, float (&v)[N]) {
+#pragma unroll
+    for (int c = 0; c < N; c += 8) tc::ld_chunk8(tile, threadIdx.x, c, cols, v + c);
+}
+
+// Epilogue of a forward layer: row = relu(ACC + bias) for N columns, 16 at a time, into `tile`.
+__device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N, const float* bias, unsigned char* tile,
+                                              int cols) {
+    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+    for (int j = 0; j < N; j += 16) {
+        float v[16];
+        tc::tmem_ld16(tmem + lane + col + j, v);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = fmaxf(v[i] + bias[j + i], 0.0f);
+        tc::st_chunk8(tile, threadIdx.x, j, cols, v);
+        tc::st_chunk8(tile, threadIdx.x, j + 8, cols, v + 8);
+    }
+}
+
+// Epilogue of a backward layer: row = ACC masked by (activation in `tile` > 0), written in place.
+__device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N, unsigned char* tile, int cols) {
+    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+    for (int j = 0; j < N; j += 16) {
+        float v[16], act[16];
+        tc::tmem_ld16(tmem + lane + col + j, v);
+        tc::ld_chunk8(tile, threadIdx.x, j, cols, act);
+        tc::ld_chunk8(tile, threadIdx.x, j + 8, cols, act + 8);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = act[i] > 0.0f ? v[i] : 0.0f;
+        tc::st_chunk8(tile, threadIdx.x, j, cols, v);
+        tc::st_chunk8(tile, threadIdx.x, j + 8, cols, v + 8);
+    }
+}
+
+// Hash encoding of this thread's sample straight into its fp16 row of the X0 tile, one 8-feature
+// chunk (8/F levels, 64/F independent gathers) at a time.
+template <int F>
+__device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __restrict__ table, V3 p, bool hit,
+                                            unsigned char* tile) {
+    constexpr int LPOS = L * F, LV = 8 / F;
+#pragma unroll 1
+    for (int q = 0; q < LPOS / 8; ++q) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        if (hit) {
+#pragma unroll
+            for (int li = 0; li < LV; ++li) {
+                const int lvl = q * LV + li;
+                Corner8 k;
+                level_corners<F>(c, p, lvl, k);
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    if constexpr (F == 2) {
+                        const float2 t = __ldg(reinterpret_cast<const float2*>(table + k.base[cc]));
+                        v[li * 2] = fmaf(k.w[cc], t.x, v[li * 2]);
+                        v[li * 2 + 1] = fmaf(k.w[cc], t.y, v[li * 2 + 1]);
+                    } else {
+                        const float4 t = __ldg(reinterpret_cast<const float4*>(table + k.base[cc]));
+                        v[li * 4] = fmaf(k.w[cc], t.x, v[li * 4]);
+                        v[li * 4 + 1] = fmaf(k.w[cc], t.y, v[li * 4 + 1]);
+                        v[li * 4 + 2] = fmaf(k.w[cc], t.z, v[li * 4 + 2]);
+                        v[li * 4 + 3] = fmaf(k.w[cc], t.w, v[li * 4 + 3]);
+                    }
+                }
+            }
+        }
+        tc::st_chunk8(tile, threadIdx.x, q * 8, LPOS, v);
+    }
+}
+
+// Hash-grid gradient from the ACC region (scaled deltas times Wd_in), 16 features at a time,
+// scattered with vector atomics (ffnerf_OG.cl:2090-2173).
+template <int F>
+__device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
+                                                  V3 p, float unscale) {
+    constexpr int LPOS = L * F, LV = 16 / F;
+    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+#pragma unroll 1
+    for (int j = 0; j < LPOS; j += 16) {
+        float g[16];
+        tc::tmem_ld16(tmem + lane + col + j, g);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int li = 0; li < LV; ++li) {
+            const int lvl = j / F + li;
+            float gf[F];
+            bool any = false;
+#pragma unroll
+            for (int f = 0; f < F; ++f) {
+                const float v = g[li * F + f] * unscale;
+                gf[f] = isfinite(v) ? v : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
+                any |= gf[f] != 0.0f;
+            }
+            if (!any) continue;
+            Corner8 k;
+            level_corners<F>(c, p, lvl, k);
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                const float w = k.w[cc];
+                if constexpr (F == 2)
+                    atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
+                else
+                    atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
+                              make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+            }
+        }
+    }
+}
+
+template <int F, int ND>
+__global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a) {
+    using PL = TcPlan<F, ND>;
+    constexpr int LPOS = PL::LPOS;
+    extern __shared__ __align__(1024) unsigned char smem_tc[];
+    unsigned char* smem = smem_tc;
+    const DevConfig& c = a.c;
+    const ParamLayout& lo = a.lo;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    unsigned char* tX0 = smem + PL::X0;
+    unsigned char* tXC = smem + PL::XC;
+    unsigned char* tC1 = smem + PL::C1;
+    unsigned char* tC2 = smem + PL::C2;
+    unsigned char* tDC = smem + PL::DC;
+    float* bias = reinterpret_cast<float*>(smem + PL::BIAS);
+    float* bgrad = reinterpret_cast<float*>(smem + PL::BGRAD);
+    float* rayb = reinterpret_cast<float*>(smem + PL::RAY);
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + PL::MISC);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PL::MISC + 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + PL::MISC + 12);
+    const uint32_t sbase = tc::smem_u32(smem);
+    auto S = [&](int off) { return sbase + (uint32_t)off; };
+    auto tH = [&](int l) { return smem + PL::HD + l * 128 * 64 * 2; };
+
+    const bool train = a.do_train != 0;
+    const bool probe = a.probe != 0;
+    const bool backward = train && !probe;
+
+    // ---- one-time set-up: barrier, tensor memory, fp16 weights, biases, one-hot tile
+    if (tid == 0) {
+        tc::mbar_init(mbar, 1);
+        *abort_flag = 0;
+    }
+    if (warp == 0) tc::tmem_alloc(tmem_slot, PL::TMEM_COLS);
+    const float* P = a.params;
+    stage_weight(smem + PL::W_DIN, P + lo.off[P_WD_IN], 64, 64, LPOS);
+    if (ND >= 2) stage_weight(smem + PL::W_D01, P + lo.off[P_WD_01], 64, 64, 64);
+    stage_weight(smem + PL::W_DOUT, P + lo.off[P_WD_OUT], 16, 16, 64);
+    stage_weight(smem + PL::W_CIN, P + lo.off[P_WC_IN], 64, 64, 32);
+    stage_weight(smem + PL::W_C01, P + lo.off[P_WC_01], 64, 64, 64);
+    stage_weight(smem + PL::W_COUT, P + lo.off[P_WC_OUT], 3, 16, 64);
+    for (int i = tid; i < 64; i += 128) {
+        bias[i] = P[lo.off[P_BD_0] + i];
+        bias[64 + i] = ND >= 2 ? P[lo.off[P_BD_1] + i] : 0.0f;
+        bias[144 + i] = P[lo.off[P_BC_0] + i];
+        bias[208 + i] = P[lo.off[P_BC_1] + i];
+    }
+    if (tid < 16) {
+        bias[128 + tid] = P[lo.off[P_BD_OUT] + tid];
+        bias[272 + tid] = tid < 3 ? P[lo.off[P_BC_OUT] + tid] : 0.0f;
+    }
+    if (tid < 32) bgrad[tid] = 0.0f;
+    {
+        float v[8] = {1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        tc::st_chunk8(smem + PL::ONES, tid, 0, 8, v);
+    }
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    uint32_t phase = 0;
+    bool dw_started = false;
+
+    // Commit the MMAs issued so far and wait for them (all threads).
+    auto sync_mma = [&]() {
+        if (tid == 0) tc::commit(mbar);
+        if (!*abort_flag) {
+            if (!tc::mbar_wait(mbar, phase, WAIT_LIMIT)) {
+                *abort_flag = 1;
+                if (a.status) atomicOr(a.status, 4);
+            }
+        }
+        phase ^= 1u;
+        tc::fence_after_sync();
+    };
+    // All threads have finished reading TMEM and writing shared operands: MMAs may be issued.
+    auto handoff = [&]() {
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+    };
+
+    const V3 bmin = v3(c.bmin[0], c.bmin[1], c.bmin[2]);
+    const V3 bmax = v3(c.bmax[0], c.bmax[1], c.bmax[2]);
+    const V3 bsize = vsub(bmax, bmin);
+    const V3 inv_box = v3(fd(1.0f, bsize.x), fd(1.0f, bsize.y), fd(1.0f, bsize.z));
+    const int spr = c.spr;
+    const int rl = tid / spr, lid = tid - rl * spr, rbase = rl * spr;
+    const int rays_per_tile = 128 / spr;
+    const int n_tiles = (int)((a.n_rays + rays_per_tile - 1) / rays_per_tile);
+    float* sCand = rayb;
+    float* sCdf = sCand + 128;
+    float* sTs = sCdf + 128;
+    float* sDTs = sTs + 128;
+    float* sTr = sDTs + 128;
+    uint32_t* sKey = reinterpret_cast<uint32_t*>(sTr + 128);
+    float4* sSeg = reinterpret_cast<float4*>(sKey + 128);
+    float2* sAffS = reinterpret_cast<float2*>(sSeg + 128);
+    float2* sAffE = sAffS + 128;
+    uint32_t* sChg = reinterpret_cast<uint32_t*>(sAffE + 128);
+    float* sRay = reinterpret_cast<float*>(sChg + 16);
+
+    for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+        const uint32_t ray_idx = (uint32_t)tile * rays_per_tile + rl;
+        const bool valid = ray_idx < a.n_rays;
+        const uint32_t ray_id = a.ray_offset + ray_idx;
+        float4 ro = make_float4(0.f, 0.f, 0.f, 0.f), rd = make_float4(0.f, 0.f, 1.f, 0.f);
+        if (valid) { ro = a.rays[2 * ray_idx]; rd = a.rays[2 * ray_idx + 1]; }
+        const V3 o = v3(ro.x, ro.y, ro.z), d = v3(rd.x, rd.y, rd.z);
+        RayTile R{sCand, sCdf, sTs, sDTs, sTr, sKey, sSeg, sAffS, sAffE, sChg, sRay, tid, spr, rl, lid, rbase,
+                  ray_idx, ray_id, valid, train, probe, o, d, bmin, bmax, bsize, inv_box, (float)c.G, 1.0f / (float)spr};
+        bool hit;
+        int idx_sel;
+        ray_sampler(a, R, hit, idx_sel);
+        const float* rs = sRay + rl * 16;
+        const float t_s = sTs[tid];
+        const float dt_s = sDTs[tid];
+        const V3 xs = ray_point(o, d, t_s);
+        const V3 pn = normalize_pos(c, xs);
+
+        // ---------------- forward MLP on the tensor cores
+        float sigma = 0.0f, rgb[3] = {0.f, 0.f, 0.f}, dout0 = 0.0f;
+        if (probe && a.bypass) {
+            float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (valid) b = a.bypass[(size_t)ray_idx * spr + lid];
+            sigma = b.x; rgb[0] = b.y; rgb[1] = b.z; rgb[2] = b.w;
+        } else {
+            encode_rows<F>(c, a.table, pn, hit, tX0);
+            handoff();
+            if (tid == 0) gemm(tmem + PL::ACC, S(PL::X0), LPOS, false, S(PL::W_DIN), LPOS, false, 128, 64, LPOS, 0);
+            sync_mma();
+            epi_bias_relu(tmem, PL::ACC, 64, bias, tH(0), 64);
+            if (ND >= 2) {
+                handoff();
+                if (tid == 0) gemm(tmem + PL::ACC, S(PL::HD), 64, false, S(PL::W_D01), 64, false, 128, 64, 64, 0);
+                sync_mma();
+                epi_bias_relu(tmem, PL::ACC, 64, bias + 64, tH(ND - 1), 64);
+            }
+            handoff();
+            if (tid == 0)
+                gemm(tmem + PL::ACC, S(PL::HD + (ND - 1) * 128 * 64 * 2), 64, false, S(PL::W_DOUT), 64, false, 128, 16, 64, 0);
+            sync_mma();
+            {
+                float v[32];
+                float dv[16];
+                acc_row<16>(tmem, PL::ACC, dv);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = dv[j] + bias[128 + j];
+                dout0 = v[0];
+                sigma = softplus(fclamp(dout0, -10.0f, 10.0f));
+                float sh[L_DIR];
+                sh16(d.x, d.y, d.z, sh);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[16 + j] = sh[j] * a.sh_mult;
+                store_row<32>(tXC, 32, v);
+            }
+            handoff();
+            if (tid == 0) gemm(tmem + PL::ACC, S(PL::XC), 32, false, S(PL::W_CIN), 32, false, 128, 64, 32, 0);
+            sync_mma();
+            epi_bias_relu(tmem, PL::ACC, 64, bias + 144, tC1, 64);
+            handoff();
+            if (tid == 0) gemm(tmem + PL::ACC, S(PL::C1), 64, false, S(PL::W_C01), 64, false, 128, 64, 64, 0);
+            sync_mma();
+            epi_bias_relu(tmem, PL::ACC, 64, bias + 208, tC2, 64);
+            handoff();
+            if (tid == 0) gemm(tmem + PL::ACC, S(PL::C2), 64, false, S(PL::W_COUT), 64, false, 128, 16, 64, 0);
+            sync_mma();
+            {
+                float v[16];
+                acc_row<16>(tmem, PL::ACC, v);
+#pragma unroll
+                for (int k = 0; k < 3; ++k) rgb[k] = sigmoid_soft(v[k] + bias[272 + k]);
+            }
+        }
+        if (dt_s <= 0.0f) sigma = 0.0f;
+
+        // ---------------- compositing, loss gradient, occupancy proposals
+        float T_s, dLds, dLdc[3];
+        uint32_t chg0, chg1;
+        ray_composite(a, R, rs, sigma, rgb, xs, t_s, dt_s, T_s, dLds, dLdc, chg0, chg1);
+
+        if (probe) {
+            if (valid) {
+                const size_t s = (size_t)ray_idx * spr + lid;
+                if (a.dbg_t) a.dbg_t[s] = t_s;
+                if (a.dbg_dt) a.dbg_dt[s] = dt_s;
+                if (a.dbg_idx) a.dbg_idx[s] = idx_sel;
+                if (a.dbg_sigma) a.dbg_sigma[s] = sigma;
+                if (a.dbg_rgb) { a.dbg_rgb[3 * s] = rgb[0]; a.dbg_rgb[3 * s + 1] = rgb[1]; a.dbg_rgb[3 * s + 2] = rgb[2]; }
+                if (a.dbg_trans) a.dbg_trans[s] = T_s;
+                if (a.dbg_flags && lid == 0) { a.dbg_flags[2 * ray_idx] = chg0; a.dbg_flags[2 * ray_idx + 1] = chg1; }
+            }
+        }
+        if (!backward) {
+            tc::fence_before_sync();
+            __syncthreads();
+            continue;
+        }
+
+        // ---------------- output deltas (ffnerf_OG.cl:1858-1891)
+        float dcout[3], ddout0;
+        {
+            const float Dh = 0.5f * vlength(bsize);
+            const float t = t_s, dtl = dt_s;
+            const float num = t * t + t * dtl + (dtl * dtl / 3.0f);
+            const float den = Dh * Dh + Dh * dtl + (dtl * dtl / 3.0f);
+            const float xr = t / fmaxf(Dh, 1.0e-12f);
+            const float sflag = xr >= 1.0f ? 0.0f : 1.0f;
+            const float gate = (1.0f - sflag) * 1.0f + sflag * powf(fmaxf(xr, 1.0e-12f), 0.2f);
+            float f_vol = gate * num / fmaxf(den, 1.0e-12f);
+            if (!valid || !hit) f_vol = 0.0f;
+            const float d_sigma = f_vol * dLds;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) dcout[k] = (f_vol * dLdc[k]) * ((rgb[k] * (1.0f - rgb[k])) * 0.5f);
+            ddout0 = 1.0f * d_sigma * softplus_prime(fclamp(dout0, -18.0f, 18.0f));
+        }
+        {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+            v[0] = dcout[0] * DELTA_SCALE; v[1] = dcout[1] * DELTA_SCALE; v[2] = dcout[2] * DELTA_SCALE;
+            store_row<16>(tDC, 16, v);
+            // colour-head bias gradient: warp sums, then one shared-memory add per warp
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                float s = v[k];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if ((tid & 31) == 0) atomicAdd(bgrad + 16 + k, s);
+            }
+        }
+        const uint32_t acc0 = dw_started ? 1u : 0u;
+        handoff();
+        if (tid == 0) {
+            gemm(tmem + PL::DW_COUT_T, S(PL::C2), 64, true, S(PL::DC), 16, true, 64, 16, 128, acc0);  // dWc_out^T
+            gemm(tmem + PL::ACC, S(PL::DC), 16, false, S(PL::W_COUT), 64, true, 128, 64, 16, 0);     // dC2
+        }
+        sync_mma();
+        {
+            epi_relu_mask(tmem, PL::ACC, 64, tC2, 64);
+        }
+        handoff();
+        if (tid == 0) {
+            gemm(tmem + PL::DW_C01, S(PL::C2), 64, true, S(PL::C1), 64, true, 64, 64, 128, acc0);    // dWc_01
+            gemm(tmem + PL::B_C1, S(PL::C2), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);     // dbc_1
+            gemm(tmem + PL::ACC, S(PL::C2), 64, false, S(PL::W_C01), 64, true, 128, 64, 64, 0);      // dC1
+        }
+        sync_mma();
+        {
+            epi_relu_mask(tmem, PL::ACC, 64, tC1, 64);
+        }
+        handoff();
+        if (tid == 0) {
+            gemm(tmem + PL::DW_CIN, S(PL::C1), 64, true, S(PL::XC), 32, true, 64, 32, 128, acc0);    // dWc_in
+            gemm(tmem + PL::B_C0, S(PL::C1), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);     // dbc_0
+            gemm(tmem + PL::ACC, S(PL::C1), 64, false, S(PL::W_CIN), 32, true, 128, 16, 64, 0);      // dDout
+        }
+        sync_mma();
+        {
+            float v[16];
+            acc_row<16>(tmem, PL::ACC, v);
+            v[0] += ddout0 * DELTA_SCALE;
+            // delta at the density output replaces the colour input's first 16 columns
+#pragma unroll
+            for (int cc = 0; cc < 16; cc += 8) tc::st_chunk8(tXC, tid, cc, 32, v + cc);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                float s = v[k];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if ((tid & 31) == 0) atomicAdd(bgrad + k, s);
+            }
+        }
+        const uint32_t hlast = S(PL::HD + (ND - 1) * 128 * 64 * 2);
+        handoff();
+        if (tid == 0) {
+            gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, S(PL::XC), 32, true, 64, 16, 128, acc0);     // dWd_out^T
+            gemm(tmem + PL::ACC, S(PL::XC), 32, false, S(PL::W_DOUT), 64, true, 128, 64, 16, 0);     // dH_last
+        }
+        sync_mma();
+        {
+            epi_relu_mask(tmem, PL::ACC, 64, tH(ND - 1), 64);
+        }
+        if (ND >= 2) {
+            handoff();
+            if (tid == 0) {
+                gemm(tmem + PL::DW_D01, hlast, 64, true, S(PL::HD), 64, true, 64, 64, 128, acc0);    // dWd_01
+                gemm(tmem + PL::B_D1, hlast, 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);     // dbd_1
+                gemm(tmem + PL::ACC, hlast, 64, false, S(PL::W_D01), 64, true, 128, 64, 64, 0);      // dH_0
+            }
+            sync_mma();
+            epi_relu_mask(tmem, PL::ACC, 64, tH(0), 64);
+        }
+        handoff();
+        if (tid == 0) {
+            gemm(tmem + PL::DW_DIN, S(PL::HD), 64, true, S(PL::X0), LPOS, true, 64, LPOS, 128, acc0);  // dWd_in
+            gemm(tmem + PL::B_D0, S(PL::HD), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);       // dbd_0
+            gemm(tmem + PL::ACC, S(PL::HD), 64, false, S(PL::W_DIN), LPOS, true, 128, LPOS, 64, 0);    // hash grads
+        }
+        sync_mma();
+        dw_started = true;
+        if (hit && valid) scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE);
+        tc::fence_before_sync();
+        __syncthreads();
+    }
+
+    // ---- weight-gradient partials of this CTA: TMEM (M = 64 layout) -> global, unscaled
+    if (backward && a.partials) {
+        float* part = a.partials + (size_t)blockIdx.x * lo.total;
+        const int lane = tid & 31;
+        const int row = warp * 16 + lane;              // M = 64: rows 16w..16w+15 live in lanes 32w..32w+15
+        const bool live = dw_started && !*abort_flag;
+        auto dump = [&](uint32_t col, int ncols, int dst_off, bool transposed, int out_rows, int in_cols) {
+            for (int j = 0; j < ncols; j += 16) {
+                float v[16];
+                tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + col + j, v);
+                tc::tmem_wait_ld();
+                if (lane < 16) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int n = j + i;
+                        const float g = live ? v[i] * (1.0f / DELTA_SCALE) : 0.0f;
+                        if (!transposed) { if (row < out_rows && n < in_cols) part[dst_off + row * in_cols + n] = g; }
+                        else { if (n < out_rows && row < in_cols) part[dst_off + n * in_cols + row] = g; }
+                    }
+                }
+            }
+        };
+        dump(PL::DW_DIN, LPOS, lo.off[P_WD_IN], false, 64, LPOS);
+        if (ND >= 2) dump(PL::DW_D01, 64, lo.off[P_WD_01], false, 64, 64);
+        dump(PL::DW_DOUT_T, 16, lo.off[P_WD_OUT], true, 16, 64);
+        dump(PL::DW_CIN, 32, lo.off[P_WC_IN], false, 64, 32);
+        dump(PL::DW_C01, 64, lo.off[P_WC_01], false, 64, 64);
+        dump(PL::DW_COUT_T, 16, lo.off[P_WC_OUT], true, 3, 64);
+        auto dump_bias = [&](uint32_t col, int dst_off) {
+            float v[16];
+            tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + col, v);
+            tc::tmem_wait_ld();
+            if (lane < 16) part[dst_off + row] = live ? v[0] * (1.0f / DELTA_SCALE) : 0.0f;
+        };
+        // bias accumulators are 8 columns wide; a 16-column load spans the next one, which is fine
+        dump_bias(PL::B_D0, lo.off[P_BD_0]);
+        if (ND >= 2) dump_bias(PL::B_D1, lo.off[P_BD_1]);
+        dump_bias(PL::B_C0, lo.off[P_BC_0]);
+        dump_bias(PL::B_C1, lo.off[P_BC_1]);
+        if (tid < 16) part[lo.off[P_BD_OUT] + tid] = live ? bgrad[tid] * (1.0f / DELTA_SCALE) : 0.0f;
+        if (tid < 4) part[lo.off[P_BC_OUT] + tid] = (live && tid < 3) ? bgrad[16 + tid] * (1.0f / DELTA_SCALE) : 0.0f;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, PL::TMEM_COLS);
+}
+
+}  // namespace ffn

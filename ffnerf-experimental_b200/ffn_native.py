@@ -34,7 +34,7 @@ class FfnConfig(C.Structure):
                 ("rho_min", C.c_float), ("rho_max", C.c_float), ("dt_min", C.c_float),
                 ("dt_max", C.c_float), ("t_near", C.c_float), ("t_far", C.c_float),
                 ("adam_beta1", C.c_float), ("adam_beta2", C.c_float), ("adam_eps", C.c_float),
-                ("table_adam_eps", C.c_float)]
+                ("table_adam_eps", C.c_float), ("mlp_precision", C.c_int32)]
 
 
 class FfnStep(C.Structure):
@@ -62,6 +62,7 @@ _SIGS = {
     "ffn_hash_encode": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_hash_encode_bwd": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_adam": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_float, _VP]),
+    "ffn_status": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
 }
 EXPORTED = tuple(_SIGS)
 
@@ -87,8 +88,11 @@ def load_library(path: Path | None = None):
     return lib
 
 
+MLP_PRECISIONS = {"fp32": 0, "fp16": 1}
+
+
 def make_ffn_config(geom: dict, table_optimizer: int = 0, max_rays: int = 0, adam_beta1=0.9,
-                    adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15) -> FfnConfig:
+                    adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15, mlp_precision: str = "fp32") -> FfnConfig:
     c = FfnConfig()
     for k in ("F", "ND", "NC", "spr", "G", "background"):
         setattr(c, k, int(geom[k]))
@@ -104,6 +108,7 @@ def make_ffn_config(geom: dict, table_optimizer: int = 0, max_rays: int = 0, ada
     for k in ("rho_min", "rho_max", "dt_min", "dt_max", "t_near", "t_far"):
         setattr(c, k, float(geom[k]))
     c.adam_beta1, c.adam_beta2, c.adam_eps, c.table_adam_eps = adam_beta1, adam_beta2, adam_eps, table_adam_eps
+    c.mlp_precision = MLP_PRECISIONS[mlp_precision]
     return c
 
 
@@ -135,11 +140,13 @@ class Context:
     """One native context (parameters, optimizer state, table, occupancy grids, gradients)."""
 
     def __init__(self, geom: dict, device: int = 0, table_optimizer: int = 0, max_rays: int = 0,
-                 adam_beta1=0.9, adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15):
+                 adam_beta1=0.9, adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15, mlp_precision: str = "fp32"):
         self.lib = load_library()
         self.geom = dict(geom)
         self.device = int(device)
-        self.cfg = make_ffn_config(geom, table_optimizer, max_rays, adam_beta1, adam_beta2, adam_eps, table_adam_eps)
+        self.mlp_precision = mlp_precision
+        self.cfg = make_ffn_config(geom, table_optimizer, max_rays, adam_beta1, adam_beta2, adam_eps, table_adam_eps,
+                                   mlp_precision)
         h = _VP()
         rc = self.lib.ffn_create(C.byref(self.cfg), self.device, C.byref(h))
         if rc != FFN_OK:
@@ -246,6 +253,12 @@ class Context:
         self._check(self.lib.ffn_occ_st_bytes(self.h, _ptr(buf), 1 if to_bytes else 0, self._stream(stream)),
                     "ffn_occ_st_bytes")
         self.launches += 1
+
+    def status(self) -> int:
+        """Device status word since the last call (0 = every kernel completed normally)."""
+        v = C.c_uint32()
+        self._check(self.lib.ffn_status(self.h, C.byref(v)), "ffn_status")
+        return int(v.value)
 
     def grad_buffer(self):
         p, n = _VP(), C.c_size_t()

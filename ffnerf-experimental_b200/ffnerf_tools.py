@@ -451,7 +451,7 @@ class Nerf:
                  f_per_level: int = F_PER_LEVEL, occ: OccParams | None = None, load_id: str | None = None,
                  rng_seed: int = 777, *, background: str = "black", finest_resolution: float | None = None,
                  level_log2=None, nd: int | None = None, nc: int | None = None, table_optimizer: str = "sgd",
-                 verbose: bool = True):
+                 mlp_precision: str = "fp32", verbose: bool = True):
         self.do_train = True
         self.verbose = verbose
         self.ctx = ctx
@@ -466,6 +466,9 @@ class Nerf:
         self.background = background
         self.finest_resolution = float(finest_resolution if finest_resolution is not None else fc.RESOLUTION_LVLMAX)
         self.table_optimizer = table_optimizer
+        if mlp_precision not in ffn_native.MLP_PRECISIONS:
+            raise ValueError("mlp_precision must be 'fp32' (CUDA cores) or 'fp16' (tensor cores)")
+        self.mlp_precision = mlp_precision
         self.M, self.L_DIR, self.C_OUT, self.D_D_OUT = M, L_DIR, C_OUT, D_OUT
         self.C_IN = D_OUT + L_DIR
         self.NDMAX, self.NCMAX = NDMAX, NCMAX
@@ -669,7 +672,8 @@ class Nerf:
             opt = {"sgd": 0, "adam": 1}[self.table_optimizer]
             self.native = ffn_native.Context(self.geometry(self.samples_per_ray), device=self.ctx.device.index,
                                              table_optimizer=opt, adam_beta1=float(self.ADAM_BETA1),
-                                             adam_beta2=float(self.ADAM_BETA2), adam_eps=float(self.ADAM_EPS))
+                                             adam_beta2=float(self.ADAM_BETA2), adam_eps=float(self.ADAM_EPS),
+                                             mlp_precision=self.mlp_precision)
             self._push_params_to_device()
         self.buf = {"native": self.native}
 

@@ -79,6 +79,8 @@ typedef struct ffn_config {
     float rho_min, rho_max, dt_min, dt_max, t_near, t_far;
     float adam_beta1, adam_beta2, adam_eps;   /* MLP (and table) Adam */
     float table_adam_eps;
+    int32_t mlp_precision;   /* 0: fp32 on the CUDA cores (reference-exact arithmetic),
+                                1: fp16 operands / fp32 accumulation on the tensor cores (tcgen05) */
 } ffn_config;
 
 typedef struct ffn_step_scalars {
@@ -144,6 +146,10 @@ int ffn_probe(ffn_ctx* ctx, const void* rays, const void* targets, void* out, ui
 int ffn_hash_encode(ffn_ctx* ctx, const float* pts, float* enc, int64_t n, void* stream);
 int ffn_hash_encode_bwd(ffn_ctx* ctx, const float* pts, const float* denc, int64_t n,
                         void* stream);
+/* Reads and clears the context's device status word (waits for the device): 0 when every kernel
+ * since the last call completed normally; bit 2 = a tensor-core wait exceeded its bound. */
+int ffn_status(ffn_ctx* ctx, uint32_t* status);
+
 /* Plain Adam over n float32 parameters (vectorised; beta/eps as given). */
 int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float beta1,
              float beta2, float eps, void* stream);
