@@ -24,7 +24,11 @@
 namespace ffn {
 
 constexpr float DELTA_SCALE = 1024.0f;
-constexpr uint32_t WAIT_LIMIT = 1u << 26;   // polls of an mbarrier before a wait is declared failed
+// The hash encoding is stored as X0 * INPUT_SCALE: freshly initialised tables give features of
+// ~1e-4, at the bottom of fp16's normal range; the first layer's accumulator and dWd_in are
+// divided by the same factor.
+constexpr float INPUT_SCALE = 256.0f;
+constexpr uint32_t WAIT_LIMIT = 1u << 22;   // polls of an mbarrier before a wait is declared failed
 
 template <int F, int ND>
 struct TcPlan {
@@ -120,16 +124,16 @@ __device__ __forceinline__ void load_row_h(const unsigned char* tile, int cols, 
     for (int c = 0; c < N; c += 8) tc::ld_chunk8(tile, threadIdx.x, c, cols, v + c);
 }
 
-// Epilogue of a forward layer: row = relu(ACC + bias) for N columns, 16 at a time, into `tile`.
+// Epilogue of a forward layer: row = relu(ACC * in_scale + bias) for N columns, 16 at a time.
 __device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N, const float* bias, unsigned char* tile,
-                                              int cols) {
+                                              int cols, float in_scale = 1.0f) {
     const uint32_t lane = (threadIdx.x & ~31u) << 16;
     for (int j = 0; j < N; j += 16) {
         float v[16];
         tc::tmem_ld16(tmem + lane + col + j, v);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = fmaxf(v[i] + bias[j + i], 0.0f);
+        for (int i = 0; i < 16; ++i) v[i] = fmaxf(fmaf(v[i], in_scale, bias[j + i]), 0.0f);
         tc::st_chunk8(tile, threadIdx.x, j, cols, v);
         tc::st_chunk8(tile, threadIdx.x, j + 8, cols, v + 8);
     }
@@ -184,6 +188,8 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
                 }
             }
         }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] *= INPUT_SCALE;
         tc::st_chunk8(tile, threadIdx.x, q * 8, LPOS, v);
     }
 }
@@ -361,7 +367,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             handoff();
             if (tid == 0) gemm(tmem + PL::ACC, S(PL::X0), LPOS, false, S(PL::W_DIN), LPOS, false, 128, 64, LPOS, 0);
             sync_mma();
-            epi_bias_relu(tmem, PL::ACC, 64, bias, tH(0), 64);
+            epi_bias_relu(tmem, PL::ACC, 64, bias, tH(0), 64, 1.0f / INPUT_SCALE);
             if (ND >= 2) {
                 handoff();
                 if (tid == 0) gemm(tmem + PL::ACC, S(PL::HD), 64, false, S(PL::W_D01), 64, false, 128, 64, 64, 0);
@@ -542,7 +548,8 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         const int lane = tid & 31;
         const int row = warp * 16 + lane;              // M = 64: rows 16w..16w+15 live in lanes 32w..32w+15
         const bool live = dw_started && !*abort_flag;
-        auto dump = [&](uint32_t col, int ncols, int dst_off, bool transposed, int out_rows, int in_cols) {
+        auto dump = [&](uint32_t col, int ncols, int dst_off, bool transposed, int out_rows, int in_cols,
+                        float extra = 1.0f) {
             for (int j = 0; j < ncols; j += 16) {
                 float v[16];
                 tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + col + j, v);
@@ -551,14 +558,14 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int n = j + i;
-                        const float g = live ? v[i] * (1.0f / DELTA_SCALE) : 0.0f;
+                        const float g = live ? v[i] * (extra / DELTA_SCALE) : 0.0f;
                         if (!transposed) { if (row < out_rows && n < in_cols) part[dst_off + row * in_cols + n] = g; }
                         else { if (n < out_rows && row < in_cols) part[dst_off + n * in_cols + row] = g; }
                     }
                 }
             }
         };
-        dump(PL::DW_DIN, LPOS, lo.off[P_WD_IN], false, 64, LPOS);
+        dump(PL::DW_DIN, LPOS, lo.off[P_WD_IN], false, 64, LPOS, 1.0f / INPUT_SCALE);
         if (ND >= 2) dump(PL::DW_D01, 64, lo.off[P_WD_01], false, 64, 64);
         dump(PL::DW_DOUT_T, 16, lo.off[P_WD_OUT], true, 16, 64);
         dump(PL::DW_CIN, 32, lo.off[P_WC_IN], false, 64, 32);
