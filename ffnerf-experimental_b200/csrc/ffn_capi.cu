@@ -148,6 +148,11 @@ StepArgs base_args(ffn_ctx* c, const void* rays, const void* targets, void* out,
     a.targets = static_cast<const float4*>(targets);
     a.out = static_cast<float4*>(out);
     a.grad_table = c->grads;
+    for (int l = 0; l < L; ++l) a.hash_coef[l] = 1.0f;
+    if (s->flags & FFN_STEP_TABLE_IMMEDIATE) {
+        a.grad_table = c->table;
+        for (int l = 0; l < L; ++l) a.hash_coef[l] = -(s->lr_f * c->cfg.hash_lr_scale[l]) * 0.5f;   // HASH_LR_RATE
+    }
     a.partials = c->partials;
     a.status = c->status;
     a.n_rays = n;
@@ -309,9 +314,10 @@ int ffn_forward_backward(ffn_ctx* c, const void* rays, const void* targets, void
     if (!targets || !aligned16(targets)) return fail(c, FFN_E_CONFIG, "targets must be a 16-byte aligned device pointer");
     DeviceGuard guard(c->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((s->flags & FFN_STEP_TABLE_IMMEDIATE) && c->cfg.table_optimizer != 0)
+        return fail(c, FFN_E_CONFIG, "immediate table updates need the SGD table optimizer");
     StepArgs a = base_args(c, rays, targets, out, n, s);
     a.do_train = 1;
-    a.grad_table = c->grads;
     int grid = 0;
     if ((rc = launch_fused(c, a, st, &grid)) != FFN_OK) return rc;
     reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
@@ -337,7 +343,9 @@ int ffn_apply_updates(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
     lc.start[L] = (uint32_t)c->table_floats;
     const uint32_t n4 = (uint32_t)(c->table_floats / 4);
     const int blocks = (int)((n4 + 255) / 256 < 148u * 16u ? (n4 + 255) / 256 : 148u * 16u);
-    if (g.table_optimizer == 1)
+    if (s->flags & FFN_STEP_TABLE_IMMEDIATE) {
+        // the table was updated inside the forward/backward pass
+    } else if (g.table_optimizer == 1)
         table_adam_kernel<<<blocks, 256, 0, st>>>(c->table, c->grads, c->table_m, c->table_v, n4, lc,
                                                    g.adam_beta1, g.adam_beta2, g.table_adam_eps);
     else

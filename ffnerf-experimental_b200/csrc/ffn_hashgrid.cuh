@@ -77,8 +77,21 @@ __device__ __forceinline__ V3 normalize_pos(const DevConfig& c, V3 x) {
     return v3(fclamp(p.x, 0.0f, hi), fclamp(p.y, 0.0f, hi), fclamp(p.z, 0.0f, hi));
 }
 
+// Reads one table entry: through L2 only (COHERENT, for tables updated during the kernel) or
+// through the read-only cache.
+template <bool COHERENT>
+__device__ __forceinline__ float2 table_ld2(const float* p) {
+    if constexpr (COHERENT) return __ldcg(reinterpret_cast<const float2*>(p));
+    else return __ldg(reinterpret_cast<const float2*>(p));
+}
+template <bool COHERENT>
+__device__ __forceinline__ float4 table_ld4(const float* p) {
+    if constexpr (COHERENT) return __ldcg(reinterpret_cast<const float4*>(p));
+    else return __ldg(reinterpret_cast<const float4*>(p));
+}
+
 // Writes the 16*F features of point p to a0 (a shared-memory row or a global output row).
-template <int F>
+template <int F, bool COHERENT = false>
 __device__ __forceinline__ void encode(const DevConfig& c, const float* __restrict__ table, V3 p,
                                        float* a0) {
 #pragma unroll 2
@@ -91,11 +104,11 @@ __device__ __forceinline__ void encode(const DevConfig& c, const float* __restri
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
             if constexpr (F == 2) {
-                const float2 t = __ldg(reinterpret_cast<const float2*>(table + k.base[cc]));
+                const float2 t = table_ld2<COHERENT>(table + k.base[cc]);
                 acc[0] = fmaf(k.w[cc], t.x, acc[0]);
                 acc[1] = fmaf(k.w[cc], t.y, acc[1]);
             } else {
-                const float4 t = __ldg(reinterpret_cast<const float4*>(table + k.base[cc]));
+                const float4 t = table_ld4<COHERENT>(table + k.base[cc]);
                 acc[0] = fmaf(k.w[cc], t.x, acc[0]);
                 acc[1] = fmaf(k.w[cc], t.y, acc[1]);
                 acc[2] = fmaf(k.w[cc], t.z, acc[2]);
@@ -109,7 +122,7 @@ __device__ __forceinline__ void encode(const DevConfig& c, const float* __restri
 
 template <int F>
 __device__ __forceinline__ void scatter_grad(const DevConfig& c, float* __restrict__ grad, V3 p,
-                                             const float* g /* 16*F */) {
+                                             const float* g /* 16*F */, const float* coef) {
 #pragma unroll 1
     for (int lvl = 0; lvl < L; ++lvl) {
         float gf[F];
@@ -120,7 +133,7 @@ __device__ __forceinline__ void scatter_grad(const DevConfig& c, float* __restri
 #pragma unroll
         for (int f = 0; f < F; ++f) {
             float v = gv[f];
-            gf[f] = isfinite(v) ? v : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
+            gf[f] = isfinite(v) ? coef[lvl] * v : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
             any |= gf[f] != 0.0f;
         }
         if (!any) continue;

@@ -21,7 +21,8 @@ struct StepArgs {
     const float4* rays;        // [n][2]: o, d
     const float4* targets;     // [n]
     float4* out;               // [n]
-    float* grad_table;         // table gradient accumulator (sum of g*w)
+    float* grad_table;         // destination of the hash scatter: gradient buffer or the table itself
+    float hash_coef[L];        // scatter value = (hash_coef[l] * g) * w: 1 (gradient) or -lr*2^(-0.1l)*0.5
     float* partials;           // [gridDim.x][P] per-CTA weight-gradient partials
     uint32_t n_rays;
     uint32_t ray_offset;

@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
             sigma = b.x; rgb[0] = b.y; rgb[1] = b.z; rgb[2] = b.w;
         } else {
             float* a0row = sA0 + tid * LDA0;
-            if (hit) encode<F>(c, a.table, pn, a0row);   // rays that miss the box contribute nothing
+            if (hit) encode<F, true>(c, a.table, pn, a0row);   // rays that miss the box contribute nothing
             else {
 #pragma unroll
                 for (int i = 0; i < LPOS; i += 4) *reinterpret_cast<float4*>(a0row + i) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
             load_row<M>(dv, sHd + tid * LDH);
             float* grow = sA0 + tid * LDA0;   // A0 is no longer needed: reuse for g
             dense_bwd<M, LPOS, false>(dv, Wd_in, nullptr, grow);
-            if (hit && valid) scatter_grad<F>(c, a.grad_table, pn, grow);
+            if (hit && valid) scatter_grad<F>(c, a.grad_table, pn, grow, a.hash_coef);
         }
         __syncthreads();
     }
@@ -576,7 +576,8 @@ __global__ void hash_bwd_kernel(const DevConfig c, float* __restrict__ grad, con
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float hi = 1.0f - 1.0e-6f;
         const V3 p = v3(fclamp(pts[3 * i], 0.f, hi), fclamp(pts[3 * i + 1], 0.f, hi), fclamp(pts[3 * i + 2], 0.f, hi));
-        scatter_grad<F>(c, grad, p, denc + i * (L * F));
+        const float one[L] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+        scatter_grad<F>(c, grad, p, denc + i * (L * F), one);
     }
 }
 

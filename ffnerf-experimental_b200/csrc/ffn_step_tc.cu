@@ -175,11 +175,11 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
 #pragma unroll
                 for (int cc = 0; cc < 8; ++cc) {
                     if constexpr (F == 2) {
-                        const float2 t = __ldg(reinterpret_cast<const float2*>(table + k.base[cc]));
+                        const float2 t = table_ld2<true>(table + k.base[cc]);
                         v[li * 2] = fmaf(k.w[cc], t.x, v[li * 2]);
                         v[li * 2 + 1] = fmaf(k.w[cc], t.y, v[li * 2 + 1]);
                     } else {
-                        const float4 t = __ldg(reinterpret_cast<const float4*>(table + k.base[cc]));
+                        const float4 t = table_ld4<true>(table + k.base[cc]);
                         v[li * 4] = fmaf(k.w[cc], t.x, v[li * 4]);
                         v[li * 4 + 1] = fmaf(k.w[cc], t.y, v[li * 4 + 1]);
                         v[li * 4 + 2] = fmaf(k.w[cc], t.z, v[li * 4 + 2]);
@@ -198,7 +198,7 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
 // scattered with vector atomics (ffnerf_OG.cl:2090-2173).
 template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
-                                                  V3 p, float unscale) {
+                                                  V3 p, float unscale, const float* coef) {
     constexpr int LPOS = L * F, LV = 16 / F;
     const uint32_t lane = (threadIdx.x & ~31u) << 16;
 #pragma unroll 1
@@ -214,7 +214,7 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
 #pragma unroll
             for (int f = 0; f < F; ++f) {
                 const float v = g[li * F + f] * unscale;
-                gf[f] = isfinite(v) ? v : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
+                gf[f] = isfinite(v) ? coef[lvl] * v : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
                 any |= gf[f] != 0.0f;
             }
             if (!any) continue;
@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         }
         sync_mma();
         dw_started = true;
-        if (hit && valid) scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE);
+        if (hit && valid) scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef);
         tc::fence_before_sync();
         __syncthreads();
     }

@@ -40,7 +40,10 @@ class FfnConfig(C.Structure):
 class FfnStep(C.Structure):
     _fields_ = [("lr_f", C.c_float), ("lr_t", C.c_float), ("sh_mult", C.c_float),
                 ("color_rel_lr", C.c_float), ("occ_strength", C.c_float), ("rng_u32", C.c_uint32),
-                ("ray_offset", C.c_uint32), ("table_lr_t", C.c_float), ("spr", C.c_uint32)]
+                ("ray_offset", C.c_uint32), ("table_lr_t", C.c_float), ("spr", C.c_uint32), ("flags", C.c_uint32)]
+
+
+STEP_TABLE_IMMEDIATE = 1
 
 
 _VP = C.c_void_p
@@ -113,10 +116,11 @@ def make_ffn_config(geom: dict, table_optimizer: int = 0, max_rays: int = 0, ada
 
 
 def make_step(lr_f=0.0, lr_t=0.0, sh_mult=1.0, color_rel_lr=1.0, occ_strength=0.0, rng_u32=0,
-              ray_offset=0, table_lr_t=0.0, spr=0) -> FfnStep:
+              ray_offset=0, table_lr_t=0.0, spr=0, table_immediate: bool = False) -> FfnStep:
     return FfnStep(float(np.float32(lr_f)), float(np.float32(lr_t)), float(np.float32(sh_mult)),
                    float(np.float32(color_rel_lr)), float(np.float32(occ_strength)), int(rng_u32) & 0xFFFFFFFF,
-                   int(ray_offset) & 0xFFFFFFFF, float(np.float32(table_lr_t)), int(spr))
+                   int(ray_offset) & 0xFFFFFFFF, float(np.float32(table_lr_t)), int(spr),
+                   STEP_TABLE_IMMEDIATE if table_immediate else 0)
 
 
 class _CudaArray:
@@ -215,12 +219,12 @@ class Context:
 
     def apply_updates(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_apply_updates(self.h, C.byref(step), self._stream(stream)), "ffn_apply_updates")
-        self.launches += 2
+        self.launches += 1 if step.flags & STEP_TABLE_IMMEDIATE else 2
 
     def train_step(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_train_step(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                             C.byref(step), self._stream(stream)), "ffn_train_step")
-        self.launches += 4
+        self.launches += 3 if step.flags & STEP_TABLE_IMMEDIATE else 4
 
     def render(self, rays, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_render(self.h, _ptr(rays), _ptr(out), int(n_rays), C.byref(step),

@@ -451,7 +451,7 @@ class Nerf:
                  f_per_level: int = F_PER_LEVEL, occ: OccParams | None = None, load_id: str | None = None,
                  rng_seed: int = 777, *, background: str = "black", finest_resolution: float | None = None,
                  level_log2=None, nd: int | None = None, nc: int | None = None, table_optimizer: str = "sgd",
-                 mlp_precision: str = "fp32", verbose: bool = True):
+                 mlp_precision: str = "fp32", table_update: str = "immediate", verbose: bool = True):
         self.do_train = True
         self.verbose = verbose
         self.ctx = ctx
@@ -466,6 +466,13 @@ class Nerf:
         self.background = background
         self.finest_resolution = float(finest_resolution if finest_resolution is not None else fc.RESOLUTION_LVLMAX)
         self.table_optimizer = table_optimizer
+        # "immediate": the SGD step lands in the table inside the fused kernel while other rays read
+        # it (the reference's Hogwild update, ffnerf_OG.cl:2155-2168); "deferred": gradients are
+        # summed into a buffer and applied after the kernel.  Adam tables and data-parallel runs
+        # (whose gradients are all-reduced first) always use "deferred".
+        if table_update not in ("immediate", "deferred"):
+            raise ValueError("table_update must be 'immediate' or 'deferred'")
+        self.table_update = table_update
         if mlp_precision not in ffn_native.MLP_PRECISIONS:
             raise ValueError("mlp_precision must be 'fp32' (CUDA cores) or 'fp16' (tensor cores)")
         self.mlp_precision = mlp_precision
@@ -801,6 +808,10 @@ class Nerf:
     def _get_rng_u32(self) -> np.uint32:
         return np.uint32(self.rng.integers(0, 2**32, dtype=np.uint32))
 
+    @property
+    def table_immediate(self) -> bool:
+        return self.table_update == "immediate" and self.table_optimizer == "sgd" and self.dp is None
+
     def enable_data_parallel(self, group=None, ray_offset: int | None = None):
         """Shards batches across the ranks of ``group``: this rank's rays start at global index
         ``ray_offset`` (default rank * num_rays of the current batch)."""
@@ -858,7 +869,8 @@ class Nerf:
                 lr_t = self.lr_t(lr_f)
                 s = ffn_native.make_step(lr_f=lr_f, lr_t=lr_t, sh_mult=sh_multiplier, color_rel_lr=color_MLP_rel_lr,
                                          occ_strength=occ_update_strength, rng_u32=int(rng_u32), ray_offset=offset,
-                                         table_lr_t=lr_t, spr=io.samples_per_ray)
+                                         table_lr_t=lr_t, spr=io.samples_per_ray,
+                                         table_immediate=self.table_immediate)
                 if self.fb_events is not None:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e0.record(q.stream)

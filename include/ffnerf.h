@@ -93,7 +93,15 @@ typedef struct ffn_step_scalars {
     uint32_t ray_offset;   /* global index of the first ray (data-parallel shards)          */
     float table_lr_t;      /* bias-corrected Adam step size for the table (optimizer 1)     */
     uint32_t spr;          /* samples per ray of this batch (16/32/64); 0 = ffn_config.spr  */
+    uint32_t flags;        /* FFN_STEP_* bits                                               */
 } ffn_step_scalars;
+
+/* ffn_step_scalars.flags: apply the hash-table SGD step inside ffn_forward_backward, as atomic adds
+ * of -lr_f * hash_lr_scale[l] * 0.5 * g * w into the table while other rays read it -- the
+ * reference's own (Hogwild) semantics.  The table part of FFN_BUF_GRADS stays zero and
+ * ffn_apply_updates skips the table pass.  Needs table_optimizer = 0; not for data-parallel runs,
+ * whose table gradients must be all-reduced first. */
+#define FFN_STEP_TABLE_IMMEDIATE 1u
 
 typedef struct ffn_ctx ffn_ctx;
 

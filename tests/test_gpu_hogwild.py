@@ -1,0 +1,108 @@
+"""Immediate (Hogwild) hash-table updates -- the reference's own semantics, where every sample's
+table gradient is added into the table as -lr * 2^(-0.1 l) * 0.5 * g * w while other rays of the
+same step read it (ffnerf_OG.cl:2155-2168) -- against the CPU oracle in sequential table mode
+(rays in order, each update applied at once: one legal schedule of the same race).
+
+Contracts:
+  * one step: the table change matches the oracle's within rel-L2 1e-3 (fp32 MLP) / 5e-2 (fp16
+    tensor-core MLP), the gradient buffer's table part stays zero;
+  * 100 training steps: per-step loss within 1e-3 relative, parameters and table within rel-L2
+    1e-2 of the oracle (fp32 MLP); the fp16 path keeps the loss within 1e-3 and the updates
+    within rel-L2 5e-2;
+  * ffn_train_step launches one kernel fewer (no table pass).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from _helpers import init_blob, init_occ, init_table, rays_toward_box, rel_l2, targets
+from ffn_config import make_geometry
+from oracle import OrcStep, make_orc_config
+import ffn_native as fn
+
+GEOM = dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0)
+TOL = {"fp32": (1e-3, 1e-2), "fp16": (5e-2, 5e-2)}
+MLP_GRAD_TOL = {"fp32": 1e-3, "fp16": 5e-2}
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _make(prec, seed, n_rays):
+    g = make_geometry(**GEOM)
+    ctx = fn.Context(g, mlp_precision=prec)
+    blob, table, occ = init_blob(g, seed), init_table(g, seed), init_occ(g, seed)
+    ctx.tensor(fn.BUF_PARAMS).copy_(_cuda(blob))
+    ctx.tensor(fn.BUF_TABLE).copy_(_cuda(table))
+    ctx.tensor(fn.BUF_OCC_IN).copy_(_cuda(occ.view(np.int32)))
+    ctx.tensor(fn.BUF_OCC_ST).copy_(_cuda(occ.view(np.int32)))
+    rays = rays_toward_box(n_rays, seed, radius=2.0, n_miss=0)
+    return g, ctx, blob, table, occ, rays, targets(n_rays, seed)
+
+
+@pytest.mark.parametrize("prec", ["fp32", "fp16"])
+def test_immediate_one_step(oracle, prec):
+    g, ctx, blob, table, occ, rays, tg = _make(prec, 21, 128)
+    n, lr_f, seed = rays.shape[0], np.float32(1e-2), 4242
+    cfg = make_orc_config(g, table_mode=1)
+    tab_o = table.copy()
+    out_o = np.zeros((n, 4), np.float32)
+    mgo = np.zeros(blob.size, np.float32)
+    oracle.forward_backward(cfg, OrcStep(lr_f, 1.0, 0.0, seed, 1, 0), blob, tab_o, occ.copy(), occ.copy(), rays, tg,
+                            out_o, None, mgo)
+    assert not np.array_equal(tab_o, table)
+    dout = torch.zeros((n, 4), device="cuda")
+    ctx.forward_backward(_cuda(rays), _cuda(tg), dout, n, fn.make_step(lr_f=lr_f, rng_u32=seed, table_immediate=True))
+    torch.cuda.synchronize()
+    tab_g = ctx.tensor(fn.BUF_TABLE).cpu().numpy()
+    assert rel_l2(tab_g - table, tab_o - table) < TOL[prec][0], rel_l2(tab_g - table, tab_o - table)
+    grads = ctx.tensor(fn.BUF_GRADS).cpu().numpy()
+    assert not grads[:table.size].any()
+    assert rel_l2(grads[table.size:], mgo) < MLP_GRAD_TOL[prec]
+    assert np.abs(dout.cpu().numpy()[:, :3] - out_o[:, :3]).max() < 1e-3
+    assert ctx.status() == 0
+
+
+@pytest.mark.parametrize("prec", ["fp32", "fp16"])
+def test_immediate_training_100_steps(oracle, prec):
+    n, steps = 128, 100
+    g, ctx, blob, table, occ, rays_all, tg_all = _make(prec, 11, n * steps)
+    cfg = make_orc_config(g, table_mode=1)
+    b1, b2 = np.float32(0.9), np.float32(0.999)
+    p, m, v, tab, oi, os_ = blob.copy(), np.zeros_like(blob), np.zeros_like(blob), table.copy(), occ.copy(), occ.copy()
+    lo, lg = [], []
+    for step in range(1, steps + 1):
+        rays, tg = rays_all[(step - 1) * n: step * n], tg_all[(step - 1) * n: step * n]
+        lr_f = np.float32(5e-3)
+        lr_t = np.float32(lr_f * np.sqrt(1.0 - b2 ** np.float32(step)) / (1.0 - b1 ** np.float32(step)))
+        seed = (step * 2654435761) & 0xFFFFFFFF
+        mgo = np.zeros(blob.size, np.float32)
+        out_o = np.zeros((n, 4), np.float32)
+        oracle.forward_backward(cfg, OrcStep(lr_f, 1.0, 0.0, seed, 1, 0), p, tab, oi, os_, rays, tg, out_o, None, mgo)
+        oracle.mlp_adam(cfg, p, mgo, m, v, lr_t, 0.5, b1, b2, np.float32(1e-6))
+        dout = torch.zeros((n, 4), device="cuda")
+        before = ctx.launches
+        ctx.train_step(_cuda(rays), _cuda(tg), dout, n,
+                       fn.make_step(lr_f=lr_f, lr_t=lr_t, color_rel_lr=0.5, rng_u32=seed, table_immediate=True))
+        assert ctx.launches - before == 3
+        lo.append(float(np.mean((out_o[:, :3] - tg[:, :3]) ** 2)))
+        lg.append(float(np.mean((dout.cpu().numpy()[:, :3] - tg[:, :3]) ** 2)))
+    lo, lg = np.array(lo), np.array(lg)
+    assert np.all(np.abs(lg - lo) <= 1e-3 * lo), (np.abs(lg - lo) / lo).max()
+    tol = TOL[prec][1]
+    p_g, tab_g = ctx.tensor(fn.BUF_PARAMS).cpu().numpy(), ctx.tensor(fn.BUF_TABLE).cpu().numpy()
+    assert rel_l2(p_g - blob, p - blob) < tol, rel_l2(p_g - blob, p - blob)
+    assert rel_l2(tab_g - table, tab - table) < tol, rel_l2(tab_g - table, tab - table)
+    assert ctx.status() == 0
+
+
+def test_immediate_needs_sgd_table():
+    g = make_geometry(**GEOM)
+    ctx = fn.Context(g, table_optimizer=1)   # Adam
+    rays = _cuda(rays_toward_box(8, 0))
+    with pytest.raises(ValueError):
+        ctx.forward_backward(rays, _cuda(targets(8, 0)), torch.zeros((8, 4), device="cuda"), 8,
+                             fn.make_step(lr_f=1e-3, table_immediate=True))
