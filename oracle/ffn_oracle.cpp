@@ -858,24 +858,33 @@ extern "C" int32_t orc_forward_backward(const orc_config* c, const orc_step* st,
         const int B = (int)stage.size();
         const int TK = c->tilek > 0 ? c->tilek : 236;
         std::memset(mlp_grad, 0, sizeof(float) * (size_t)lo.total);
+        // Per weight (oo, ii): acc over each TILEK chunk of samples in sample order, chunk sums
+        // added in chunk order; per bias: one running sum in sample order.  All weights of a layer
+        // advance together so each staged sample is read once per layer (same sums, same order).
+        std::vector<float> tot, acc, bacc;
         auto layer = [&](int wi, int bi, int OUT, int IN, auto dsel, auto asel) {
             float* gW = mlp_grad + lo.off[wi];
             float* gb = mlp_grad + lo.off[bi];
-            for (int oo = 0; oo < OUT; ++oo) {
-                for (int ii = 0; ii < IN; ++ii) {
-                    float tot = 0.0f;
-                    for (int kb = 0; kb < B; kb += TK) {
-                        float acc = 0.0f;
-                        int ke = std::min(B, kb + TK);
-                        for (int k = kb; k < ke; ++k) acc += dsel(stage[k])[oo] * asel(stage[k])[ii];
-                        tot += acc;
+            tot.assign((size_t)OUT * IN, 0.0f);
+            acc.resize((size_t)OUT * IN);
+            bacc.assign((size_t)OUT, 0.0f);
+            for (int kb = 0; kb < B; kb += TK) {
+                std::fill(acc.begin(), acc.end(), 0.0f);
+                const int ke = std::min(B, kb + TK);
+                for (int k = kb; k < ke; ++k) {
+                    const float* d = dsel(stage[k]);
+                    const float* a = asel(stage[k]);
+                    for (int oo = 0; oo < OUT; ++oo) {
+                        float* row = acc.data() + (size_t)oo * IN;
+                        const float dv = d[oo];
+                        for (int ii = 0; ii < IN; ++ii) row[ii] += dv * a[ii];
+                        bacc[oo] += dv;
                     }
-                    gW[oo * IN + ii] = tot;
                 }
-                float bacc = 0.0f;
-                for (int k = 0; k < B; ++k) bacc += dsel(stage[k])[oo];
-                gb[oo] = bacc;
+                for (size_t i = 0; i < tot.size(); ++i) tot[i] += acc[i];
             }
+            for (size_t i = 0; i < tot.size(); ++i) gW[i] = tot[i];
+            for (int oo = 0; oo < OUT; ++oo) gb[oo] = bacc[oo];
         };
         const int LP = LPOS;
         // color head and hidden layers (weight_update.cl:487-533)

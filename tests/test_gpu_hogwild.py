@@ -6,10 +6,8 @@ same step read it (ffnerf_OG.cl:2155-2168) -- against the CPU oracle in sequenti
 Contracts:
   * one step: the table change matches the oracle's within rel-L2 1e-3 (fp32 MLP) / 5e-2 (fp16
     tensor-core MLP), the gradient buffer's table part stays zero;
-  * 100 training steps: per-step loss within 1e-3 relative, parameters and table within rel-L2
-    1e-2 of the oracle (fp32 MLP); the fp16 path keeps the loss within 1e-3 and the updates
-    within rel-L2 5e-2;
-  * ffn_train_step launches one kernel fewer (no table pass).
+  * an Adam table refuses immediate updates.
+(100-step training runs in this mode are in test_gpu_train100.py.)
 """
 import numpy as np
 import pytest
@@ -23,7 +21,7 @@ from oracle import OrcStep, make_orc_config
 import ffn_native as fn
 
 GEOM = dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0)
-TOL = {"fp32": (1e-3, 1e-2), "fp16": (5e-2, 5e-2)}
+TOL = {"fp32": (1e-3,), "fp16": (5e-2,)}
 MLP_GRAD_TOL = {"fp32": 1e-3, "fp16": 5e-2}
 
 
@@ -63,39 +61,6 @@ def test_immediate_one_step(oracle, prec):
     assert not grads[:table.size].any()
     assert rel_l2(grads[table.size:], mgo) < MLP_GRAD_TOL[prec]
     assert np.abs(dout.cpu().numpy()[:, :3] - out_o[:, :3]).max() < 1e-3
-    assert ctx.status() == 0
-
-
-@pytest.mark.parametrize("prec", ["fp32", "fp16"])
-def test_immediate_training_100_steps(oracle, prec):
-    n, steps = 128, 100
-    g, ctx, blob, table, occ, rays_all, tg_all = _make(prec, 11, n * steps)
-    cfg = make_orc_config(g, table_mode=1)
-    b1, b2 = np.float32(0.9), np.float32(0.999)
-    p, m, v, tab, oi, os_ = blob.copy(), np.zeros_like(blob), np.zeros_like(blob), table.copy(), occ.copy(), occ.copy()
-    lo, lg = [], []
-    for step in range(1, steps + 1):
-        rays, tg = rays_all[(step - 1) * n: step * n], tg_all[(step - 1) * n: step * n]
-        lr_f = np.float32(5e-3)
-        lr_t = np.float32(lr_f * np.sqrt(1.0 - b2 ** np.float32(step)) / (1.0 - b1 ** np.float32(step)))
-        seed = (step * 2654435761) & 0xFFFFFFFF
-        mgo = np.zeros(blob.size, np.float32)
-        out_o = np.zeros((n, 4), np.float32)
-        oracle.forward_backward(cfg, OrcStep(lr_f, 1.0, 0.0, seed, 1, 0), p, tab, oi, os_, rays, tg, out_o, None, mgo)
-        oracle.mlp_adam(cfg, p, mgo, m, v, lr_t, 0.5, b1, b2, np.float32(1e-6))
-        dout = torch.zeros((n, 4), device="cuda")
-        before = ctx.launches
-        ctx.train_step(_cuda(rays), _cuda(tg), dout, n,
-                       fn.make_step(lr_f=lr_f, lr_t=lr_t, color_rel_lr=0.5, rng_u32=seed, table_immediate=True))
-        assert ctx.launches - before == 3
-        lo.append(float(np.mean((out_o[:, :3] - tg[:, :3]) ** 2)))
-        lg.append(float(np.mean((dout.cpu().numpy()[:, :3] - tg[:, :3]) ** 2)))
-    lo, lg = np.array(lo), np.array(lg)
-    assert np.all(np.abs(lg - lo) <= 1e-3 * lo), (np.abs(lg - lo) / lo).max()
-    tol = TOL[prec][1]
-    p_g, tab_g = ctx.tensor(fn.BUF_PARAMS).cpu().numpy(), ctx.tensor(fn.BUF_TABLE).cpu().numpy()
-    assert rel_l2(p_g - blob, p - blob) < tol, rel_l2(p_g - blob, p - blob)
-    assert rel_l2(tab_g - table, tab - table) < tol, rel_l2(tab_g - table, tab - table)
     assert ctx.status() == 0
 
 
