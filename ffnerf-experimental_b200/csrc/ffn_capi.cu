@@ -459,3 +459,5 @@ int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t
 }
 
 }  // extern "C"
+
+#include "ffn_noalloc.cu"

@@ -66,6 +66,7 @@ _SIGS = {
     "ffn_hash_encode_bwd": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_adam": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_float, _VP]),
     "ffn_status": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
+    "ffn_forward_backward_noalloc": (C.c_int, [C.POINTER(FfnConfig)] + [_VP] * 9 + [C.c_uint32, C.POINTER(FfnStep), _VP]),
 }
 EXPORTED = tuple(_SIGS)
 

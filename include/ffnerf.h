@@ -162,6 +162,32 @@ int ffn_status(ffn_ctx* ctx, uint32_t* status);
 int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float beta1,
              float beta2, float eps, void* stream);
 
+/* ffn_forward_backward for callers that cannot allocate device memory.  No reference
+ * counterpart: the reference allocates its buffers through PyOpenCL.  It serves code that runs
+ * inside another runtime's device-memory budget (an engine or serving process that owns every
+ * allocation through its own pool), where the library may not call cudaMalloc: such a caller
+ * holds the model's buffers itself and passes them in, with no ffn_ctx.
+ *
+ * Inputs: cfg (as for ffn_create), params (FFN_BUF_PARAMS layout), occ_in, rays, targets; in/out:
+ * table (read; also updated when s->flags has FFN_STEP_TABLE_IMMEDIATE), occ_st (occupancy
+ * proposals when s->occ_strength > 0); outputs: out [n][4], grads (FFN_BUF_GRADS layout,
+ * table_entries*F + params floats, overwritten: cleared, then accumulated), status (device int,
+ * ffn_status bits; may be NULL).  The device is the caller's current device.
+ *
+ * Allocates nothing: no cudaMalloc, cudaFree or allocating library call.  The per-CTA
+ * weight-gradient partial sums live in a static device array of FFN_NOALLOC_SCRATCH_BYTES that
+ * every GPU which loads the library holds until the process exits; a call whose partials
+ * (CTAs x params floats, plus 256 bytes) exceed it fails with FFN_E_CAPACITY.  The first call on
+ * each device also resolves that array's address and sets the kernels' shared-memory limits;
+ * make that first call before any stream capture.  All calls on a device share the array, so
+ * calls that overlap on the GPU (other streams, other threads) race and must be serialised by
+ * the caller. */
+#define FFN_NOALLOC_SCRATCH_BYTES (24u << 20)
+int ffn_forward_backward_noalloc(const ffn_config* cfg, const float* params, float* table,
+                                 const uint32_t* occ_in, uint32_t* occ_st, const void* rays,
+                                 const void* targets, void* out, float* grads, int* status,
+                                 uint32_t n_rays, const ffn_step_scalars* s, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
