@@ -44,6 +44,7 @@ class FfnStep(C.Structure):
 
 
 STEP_TABLE_IMMEDIATE = 1
+ABI_VERSION = 2          # include/ffnerf.h FFN_ABI_VERSION
 
 
 _VP = C.c_void_p
@@ -87,6 +88,9 @@ def load_library(path: Path | None = None):
         f = getattr(lib, name)
         f.restype = res
         f.argtypes = args
+    if lib.ffn_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"{p} has ABI version {lib.ffn_abi_version()}, this module expects {ABI_VERSION}: "
+                           "rebuild it (python build_native.py)")
     if path is None:
         _lib = lib
     return lib

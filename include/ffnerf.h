@@ -38,7 +38,7 @@ extern "C" {
 #endif
 
 #define FFN_N_LEVELS 16
-#define FFN_ABI_VERSION 1
+#define FFN_ABI_VERSION 2   /* 2: ffn_step_scalars.flags */
 
 enum {
     FFN_OK = 0,

@@ -21,7 +21,7 @@ def test_header_symbols_exported():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared but not exported"
     assert declared == set(fn.EXPORTED), declared ^ set(fn.EXPORTED)
-    assert lib.ffn_abi_version() == 1
+    assert lib.ffn_abi_version() == fn.ABI_VERSION
 
 
 def test_param_layout_matches_oracle(oracle):
