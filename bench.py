@@ -54,6 +54,175 @@ WORKLOADS = {
                  maint=32, desc="cfg1: 512 rays x 64 samples; hash L=16 F=2 T=2^14, Rmax 512; occupancy 64^3; "
                                 "8 cameras at 64x64"),
 }
+# Kernel microbenchmarks (BASELINE configs 4 and 5): one JSON line each, own metric.
+MICRO = {
+    "cfg4": dict(kind="hash", points=1 << 22, F=2, log2T=19, rmax=2048.0,
+                 desc="cfg4: hash encode fwd+bwd, 2^22 points U[0,1]^3, L=16 F=2 T=2^19 fp32 table, "
+                      "upstream grads N(0,1) [2^22, 32] fp32"),
+    "cfg4-T22": dict(kind="hash", points=1 << 22, F=2, log2T=22, rmax=2048.0,
+                     desc="cfg4: hash encode fwd+bwd, 2^22 points U[0,1]^3, L=16 F=2 T=2^22 fp32 table, "
+                          "upstream grads N(0,1) [2^22, 32] fp32"),
+    "cfg5-adam": dict(kind="adam", n=1 << 24, desc="cfg5: Adam over 2^24 fp32 parameters, grads N(0,1e-3), "
+                                                    "beta1 0.9 beta2 0.99 eps 1e-15 lr 1e-2"),
+}
+
+
+def hash_bytes_per_point(F: int):
+    """Algorithmic bytes per point: forward = xyz + 16 levels x 8 corners x F x 4 B gathered + 16 F x 4 B
+    written; backward = xyz + 16 F x 4 B upstream + 16 x 8 x F x 4 B atomic read-modify-write."""
+    gather = 16 * 8 * F * 4
+    return 12 + gather + 16 * F * 4, 12 + 16 * F * 4 + 2 * gather
+
+
+def run_micro(args, name: str) -> dict:
+    import torch
+    import ffn_native as fn
+    from ffn_config import make_geometry
+    wl = MICRO[name]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    st = torch.cuda.Stream()
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    hbm, _, peak_kind = peaks()
+
+    def timed(fns, flush=True):
+        """Per-iteration CUDA events on stream st around each callable; L2 flushed before each."""
+        sums = [0.0] * len(fns)
+        for _ in range(args.steps):
+            with torch.cuda.stream(st):
+                if flush:
+                    flush_buf.zero_()
+                for k, f in enumerate(fns):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record(st)
+                    f()
+                    b.record(st)
+                    torch.cuda.synchronize()
+                    sums[k] += a.elapsed_time(b)
+        return sums
+
+    if wl["kind"] == "hash":
+        g = make_geometry(F=wl["F"], ND=1, NC=2, spr=64, G=16, log2_entries=wl["log2T"], rmax=wl["rmax"])
+        ctx = fn.Context(g, device=0)
+        n = wl["points"]
+        ctx.tensor(fn.BUF_TABLE).uniform_(-1e-4, 1e-4, generator=gen)
+        pts = torch.rand((n, 3), device=dev, generator=gen)
+        enc = torch.empty((n, 16 * wl["F"]), device=dev)
+        denc = torch.randn((n, 16 * wl["F"]), device=dev, generator=gen)
+        fwd = lambda: ctx.hash_encode(pts, enc, n, stream=st)            # noqa: E731
+        bwd = lambda: ctx.hash_encode_bwd(pts, denc, n, stream=st)       # noqa: E731
+        for _ in range(args.warmup):
+            with torch.cuda.stream(st):
+                fwd(); bwd()
+        torch.cuda.synchronize()
+        with ClockSampler(0) as clk:
+            t_fwd, t_bwd = timed([fwd, bwd])
+            # end to end: pinned-host points and upstream grads in, encoding out, every iteration
+            h_pts = pts.cpu().pin_memory()
+            h_denc = denc.cpu().pin_memory()
+            h_enc = torch.empty(enc.shape, dtype=enc.dtype).pin_memory()
+
+            def e2e():
+                pts.copy_(h_pts, non_blocking=True)
+                denc.copy_(h_denc, non_blocking=True)
+                fwd(); bwd()
+                h_enc.copy_(enc, non_blocking=True)
+            (t_e2e,) = timed([e2e])
+        bf, bb = hash_bytes_per_point(wl["F"])
+        gbs_f = bf * n / (t_fwd / args.steps * 1e-3) / 1e9
+        gbs_b = bb * n / (t_bwd / args.steps * 1e-3) / 1e9
+        gbs = (bf + bb) * n / ((t_fwd + t_bwd) / args.steps * 1e-3) / 1e9
+        e2e_gbs = (bf + bb) * n / (t_e2e / args.steps * 1e-3) / 1e9
+        # CPU: the oracle's hash encode / scatter on a bounded sample (one thread)
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as orc
+        o = orc.Oracle()
+        m = 1 << 15
+        table_h = ctx.tensor(fn.BUF_TABLE).cpu().numpy()
+        p_h, d_h = pts[:m].cpu().numpy(), denc[:m].cpu().numpy()
+        e_h, tg_h = np.zeros((m, 16 * wl["F"]), np.float32), np.zeros_like(table_h)
+        cfg = orc.make_orc_config(g)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 10.0:
+            o.hash_fwd(cfg, table_h, p_h, e_h)
+            o.hash_bwd(cfg, p_h, d_h, tg_h)
+            reps += 1
+        cpu_gbs = (bf + bb) * m * reps / (time.perf_counter() - t0) / 1e9
+        ctx.close()
+        line = {
+            "metric": "hash-grid GB/s (encode fwd+bwd, algorithmic bytes)", "value": gbs, "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": (t_fwd + t_bwd) / args.steps, "higher_is_better": True, "scaling": "none",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl["desc"], "points": n, "l2": "flushed between iterations (256 MB write)",
+                       "table_bytes": g["table_entries"] * wl["F"] * 4},
+            "fwd": {"ms": t_fwd / args.steps, "GB/s": gbs_f, "points/s": n / (t_fwd / args.steps * 1e-3),
+                    "bytes_per_point": bf},
+            "bwd": {"ms": t_bwd / args.steps, "GB/s": gbs_b, "points/s": n / (t_bwd / args.steps * 1e-3),
+                    "bytes_per_point": bb},
+            "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": n * (12 + 16 * wl["F"] * 4),
+                    "d2h_bytes_per_step": n * 16 * wl["F"] * 4},
+            "gpu_launches": args.steps * 2,
+            "roofline": {"bound": "hbm" if g["table_entries"] * wl["F"] * 4 > 100e6 else "l2",
+                         "kernel": "hash_fwd_kernel + hash_bwd_kernel", "achieved": gbs, "peak": hbm,
+                         "unit": "GB/s", "frac": gbs / hbm, "traffic": None, "peak_source": peak_kind,
+                         "note": "peak = measured HBM copy bandwidth; random 8 B gathers move 32 B sectors"},
+            "clocks": clk.summary(),
+            "cpu_baseline": {"value": cpu_gbs, "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": f"{m} points fwd+bwd, oracle restatement, repeated for 10 s"},
+        }
+        return line
+    # Adam
+    n = wl["n"]
+    p = torch.randn(n, device=dev, generator=gen)
+    gr = torch.randn(n, device=dev, generator=gen) * 1e-3
+    m_ = torch.zeros(n, device=dev)
+    v_ = torch.zeros(n, device=dev)
+    step = lambda: fn.adam(p, gr, m_, v_, n, 1e-2, 0.9, 0.99, 1e-15, stream=st)   # noqa: E731
+    for _ in range(args.warmup):
+        with torch.cuda.stream(st):
+            step()
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        (t,) = timed([step], flush=False)
+        h_g = gr.cpu().pin_memory()
+        h_p = torch.empty(n).pin_memory()
+
+        def e2e():
+            gr.copy_(h_g, non_blocking=True)
+            step()
+            h_p.copy_(p, non_blocking=True)
+        (t_e2e,) = timed([e2e], flush=False)
+    gbs = 28 * n / (t / args.steps * 1e-3) / 1e9
+    # CPU: numpy Adam on a bounded slice (same update, vectorised, one thread)
+    mm = 1 << 22
+    ph, gh = p[:mm].cpu().numpy(), gr[:mm].cpu().numpy()
+    mh, vh = np.zeros(mm, np.float32), np.zeros(mm, np.float32)
+    t0 = time.perf_counter()
+    reps = 0
+    while time.perf_counter() - t0 < 5.0:
+        mh = 0.9 * mh + 0.1 * gh
+        vh = 0.99 * vh + 0.01 * gh * gh
+        ph -= 1e-2 * mh / (np.sqrt(vh) + 1e-15)
+        reps += 1
+    cpu_gbs = 28 * mm * reps / (time.perf_counter() - t0) / 1e9
+    return {
+        "metric": "Adam GB/s (28 B per parameter)", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps, "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl["desc"], "params": n, "l2": "working set 470 MB exceeds L2; no flush"},
+        "e2e": {"value": 28 * n / (t_e2e / args.steps * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * n,
+                "d2h_bytes_per_step": 4 * n},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "kernel": "adam_kernel", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "traffic": None, "peak_source": peak_kind},
+        "clocks": clk.summary(),
+        "cpu_baseline": {"value": cpu_gbs, "unit": "GB/s", "cores": 1, "kind": "port",
+                         "sample": f"numpy Adam over {mm} parameters, repeated for 5 s"},
+    }
 # Algorithmic bytes per sample of the fused forward/backward kernel (F=2): trilinear gather
 # 16 levels x 8 corners x F x 4 B, atomic scatter read+write of the same, ray/target/colour I/O
 # (64 B per ray / spr) and one occupancy word per sample.
@@ -199,7 +368,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(MICRO), default="cfg3")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end loop (profiling runs)")
@@ -209,6 +378,14 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload in MICRO:
+        if int(os.environ.get("RANK", "0")) == 0:
+            if args.impl == "reference":
+                print(json.dumps({"impl": "reference", "unavailable": "kernel microbenchmark: the reference has no "
+                                  "standalone kernel for it; the CPU figure is in this arm's cpu_baseline"}), flush=True)
+            else:
+                print(json.dumps(run_micro(args, args.workload)), flush=True)
+        return
     wl = dict(WORKLOADS[args.workload])
     if args.rays:
         wl["rays"] = int(args.rays)

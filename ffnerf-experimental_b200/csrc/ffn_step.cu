@@ -560,24 +560,81 @@ __global__ void occ_bytes_kernel(uint32_t* __restrict__ grid, uint8_t* __restric
     }
 }
 
+// One thread per (point, level), level fastest: a warp covers 32/16 = 2 points, so the point
+// reads are broadcasts and the feature rows [n][16 F] are written / read as contiguous 8 F-byte
+// pieces by consecutive lanes.  Each thread does its level's 8 corner gathers (or atomic adds).
 template <int F>
-__global__ void hash_fwd_kernel(const DevConfig c, const float* __restrict__ table, const float* __restrict__ pts,
-                                int64_t n, float* __restrict__ enc) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+__global__ void __launch_bounds__(256) hash_fwd_kernel(const DevConfig c, const float* __restrict__ table,
+                                                       const float* __restrict__ pts, int64_t n,
+                                                       float* __restrict__ enc) {
+    const int64_t total = n * L;
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < total; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = j >> 4;
+        const int lvl = (int)(j & (L - 1));
         const float hi = 1.0f - 1.0e-6f;
         const V3 p = v3(fclamp(pts[3 * i], 0.f, hi), fclamp(pts[3 * i + 1], 0.f, hi), fclamp(pts[3 * i + 2], 0.f, hi));
-        encode<F>(c, table, p, enc + i * (L * F));
+        Corner8 k;
+        level_corners<F>(c, p, lvl, k);
+        float acc[F];
+#pragma unroll
+        for (int f = 0; f < F; ++f) acc[f] = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            if constexpr (F == 2) {
+                const float2 t = table_ld2<false>(table + k.base[cc]);
+                acc[0] = fmaf(k.w[cc], t.x, acc[0]);
+                acc[1] = fmaf(k.w[cc], t.y, acc[1]);
+            } else {
+                const float4 t = table_ld4<false>(table + k.base[cc]);
+                acc[0] = fmaf(k.w[cc], t.x, acc[0]);
+                acc[1] = fmaf(k.w[cc], t.y, acc[1]);
+                acc[2] = fmaf(k.w[cc], t.z, acc[2]);
+                acc[3] = fmaf(k.w[cc], t.w, acc[3]);
+            }
+        }
+        float* dst = enc + i * (L * F) + lvl * F;
+        if constexpr (F == 2) __stcs(reinterpret_cast<float2*>(dst), make_float2(acc[0], acc[1]));
+        else __stcs(reinterpret_cast<float4*>(dst), make_float4(acc[0], acc[1], acc[2], acc[3]));
     }
 }
 
 template <int F>
-__global__ void hash_bwd_kernel(const DevConfig c, float* __restrict__ grad, const float* __restrict__ pts,
-                                const float* __restrict__ denc, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+__global__ void __launch_bounds__(256) hash_bwd_kernel(const DevConfig c, float* __restrict__ grad,
+                                                       const float* __restrict__ pts,
+                                                       const float* __restrict__ denc, int64_t n) {
+    const int64_t total = n * L;
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < total; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = j >> 4;
+        const int lvl = (int)(j & (L - 1));
+        const float* g = denc + i * (L * F) + lvl * F;
+        float gf[F];
+        bool any = false;
+        if constexpr (F == 2) {
+            const float2 t = __ldcs(reinterpret_cast<const float2*>(g));
+            gf[0] = t.x; gf[1] = t.y;
+        } else {
+            const float4 t = __ldcs(reinterpret_cast<const float4*>(g));
+            gf[0] = t.x; gf[1] = t.y; gf[2] = t.z; gf[3] = t.w;
+        }
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+            gf[f] = isfinite(gf[f]) ? gf[f] : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
+            any |= gf[f] != 0.0f;
+        }
+        if (!any) continue;
         const float hi = 1.0f - 1.0e-6f;
         const V3 p = v3(fclamp(pts[3 * i], 0.f, hi), fclamp(pts[3 * i + 1], 0.f, hi), fclamp(pts[3 * i + 2], 0.f, hi));
-        const float one[L] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
-        scatter_grad<F>(c, grad, p, denc + i * (L * F), one);
+        Corner8 k;
+        level_corners<F>(c, p, lvl, k);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const float w = k.w[cc];
+            if constexpr (F == 2)
+                atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
+            else
+                atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
+                          make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+        }
     }
 }
 
