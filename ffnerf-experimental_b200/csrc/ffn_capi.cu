@@ -37,12 +37,22 @@ struct ffn_ctx {
     int ctas_per_sm = 1;
     size_t smem = 0;
     void (*kernel)(StepArgs) = nullptr;
+    // split tensor-core step (mlp_precision = 1): stage kernels and their buffers, sized for
+    // STAGE_SAMPLES samples per launch group
+    void (*kernel_staged)(StepArgs) = nullptr;
+    void (*encoder)(DevConfig, const float*, const float4*, int64_t, int64_t, unsigned char*) = nullptr;
+    unsigned char* x0_stage = nullptr;
+    float2* tdt_stage = nullptr;
+    float4* pn_stage = nullptr;
+    uint4* ray_stage = nullptr;
     std::string err;
 };
 
 namespace {
 
 thread_local std::string g_create_err;
+
+constexpr int64_t STAGE_SAMPLES = 1 << 20;   // samples per group of the split tensor-core step
 
 int fail(ffn_ctx* ctx, int code, const std::string& msg) {
     if (ctx) ctx->err = msg; else g_create_err = msg;
@@ -66,13 +76,13 @@ struct DeviceGuard {
     }
 };
 
-int g_sms = 0;
-
 template <int F, int ND, int NC, int ROWS>
 void bind_kernel(ffn_ctx* c) {
     if (c->cfg.mlp_precision == 1) {
         using PL = TcPlan<F, ND>;
         c->kernel = fused_step_tc_kernel<F, ND>;
+        c->kernel_staged = fused_step_tc_kernel<F, ND, true>;
+        c->encoder = encode_stage_kernel<F>;
         c->rows = PL::ROWS;
         c->smem = PL::BYTES;
         c->ctas_per_sm = PL::CTAS_PER_SM;
@@ -177,6 +187,39 @@ int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The split tensor-core step over groups of at most STAGE_SAMPLES samples: sampler, encoder,
+// then the MLP/compositing/backward kernel and the fixed-order partial reduction per group.
+int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
+                            const ffn_step_scalars* s, cudaStream_t st) {
+    const int spr = s->spr ? (int)s->spr : c->cfg.spr;
+    const uint32_t group_rays = (uint32_t)(STAGE_SAMPLES / spr);
+    const int rpt = 128 / spr;
+    const int sms = c->max_grid / c->ctas_per_sm;
+    for (uint32_t r0 = 0; r0 < n; r0 += group_rays) {
+        const uint32_t m = n - r0 < group_rays ? n - r0 : group_rays;
+        StepArgs a = base_args(c, static_cast<const float4*>(rays) + 2 * (size_t)r0,
+                               static_cast<const float4*>(targets) + r0, static_cast<float4*>(out) + r0, m, s);
+        a.ray_offset = s->ray_offset + r0;
+        a.do_train = 1;
+        const int n_tiles = (int)((m + (uint32_t)rpt - 1) / (uint32_t)rpt);
+        const int sgrid = n_tiles < sms * 8 ? n_tiles : sms * 8;
+        sample_stage_kernel<<<sgrid, 128, 0, st>>>(a, c->pn_stage, c->tdt_stage, c->ray_stage);
+        const int64_t rows = (int64_t)n_tiles * 128;
+        const int64_t items = rows * L;
+        const int eblocks = (int)((items + 255) / 256 < (int64_t)sms * 16 ? (items + 255) / 256 : (int64_t)sms * 16);
+        c->encoder<<<eblocks, 256, 0, st>>>(a.c, c->table, c->pn_stage, (int64_t)m * spr, rows, c->x0_stage);
+        a.x0_stage = c->x0_stage;
+        a.tdt_stage = c->tdt_stage;
+        a.ray_stage = c->ray_stage;
+        const int grid = n_tiles < c->max_grid ? n_tiles : c->max_grid;
+        c->kernel_staged<<<grid, c->rows, c->smem, st>>>(a);
+        reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(c, e, "split step launch");
+    }
+    return FFN_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -227,7 +270,9 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
         delete c;
         return fail(nullptr, FFN_E_CONFIG, "configuration needs more shared memory than the device offers");
     }
-    if ((e = cudaFuncSetAttribute(c->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->smem)) != cudaSuccess) {
+    if ((e = cudaFuncSetAttribute(c->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->smem)) != cudaSuccess ||
+        (c->kernel_staged &&
+         (e = cudaFuncSetAttribute(c->kernel_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->smem)) != cudaSuccess)) {
         delete c;
         return cuda_fail(nullptr, e, "shared-memory attribute");
     }
@@ -243,6 +288,15 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
     for (auto& al : allocs) {
         if ((e = cudaMalloc(al.p, al.n)) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "device allocation"); }
         cudaMemset(*al.p, 0, al.n);
+    }
+    if (c->kernel_staged) {
+        struct { void** p; size_t n; } st_allocs[] = {
+            {(void**)&c->x0_stage, (size_t)STAGE_SAMPLES * 16 * cfg->F * 2},
+            {(void**)&c->tdt_stage, (size_t)STAGE_SAMPLES * sizeof(float2)},
+            {(void**)&c->pn_stage, (size_t)STAGE_SAMPLES * sizeof(float4)},
+            {(void**)&c->ray_stage, (size_t)(STAGE_SAMPLES / 16) * sizeof(uint4)}};
+        for (auto& al : st_allocs)
+            if ((e = cudaMalloc(al.p, al.n)) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "device allocation"); }
     }
     if (cfg->table_optimizer == 1) {
         if ((e = cudaMalloc((void**)&c->table_m, Tb)) != cudaSuccess || (e = cudaMalloc((void**)&c->table_v, Tb)) != cudaSuccess) {
@@ -262,7 +316,8 @@ int ffn_destroy(ffn_ctx* c) {
     DeviceGuard guard(c->device);
     cudaDeviceSynchronize();
     void* ptrs[] = {c->params, c->adam_m, c->adam_v, c->table, c->table_m, c->table_v, c->occ_in,
-                    c->occ_st, c->grads, c->partials, c->status};
+                    c->occ_st, c->grads, c->partials, c->status, c->x0_stage, c->tdt_stage, c->pn_stage,
+                    c->ray_stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -316,6 +371,7 @@ int ffn_forward_backward(ffn_ctx* c, const void* rays, const void* targets, void
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if ((s->flags & FFN_STEP_TABLE_IMMEDIATE) && c->cfg.table_optimizer != 0)
         return fail(c, FFN_E_CONFIG, "immediate table updates need the SGD table optimizer");
+    if (c->kernel_staged) return forward_backward_staged(c, rays, targets, out, n, s, st);
     StepArgs a = base_args(c, rays, targets, out, n, s);
     a.do_train = 1;
     int grid = 0;

@@ -31,6 +31,11 @@ struct StepArgs {
     int do_train;
     int* status;               // device status word (ST_* bits), may be null
     int probe;                 // ffn_probe: forward with training rules, no backward
+    // split tensor-core step: sampling and encoding staged by sample_stage_kernel and
+    // encode_stage_kernel (null when the fused kernel samples and encodes itself)
+    const unsigned char* x0_stage;   // [tiles][128 x 16F fp16 operand tile]
+    const float2* tdt_stage;         // [n_rays * spr]: sample time, step
+    const uint4* ray_stage;          // [n_rays]: run-start bits (2 words), hit
     // diagnostics (ffn_probe); all optional
     const float4* bypass;
     float* dbg_t; float* dbg_dt; int* dbg_idx; uint32_t* dbg_flags;

@@ -233,7 +233,7 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
     }
 }
 
-template <int F, int ND>
+template <int F, int ND, bool STAGED = false>
 __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a) {
     using PL = TcPlan<F, ND>;
     constexpr int LPOS = PL::LPOS;
@@ -348,8 +348,25 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         RayTile R{sCand, sCdf, sTs, sDTs, sTr, sKey, sSeg, sAffS, sAffE, sChg, sRay, tid, spr, rl, lid, rbase,
                   ray_idx, ray_id, valid, train, probe, o, d, bmin, bmax, bsize, inv_box, (float)c.G, 1.0f / (float)spr};
         bool hit;
-        int idx_sel;
-        ray_sampler(a, R, hit, idx_sel);
+        int idx_sel = 0;
+        if constexpr (STAGED) {
+            // sampling and encoding were done by the stage kernels: load their results
+            const size_t s = (size_t)tile * 128 + tid;
+            float2 tdt = make_float2(0.f, 0.f);
+            uint4 rst = make_uint4(0u, 0u, 0u, 0u);
+            if (valid) { tdt = a.tdt_stage[s]; rst = a.ray_stage[ray_idx]; }
+            sTs[tid] = tdt.x;
+            sDTs[tid] = tdt.y;
+            if (lid == 0) { sChg[rl * 2] = rst.x; sChg[rl * 2 + 1] = rst.y; }
+            hit = rst.z != 0u;
+            const uint4* src = reinterpret_cast<const uint4*>(a.x0_stage + (size_t)tile * (128 * LPOS * 2));
+            uint4* dst = reinterpret_cast<uint4*>(tX0);
+#pragma unroll
+            for (int k = tid; k < 128 * LPOS * 2 / 16; k += 128) dst[k] = __ldcs(src + k);
+            __syncthreads();
+        } else {
+            ray_sampler(a, R, hit, idx_sel);
+        }
         const float* rs = sRay + rl * 16;
         const float t_s = sTs[tid];
         const float dt_s = sDTs[tid];
@@ -363,7 +380,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             if (valid) b = a.bypass[(size_t)ray_idx * spr + lid];
             sigma = b.x; rgb[0] = b.y; rgb[1] = b.z; rgb[2] = b.w;
         } else {
-            encode_rows<F>(c, a.table, pn, hit, tX0);
+            if constexpr (!STAGED) encode_rows<F>(c, a.table, pn, hit, tX0);
             handoff();
             if (tid == 0) gemm(tmem + PL::ACC, S(PL::X0), LPOS, false, S(PL::W_DIN), LPOS, false, 128, 64, LPOS, 0);
             sync_mma();
@@ -588,6 +605,119 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) tc::tmem_dealloc(tmem, PL::TMEM_COLS);
+}
+
+
+// ---------------------------------------------------------------- split step: stage kernels
+// The tensor-core step as three launches: the sampler of every tile, the hash encoding of every
+// (sample, level) straight into the fp16 operand tiles, then fused_step_tc_kernel<..., true>, which
+// loads both and runs the MLPs, compositing, backward and scatter.  The first two carry no tensor
+// memory and little shared memory, so many more warps per SM keep the gathers in flight than the
+// fused kernel's two CTAs can.  Arithmetic is the fused kernel's, operation for operation.
+
+// Sampler of 128-sample tiles (ray_sampler unchanged); writes (t, dt) per sample, the normalised
+// position with a hit flag per sample, and (run-start bits, hit) per ray.
+__global__ void __launch_bounds__(128) sample_stage_kernel(const StepArgs a, float4* __restrict__ pn_out,
+                                                           float2* __restrict__ tdt_out, uint4* __restrict__ ray_out) {
+    constexpr int RAY_BYTES = 128 * 6 * 4 + 128 * 16 + 128 * 16 + 8 * 2 * 4 + 8 * 16 * 4;
+    __shared__ __align__(16) unsigned char sm[RAY_BYTES];
+    const DevConfig& c = a.c;
+    const int tid = threadIdx.x;
+    float* rayb = reinterpret_cast<float*>(sm);
+    float* sCand = rayb;
+    float* sCdf = sCand + 128;
+    float* sTs = sCdf + 128;
+    float* sDTs = sTs + 128;
+    float* sTr = sDTs + 128;
+    uint32_t* sKey = reinterpret_cast<uint32_t*>(sTr + 128);
+    float4* sSeg = reinterpret_cast<float4*>(sKey + 128);
+    float2* sAffS = reinterpret_cast<float2*>(sSeg + 128);
+    float2* sAffE = sAffS + 128;
+    uint32_t* sChg = reinterpret_cast<uint32_t*>(sAffE + 128);
+    float* sRay = reinterpret_cast<float*>(sChg + 16);
+    const V3 bmin = v3(c.bmin[0], c.bmin[1], c.bmin[2]);
+    const V3 bmax = v3(c.bmax[0], c.bmax[1], c.bmax[2]);
+    const V3 bsize = vsub(bmax, bmin);
+    const V3 inv_box = v3(fd(1.0f, bsize.x), fd(1.0f, bsize.y), fd(1.0f, bsize.z));
+    const int spr = c.spr;
+    const int rl = tid / spr, lid = tid - rl * spr, rbase = rl * spr;
+    const int rays_per_tile = 128 / spr;
+    const int n_tiles = (int)((a.n_rays + rays_per_tile - 1) / rays_per_tile);
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t ray_idx = (uint32_t)tile * rays_per_tile + rl;
+        const bool valid = ray_idx < a.n_rays;
+        const uint32_t ray_id = a.ray_offset + ray_idx;
+        float4 ro = make_float4(0.f, 0.f, 0.f, 0.f), rd = make_float4(0.f, 0.f, 1.f, 0.f);
+        if (valid) { ro = a.rays[2 * ray_idx]; rd = a.rays[2 * ray_idx + 1]; }
+        const V3 o = v3(ro.x, ro.y, ro.z), d = v3(rd.x, rd.y, rd.z);
+        RayTile R{sCand, sCdf, sTs, sDTs, sTr, sKey, sSeg, sAffS, sAffE, sChg, sRay, tid, spr, rl, lid, rbase,
+                  ray_idx, ray_id, valid, a.do_train != 0, false, o, d, bmin, bmax, bsize, inv_box, (float)c.G,
+                  1.0f / (float)spr};
+        bool hit;
+        int idx_sel;
+        ray_sampler(a, R, hit, idx_sel);
+        if (valid) {
+            const size_t s = (size_t)tile * 128 + tid;
+            const float t_s = sTs[tid];
+            tdt_out[s] = make_float2(t_s, sDTs[tid]);
+            const V3 pn = normalize_pos(c, ray_point(o, d, t_s));
+            pn_out[s] = make_float4(pn.x, pn.y, pn.z, hit ? 1.0f : 0.0f);
+            if (lid == 0) ray_out[ray_idx] = make_uint4(sChg[rl * 2], sChg[rl * 2 + 1], hit ? 1u : 0u, 0u);
+        }
+        __syncthreads();
+    }
+}
+
+// Hash encoding, one thread per (sample, level), level fastest, into the X0 operand tiles
+// (x INPUT_SCALE, fp16): the same accumulation order as encode_rows.  Rows of samples that are
+// not staged (past the last ray) or whose ray misses the box are zero.  The table is only read
+// during this launch.
+template <int F>
+__global__ void __launch_bounds__(256) encode_stage_kernel(const DevConfig c, const float* __restrict__ table,
+                                                           const float4* __restrict__ pn_in, int64_t n_valid,
+                                                           int64_t n_rows, unsigned char* __restrict__ x0_out) {
+    constexpr int LPOS = L * F;
+    const int64_t total = n_rows * L;
+    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < total; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = j >> 4;
+        const int lvl = (int)(j & (L - 1));
+        float v[F];
+#pragma unroll
+        for (int f = 0; f < F; ++f) v[f] = 0.0f;
+        if (i < n_valid) {
+            const float4 q = pn_in[i];
+            if (q.w != 0.0f) {
+                Corner8 k;
+                level_corners<F>(c, v3(q.x, q.y, q.z), lvl, k);
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    if constexpr (F == 2) {
+                        const float2 t = __ldg(reinterpret_cast<const float2*>(table + k.base[cc]));
+                        v[0] = fmaf(k.w[cc], t.x, v[0]);
+                        v[1] = fmaf(k.w[cc], t.y, v[1]);
+                    } else {
+                        const float4 t = __ldg(reinterpret_cast<const float4*>(table + k.base[cc]));
+                        v[0] = fmaf(k.w[cc], t.x, v[0]);
+                        v[1] = fmaf(k.w[cc], t.y, v[1]);
+                        v[2] = fmaf(k.w[cc], t.z, v[2]);
+                        v[3] = fmaf(k.w[cc], t.w, v[3]);
+                    }
+                }
+            }
+        }
+        unsigned char* tile = x0_out + (i >> 7) * (int64_t)(128 * LPOS * 2);
+        const int r = (int)(i & 127);
+        __half2 h0 = __halves2half2(tc::to_half_sat(v[0] * INPUT_SCALE), tc::to_half_sat(v[1] * INPUT_SCALE));
+        if constexpr (F == 2) {
+            *reinterpret_cast<__half2*>(tile + tc::tile_off(r, lvl * 2, LPOS)) = h0;
+        } else {
+            __half2 h1 = __halves2half2(tc::to_half_sat(v[2] * INPUT_SCALE), tc::to_half_sat(v[3] * INPUT_SCALE));
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&h0);
+            u.y = *reinterpret_cast<uint32_t*>(&h1);
+            *reinterpret_cast<uint2*>(tile + tc::tile_off(r, lvl * 4, LPOS)) = u;
+        }
+    }
 }
 
 }  // namespace ffn

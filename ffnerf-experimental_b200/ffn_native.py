@@ -44,6 +44,7 @@ class FfnStep(C.Structure):
 
 
 STEP_TABLE_IMMEDIATE = 1
+STAGE_SAMPLES = 1 << 20   # samples per group of the split tensor-core step (ffn_capi.cu)
 ABI_VERSION = 2          # include/ffnerf.h FFN_ABI_VERSION
 
 
@@ -217,10 +218,19 @@ class Context:
             return torch.cuda.current_stream().cuda_stream
         return getattr(stream, "cuda_stream", stream)
 
+    def _fb_launches(self, n_rays: int, step: FfnStep) -> int:
+        """Kernels one ffn_forward_backward launches: fused kernel + partial reduction (fp32 MLP), or
+        per group of 2^20 samples sampler + encoder + MLP kernel + reduction (tensor-core MLP)."""
+        if self.mlp_precision != "fp16" or n_rays == 0:
+            return 2 if n_rays else 0
+        spr = int(step.spr) or int(self.geom["spr"])
+        groups = -(-(int(n_rays) * spr) // STAGE_SAMPLES)
+        return 4 * groups
+
     def forward_backward(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_forward_backward(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                                   C.byref(step), self._stream(stream)), "ffn_forward_backward")
-        self.launches += 2
+        self.launches += self._fb_launches(n_rays, step)
 
     def apply_updates(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_apply_updates(self.h, C.byref(step), self._stream(stream)), "ffn_apply_updates")
@@ -229,7 +239,7 @@ class Context:
     def train_step(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_train_step(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                             C.byref(step), self._stream(stream)), "ffn_train_step")
-        self.launches += 3 if step.flags & STEP_TABLE_IMMEDIATE else 4
+        self.launches += self._fb_launches(n_rays, step) + (1 if step.flags & STEP_TABLE_IMMEDIATE else 2)
 
     def render(self, rays, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_render(self.h, _ptr(rays), _ptr(out), int(n_rays), C.byref(step),
