@@ -471,8 +471,9 @@ int ffn_hash_encode(ffn_ctx* c, const float* pts, float* enc, int64_t n, void* s
     if (n <= 0) return FFN_OK;
     if (!aligned16(enc)) return fail(c, FFN_E_CONFIG, "enc must be 16-byte aligned");
     DeviceGuard guard(c->device);
-    const int64_t items = n * L;
-    const int blocks = (int)((items + 255) / 256 < 148 * 16 ? (items + 255) / 256 : 148 * 16);
+    const int64_t items = (n + 15) / 16;   // blocks of 16 points x 16 levels
+    const int sms = c->max_grid / c->ctas_per_sm;
+    const int blocks = (int)(items < (int64_t)sms * 16 ? items : (int64_t)sms * 16);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (c->cfg.F == 2) hash_fwd_kernel<2><<<blocks, 256, 0, st>>>(c->dc, c->table, pts, n, enc);
     else hash_fwd_kernel<4><<<blocks, 256, 0, st>>>(c->dc, c->table, pts, n, enc);
@@ -485,8 +486,9 @@ int ffn_hash_encode_bwd(ffn_ctx* c, const float* pts, const float* denc, int64_t
     if (n <= 0) return FFN_OK;
     if (!aligned16(denc)) return fail(c, FFN_E_CONFIG, "denc must be 16-byte aligned");
     DeviceGuard guard(c->device);
-    const int64_t items = n * L;
-    const int blocks = (int)((items + 255) / 256 < 148 * 16 ? (items + 255) / 256 : 148 * 16);
+    const int64_t items = (n + 15) / 16;   // blocks of 16 points x 16 levels
+    const int sms = c->max_grid / c->ctas_per_sm;
+    const int blocks = (int)(items < (int64_t)sms * 16 ? items : (int64_t)sms * 16);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (c->cfg.F == 2) hash_bwd_kernel<2><<<blocks, 256, 0, st>>>(c->dc, c->grads, pts, denc, n);
     else hash_bwd_kernel<4><<<blocks, 256, 0, st>>>(c->dc, c->grads, pts, denc, n);

@@ -560,17 +560,23 @@ __global__ void occ_bytes_kernel(uint32_t* __restrict__ grid, uint8_t* __restric
     }
 }
 
-// One thread per (point, level), level fastest: a warp covers 32/16 = 2 points, so the point
-// reads are broadcasts and the feature rows [n][16 F] are written / read as contiguous 8 F-byte
+// One thread per (point, level), level fastest: a block covers all 16 levels of 16 points, so the
+// point reads are broadcasts and the feature rows [n][16 F] are written / read as contiguous 8 F-byte
 // pieces by consecutive lanes.  Each thread does its level's 8 corner gathers (or atomic adds).
-template <int F>
+// (Sweeping one level at a time over all points does not help tables larger than L2 with this row
+// layout: the partial-line writes of the feature rows evict the level's table.)
+template <int F, int LG = 16>
 __global__ void __launch_bounds__(256) hash_fwd_kernel(const DevConfig c, const float* __restrict__ table,
                                                        const float* __restrict__ pts, int64_t n,
                                                        float* __restrict__ enc) {
-    const int64_t total = n * L;
-    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < total; j += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t i = j >> 4;
-        const int lvl = (int)(j & (L - 1));
+    constexpr int CH = 256 / LG;
+    const int64_t n_chunks = (n + CH - 1) / CH;
+    const int64_t items = n_chunks * (L / LG);
+    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+        const int grp = (int)(item / n_chunks);
+        const int64_t i = (item - grp * n_chunks) * CH + threadIdx.x / LG;
+        const int lvl = grp * LG + (int)(threadIdx.x % LG);
+        if (i >= n) continue;
         const float hi = 1.0f - 1.0e-6f;
         const V3 p = v3(fclamp(pts[3 * i], 0.f, hi), fclamp(pts[3 * i + 1], 0.f, hi), fclamp(pts[3 * i + 2], 0.f, hi));
         Corner8 k;
@@ -598,14 +604,18 @@ __global__ void __launch_bounds__(256) hash_fwd_kernel(const DevConfig c, const 
     }
 }
 
-template <int F>
+template <int F, int LG = 16>
 __global__ void __launch_bounds__(256) hash_bwd_kernel(const DevConfig c, float* __restrict__ grad,
                                                        const float* __restrict__ pts,
                                                        const float* __restrict__ denc, int64_t n) {
-    const int64_t total = n * L;
-    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < total; j += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t i = j >> 4;
-        const int lvl = (int)(j & (L - 1));
+    constexpr int CH = 256 / LG;
+    const int64_t n_chunks = (n + CH - 1) / CH;
+    const int64_t items = n_chunks * (L / LG);
+    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+        const int grp = (int)(item / n_chunks);
+        const int64_t i = (item - grp * n_chunks) * CH + threadIdx.x / LG;
+        const int lvl = grp * LG + (int)(threadIdx.x % LG);
+        if (i >= n) continue;
         const float* g = denc + i * (L * F) + lvl * F;
         float gf[F];
         bool any = false;

@@ -668,19 +668,24 @@ __global__ void __launch_bounds__(128) sample_stage_kernel(const StepArgs a, flo
     }
 }
 
-// Hash encoding, one thread per (sample, level), level fastest, into the X0 operand tiles
-// (x INPUT_SCALE, fp16): the same accumulation order as encode_rows.  Rows of samples that are
-// not staged (past the last ray) or whose ray misses the box are zero.  The table is only read
-// during this launch.
+// Hash encoding into the X0 operand tiles (x INPUT_SCALE, fp16), the same accumulation order as
+// encode_rows.  Work is level-major: block-sized chunks of 256 consecutive samples for one level,
+// all chunks of level 0 first, so the whole grid gathers from one level's table at a time (an L2
+// working set of one level), and the 32 lanes of a warp -- consecutive samples of one ray -- read
+// the same corner slot, so samples that share a cell share the sector request.  Rows of samples
+// that are not staged (past the last ray) or whose ray misses the box are zero.  The table is only
+// read during this launch.
 template <int F>
 __global__ void __launch_bounds__(256) encode_stage_kernel(const DevConfig c, const float* __restrict__ table,
                                                            const float4* __restrict__ pn_in, int64_t n_valid,
                                                            int64_t n_rows, unsigned char* __restrict__ x0_out) {
     constexpr int LPOS = L * F;
-    const int64_t total = n_rows * L;
-    for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < total; j += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t i = j >> 4;
-        const int lvl = (int)(j & (L - 1));
+    const int n_chunks = (int)((n_rows + 255) / 256);
+    const int items = n_chunks * L;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int lvl = item / n_chunks;
+        const int64_t i = (int64_t)(item - lvl * n_chunks) * 256 + threadIdx.x;
+        if (i >= n_rows) continue;
         float v[F];
 #pragma unroll
         for (int f = 0; f < F; ++f) v[f] = 0.0f;

@@ -229,9 +229,9 @@ def test_adam_bit_exact(oracle, n):
     assert np.array_equal(tv.cpu().numpy(), v)
 
 
-@pytest.mark.parametrize("F", [2, 4])
-def test_hash_encode_fwd_bwd(oracle, F):
-    g = make_geometry(F=F, ND=1, NC=2, log2_entries=12, rmax=2048.0)
+@pytest.mark.parametrize("F,log2T", [(2, 12), (4, 12), (2, 21)])   # 2^21: table > 64 MB, swept by level
+def test_hash_encode_fwd_bwd(oracle, F, log2T):
+    g = make_geometry(F=F, ND=1, NC=2, log2_entries=log2T, rmax=2048.0)
     ctx = fn.Context(g)
     table = init_table(g, 1)
     ctx.tensor(fn.BUF_TABLE).copy_(_cuda(table))
