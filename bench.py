@@ -572,7 +572,9 @@ def main():
             "config": {"workload": wl["desc"], "global_batch_rays": n_glob, "samples_per_ray": spr,
                        "samples_per_step": samples_per_step, "parallelism": f"dp{world}",
                        "table_update": "immediate (Hogwild, in the fused kernel)" if nerf.table_immediate
-                                       else "deferred (gradient buffer, NCCL all-reduce, SGD pass)",
+                                       else ("deferred; fused NVLink exchange kernel (peer loads/stores: gradient "
+                                             "sum + table SGD + broadcast)" if (nerf.dp is not None and nerf.dp.fused)
+                                             else "deferred; NCCL all-reduce + table SGD pass"),
                        "l2": "flushed between timed steps (256 MB write outside the step's events)"},
             "l2_warm": {"value": samples_per_step * args.steps / (ms_warm * 1e-3), "ms_per_step": ms_warm / args.steps,
                         "note": "same steps back to back, no flush: the table stays in L2 across steps"},

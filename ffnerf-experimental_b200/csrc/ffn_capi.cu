@@ -11,6 +11,7 @@
 #include "ffn_common.cuh"
 #include "ffn_step.cu"
 #include "ffn_step_tc.cu"
+#include "ffn_dp.cu"
 
 using namespace ffn;
 
@@ -45,6 +46,7 @@ struct ffn_ctx {
     float2* tdt_stage = nullptr;
     float4* pn_stage = nullptr;
     uint4* ray_stage = nullptr;
+    DpState* dp = nullptr;       // data-parallel peer mappings (ffn_dp_attach)
     std::string err;
 };
 
@@ -315,6 +317,18 @@ int ffn_destroy(ffn_ctx* c) {
     if (!c) return FFN_OK;
     DeviceGuard guard(c->device);
     cudaDeviceSynchronize();
+    if (c->dp) {
+        for (int p = 0; p < c->dp->peers.world; ++p) {
+            if (!c->dp->opened[p]) continue;
+            cudaIpcCloseMemHandle(c->dp->peers.grads[p]);
+            cudaIpcCloseMemHandle(c->dp->peers.table[p]);
+            cudaIpcCloseMemHandle(c->dp->peers.flags[p]);
+        }
+        if (c->dp->flags) cudaFree(c->dp->flags);
+        if (c->dp->done_counter) cudaFree(c->dp->done_counter);
+        delete c->dp;
+        c->dp = nullptr;
+    }
     void* ptrs[] = {c->params, c->adam_m, c->adam_v, c->table, c->table_m, c->table_v, c->occ_in,
                     c->occ_st, c->grads, c->partials, c->status, c->x0_stage, c->tdt_stage, c->pn_stage,
                     c->ray_stage};
@@ -399,8 +413,8 @@ int ffn_apply_updates(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
     lc.start[L] = (uint32_t)c->table_floats;
     const uint32_t n4 = (uint32_t)(c->table_floats / 4);
     const int blocks = (int)((n4 + 255) / 256 < 148u * 16u ? (n4 + 255) / 256 : 148u * 16u);
-    if (s->flags & FFN_STEP_TABLE_IMMEDIATE) {
-        // the table was updated inside the forward/backward pass
+    if (s->flags & (FFN_STEP_TABLE_IMMEDIATE | FFN_STEP_TABLE_APPLIED)) {
+        // the table was updated inside the forward/backward pass or by ffn_dp_reduce_apply
     } else if (g.table_optimizer == 1)
         table_adam_kernel<<<blocks, 256, 0, st>>>(c->table, c->grads, c->table_m, c->table_v, n4, lc,
                                                    g.adam_beta1, g.adam_beta2, g.table_adam_eps);
@@ -504,6 +518,85 @@ int ffn_status(ffn_ctx* c, uint32_t* status) {
     if (e != cudaSuccess) return cuda_fail(c, e, "status read");
     cudaMemset(c->status, 0, sizeof(int));
     *status = (uint32_t)h;
+    return FFN_OK;
+}
+
+int ffn_dp_ipc_handles(ffn_ctx* c, void* out) {
+    if (!c || !out) return fail(c, FFN_E_CONFIG, "null argument");
+    DeviceGuard guard(c->device);
+    cudaError_t e;
+    if (!c->dp) {
+        c->dp = new DpState();
+        if ((e = cudaMalloc((void**)&c->dp->flags, 2 * ffn::DP_MAX_RANKS * sizeof(uint32_t))) != cudaSuccess ||
+            (e = cudaMalloc((void**)&c->dp->done_counter, sizeof(unsigned int))) != cudaSuccess)
+            return cuda_fail(c, e, "flag allocation");
+        cudaMemset(c->dp->flags, 0, 2 * ffn::DP_MAX_RANKS * sizeof(uint32_t));
+        cudaMemset(c->dp->done_counter, 0, sizeof(unsigned int));
+        if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "flag initialisation");
+    }
+    cudaIpcMemHandle_t h[3];
+    if ((e = cudaIpcGetMemHandle(&h[0], c->grads)) != cudaSuccess || (e = cudaIpcGetMemHandle(&h[1], c->table)) != cudaSuccess ||
+        (e = cudaIpcGetMemHandle(&h[2], c->dp->flags)) != cudaSuccess)
+        return cuda_fail(c, e, "IPC handle");
+    std::memcpy(out, h, sizeof(h));
+    return FFN_OK;
+}
+
+int ffn_dp_attach(ffn_ctx* c, int rank, int world, const void* handles) {
+    if (!c || !handles) return fail(c, FFN_E_CONFIG, "null argument");
+    if (!c->dp) return fail(c, FFN_E_STATE, "ffn_dp_ipc_handles must be called first");
+    if (world < 1 || world > ffn::DP_MAX_RANKS || rank < 0 || rank >= world)
+        return fail(c, FFN_E_CONFIG, "world must be 1..8 and 0 <= rank < world");
+    if (c->dp->peers.world) return fail(c, FFN_E_STATE, "already attached");
+    DeviceGuard guard(c->device);
+    const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+    ffn::DpPeers& P = c->dp->peers;
+    for (int p = 0; p < world; ++p) {
+        if (p == rank) {
+            P.grads[p] = c->grads; P.table[p] = c->table; P.flags[p] = c->dp->flags;
+            continue;
+        }
+        void *g = nullptr, *t = nullptr, *f = nullptr;
+        cudaError_t e;
+        if ((e = cudaIpcOpenMemHandle(&g, h[3 * p], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess ||
+            (e = cudaIpcOpenMemHandle(&t, h[3 * p + 1], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess ||
+            (e = cudaIpcOpenMemHandle(&f, h[3 * p + 2], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) {
+            if (g) cudaIpcCloseMemHandle(g);
+            if (t) cudaIpcCloseMemHandle(t);
+            return cuda_fail(c, e, "opening a peer's IPC handle");
+        }
+        P.grads[p] = static_cast<float*>(g); P.table[p] = static_cast<float*>(t); P.flags[p] = static_cast<uint32_t*>(f);
+        c->dp->opened[p] = true;
+    }
+    P.rank = rank;
+    P.world = world;
+    return FFN_OK;
+}
+
+int ffn_dp_reduce_apply(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
+    if (!c || !s) return fail(c, FFN_E_CONFIG, "null argument");
+    if (!c->dp || !c->dp->peers.world) return fail(c, FFN_E_STATE, "ffn_dp_attach must be called first");
+    if (c->cfg.table_optimizer != 0) return fail(c, FFN_E_CONFIG, "the fused exchange applies the SGD table update only");
+    DeviceGuard guard(c->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const ffn_config& g = c->cfg;
+    LevelCoef lc{};
+    for (int l = 0; l < L; ++l) {
+        lc.start[l] = g.level_offset[l] * (uint32_t)g.F;
+        lc.coef[l] = -(s->lr_f * g.hash_lr_scale[l]) * 0.5f;   // HASH_LR_RATE
+    }
+    lc.start[L] = (uint32_t)c->table_floats;
+    const uint32_t table4 = (uint32_t)(c->table_floats / 4);
+    const uint32_t total4 = (uint32_t)((c->table_floats + (size_t)c->Pw) / 4);
+    const int sms = c->max_grid / c->ctas_per_sm;
+    const uint32_t epoch = ++c->dp->epoch;
+    ffn::dp_reduce_apply_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, table4, total4, lc, epoch, c->status,
+                                                         c->dp->done_counter);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, "exchange launch");
+    // every rank has read this rank's table gradients: clear them for the next step
+    if ((e = cudaMemsetAsync(c->grads, 0, c->table_floats * sizeof(float), st)) != cudaSuccess)
+        return cuda_fail(c, e, "gradient clear");
     return FFN_OK;
 }
 

@@ -1,0 +1,127 @@
+// ffn_dp.cu -- the data-parallel exchange of the deferred step as one kernel over NVLink peer
+// memory: gradient reduction across ranks fused with the table SGD step and the broadcast of the
+// updated table.  Included into ffn_capi.cu's translation unit.
+//
+// Every rank owns a contiguous shard (in float4 units) of the gradient buffer [table | MLP].  For
+// each float4 of its shard it loads the W ranks' gradients over NVLink (plain peer loads), sums
+// them in rank order, and
+//   * table part: applies table += coef_l * g (the reference's SGD step, ffnerf_OG.cl:2155-2168)
+//     and stores the new value into every rank's table (peer stores);
+//   * MLP part: stores the summed gradient into every rank's MLP gradient, for the local Adam.
+// That is a reduce-scatter, the SGD update of the shard and an all-gather in one pass: each byte of
+// table crosses NVLink once in each direction.  The table part of every rank's gradient buffer is
+// cleared locally (ffn_dp_reduce_apply, after the kernel) once every rank has read it.
+//
+// Ordering between ranks uses flag words in each rank's own memory (IPC-mapped by the peers):
+//   entry: block 0 of rank r stores epoch into slot r of every rank's entry flags (release, system
+//          scope), then every block waits until all W entry slots of its own rank reach epoch
+//          (acquire), i.e. every rank's gradients are complete;
+//   exit:  the last block of rank r to finish stores epoch into slot r of every rank's exit flags,
+//          then waits until all W exit slots reach epoch, so that no rank's next step reads a
+//          table or writes a gradient buffer that a peer is still reading or writing.
+// Every wait is bounded (DP_WAIT_LIMIT polls with a back-off); a wait that runs out sets status
+// bit 8 and the kernel skips its work, so no rank can hang the others.
+#include <cuda_runtime.h>
+
+namespace ffn {
+
+constexpr int DP_MAX_RANKS = 8;
+constexpr uint32_t DP_WAIT_LIMIT = 1u << 24;   // polls of ~1 us each (~16 s) before giving up
+constexpr int ST_DP_TIMEOUT = 8;
+
+struct DpPeers {
+    float* grads[DP_MAX_RANKS];      // every rank's gradient buffer (this rank's included)
+    float* table[DP_MAX_RANKS];      // every rank's table
+    uint32_t* flags[DP_MAX_RANKS];   // every rank's flag words: [0, W) entry, [W, 2W) exit
+    int rank, world;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until flags[first .. first + n) all reach epoch (wrap-safe compare).
+__device__ __forceinline__ bool dp_wait(const uint32_t* flags, int first, int n, uint32_t epoch) {
+    for (uint32_t it = 0; it < DP_WAIT_LIMIT; ++it) {
+        bool all = true;
+        for (int k = 0; k < n; ++k) all &= (int32_t)(ld_acquire_sys(flags + first + k) - epoch) >= 0;
+        if (all) return true;
+        __nanosleep(1000);
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(256) dp_reduce_apply_kernel(const DpPeers P, uint32_t table4, uint32_t total4,
+                                                              const LevelCoef lc, uint32_t epoch, int* status,
+                                                              unsigned int* done_counter) {
+    __shared__ int ok;
+    const int W = P.world, r = P.rank;
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0) {
+            __threadfence_system();
+            for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + r, epoch);
+        }
+        ok = dp_wait(P.flags[r], 0, W, epoch) ? 1 : 0;
+        if (!ok) atomicOr(status, ST_DP_TIMEOUT);
+    }
+    __syncthreads();
+    if (ok) {
+        const uint32_t per = (total4 + (uint32_t)W - 1) / (uint32_t)W;
+        const uint32_t lo = (uint32_t)r * per;
+        const uint32_t hi = lo + per < total4 ? lo + per : total4;
+        for (uint32_t i = lo + blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += gridDim.x * blockDim.x) {
+            float4 g[DP_MAX_RANKS];
+#pragma unroll
+            for (int p = 0; p < DP_MAX_RANKS; ++p)
+                if (p < W) g[p] = reinterpret_cast<const float4*>(P.grads[p])[i];
+            float4 s = g[0];
+#pragma unroll
+            for (int p = 1; p < DP_MAX_RANKS; ++p)
+                if (p < W) { s.x = fa(s.x, g[p].x); s.y = fa(s.y, g[p].y); s.z = fa(s.z, g[p].z); s.w = fa(s.w, g[p].w); }
+            if (i < table4) {
+                const float cf = lc.coef[level_of(lc, i * 4u)];
+                float4 t = reinterpret_cast<const float4*>(P.table[r])[i];
+                t.x = fa(t.x, fm(cf, s.x)); t.y = fa(t.y, fm(cf, s.y));
+                t.z = fa(t.z, fm(cf, s.z)); t.w = fa(t.w, fm(cf, s.w));
+#pragma unroll
+                for (int p = 0; p < DP_MAX_RANKS; ++p)
+                    if (p < W) reinterpret_cast<float4*>(P.table[p])[i] = t;
+            } else {
+#pragma unroll
+                for (int p = 0; p < DP_MAX_RANKS; ++p)
+                    if (p < W) reinterpret_cast<float4*>(P.grads[p])[i] = s;
+            }
+        }
+    }
+    // exit: the last block of this rank publishes completion and waits for every rank's
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int prev = atomicAdd(done_counter, 1u);
+        if (prev == gridDim.x - 1) {
+            *done_counter = 0u;
+            __threadfence_system();
+            for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + W + r, epoch);
+            if (!dp_wait(P.flags[r], W, W, epoch)) atomicOr(status, ST_DP_TIMEOUT);
+        }
+    }
+}
+
+}  // namespace ffn
+
+namespace {
+
+struct DpState {
+    ffn::DpPeers peers{};
+    uint32_t* flags = nullptr;              // this rank's flag words [2 * world]
+    unsigned int* done_counter = nullptr;
+    bool opened[ffn::DP_MAX_RANKS] = {};    // which peer mappings this rank opened (and closes)
+    uint32_t epoch = 0;
+};
+
+}  // namespace

@@ -44,6 +44,7 @@ class FfnStep(C.Structure):
 
 
 STEP_TABLE_IMMEDIATE = 1
+STEP_TABLE_APPLIED = 2
 STAGE_SAMPLES = 1 << 20   # samples per group of the split tensor-core step (ffn_capi.cu)
 ABI_VERSION = 2          # include/ffnerf.h FFN_ABI_VERSION
 
@@ -69,6 +70,9 @@ _SIGS = {
     "ffn_adam": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_float, _VP]),
     "ffn_status": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
     "ffn_forward_backward_noalloc": (C.c_int, [C.POINTER(FfnConfig)] + [_VP] * 9 + [C.c_uint32, C.POINTER(FfnStep), _VP]),
+    "ffn_dp_ipc_handles": (C.c_int, [_VP, _VP]),
+    "ffn_dp_attach": (C.c_int, [_VP, C.c_int, C.c_int, _VP]),
+    "ffn_dp_reduce_apply": (C.c_int, [_VP, C.POINTER(FfnStep), _VP]),
 }
 EXPORTED = tuple(_SIGS)
 
@@ -122,11 +126,12 @@ def make_ffn_config(geom: dict, table_optimizer: int = 0, max_rays: int = 0, ada
 
 
 def make_step(lr_f=0.0, lr_t=0.0, sh_mult=1.0, color_rel_lr=1.0, occ_strength=0.0, rng_u32=0,
-              ray_offset=0, table_lr_t=0.0, spr=0, table_immediate: bool = False) -> FfnStep:
+              ray_offset=0, table_lr_t=0.0, spr=0, table_immediate: bool = False,
+              table_applied: bool = False) -> FfnStep:
     return FfnStep(float(np.float32(lr_f)), float(np.float32(lr_t)), float(np.float32(sh_mult)),
                    float(np.float32(color_rel_lr)), float(np.float32(occ_strength)), int(rng_u32) & 0xFFFFFFFF,
                    int(ray_offset) & 0xFFFFFFFF, float(np.float32(table_lr_t)), int(spr),
-                   STEP_TABLE_IMMEDIATE if table_immediate else 0)
+                   (STEP_TABLE_IMMEDIATE if table_immediate else 0) | (STEP_TABLE_APPLIED if table_applied else 0))
 
 
 class _CudaArray:
@@ -234,12 +239,29 @@ class Context:
 
     def apply_updates(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_apply_updates(self.h, C.byref(step), self._stream(stream)), "ffn_apply_updates")
-        self.launches += 1 if step.flags & STEP_TABLE_IMMEDIATE else 2
+        self.launches += 1 if step.flags & (STEP_TABLE_IMMEDIATE | STEP_TABLE_APPLIED) else 2
 
     def train_step(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_train_step(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                             C.byref(step), self._stream(stream)), "ffn_train_step")
         self.launches += self._fb_launches(n_rays, step) + (1 if step.flags & STEP_TABLE_IMMEDIATE else 2)
+
+    # -- data-parallel exchange over NVLink peer memory
+    def dp_ipc_handles(self) -> bytes:
+        buf = (C.c_char * 192)()
+        self._check(self.lib.ffn_dp_ipc_handles(self.h, buf), "ffn_dp_ipc_handles")
+        return bytes(buf)
+
+    def dp_attach(self, rank: int, world: int, handles: list[bytes]):
+        blob = b"".join(handles)
+        if len(blob) != 192 * world:
+            raise ValueError("one 192-byte handle block per rank is required")
+        buf = (C.c_char * len(blob)).from_buffer_copy(blob)
+        self._check(self.lib.ffn_dp_attach(self.h, int(rank), int(world), buf), "ffn_dp_attach")
+
+    def dp_reduce_apply(self, step: FfnStep, stream=None):
+        self._check(self.lib.ffn_dp_reduce_apply(self.h, C.byref(step), self._stream(stream)), "ffn_dp_reduce_apply")
+        self.launches += 1
 
     def render(self, rays, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_render(self.h, _ptr(rays), _ptr(out), int(n_rays), C.byref(step),

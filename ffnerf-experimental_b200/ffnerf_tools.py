@@ -24,6 +24,8 @@ from datetime import datetime
 from pathlib import Path
 from typing import List, Optional
 
+import os
+
 import numpy as np
 
 import ffn_config as fc
@@ -412,14 +414,50 @@ def _level_log2_for(table_size_entries: int, level_log2=None) -> list[int]:
 class DataParallel:
     """Per-step gradient and occupancy exchange between data-parallel ranks (one process per
     GPU, torch.distributed over NCCL).  Every rank takes a contiguous slice of the ray batch; the
-    RNG streams are keyed by the global ray index, so the union of the shards is the batch."""
+    RNG streams are keyed by the global ray index, so the union of the shards is the batch.
 
-    def __init__(self, group=None):
+    With ``fused`` (the default when every rank's GPU can map every other's memory), the gradient
+    all-reduce and the table SGD step run as one kernel over NVLink peer memory
+    (``ffn_dp_reduce_apply``); otherwise the gradient buffer is all-reduced with NCCL and every
+    rank applies the update.  The occupancy proposals are merged with an NCCL MAX all-reduce."""
+
+    def __init__(self, group=None, fused: bool | None = None):
         import torch.distributed as dist
         self.dist = dist
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.want_fused = fused
+        self.fused = False
+        self._ctx = None
+
+    def ensure_attached(self, nerf: "Nerf"):
+        """(Re-)maps the peers after the device context was (re)created; collective."""
+        if self._ctx is not nerf.native:
+            self.fused = False
+            self.attach(nerf)
+            self._ctx = nerf.native
+
+    def attach(self, nerf: "Nerf"):
+        """Maps every rank's gradient buffer, table and flag words (CUDA IPC) when the fused
+        exchange can run: SGD table, at most 8 ranks, every GPU pair peer-accessible, same decision
+        on every rank."""
+        import torch
+        want = self.want_fused
+        if want is None:
+            want = os.environ.get("FFNERF_DP_FUSED", "1") != "0"
+        ok = bool(want) and nerf.table_optimizer == "sgd" and 2 <= self.world <= 8
+        dev = int(nerf.native.device)
+        handles = nerf.native.dp_ipc_handles() if ok else b""
+        info = [None] * self.world
+        self.dist.all_gather_object(info, (dev, handles, ok), group=self.group)
+        ok = all(i[2] for i in info) and all(
+            d == dev or torch.cuda.can_device_access_peer(dev, d) for d, _, _ in info)
+        flag = torch.tensor([1 if ok else 0], device=f"cuda:{dev}")
+        self.dist.all_reduce(flag, op=self.dist.ReduceOp.MIN, group=self.group)
+        if int(flag.item()) == 1:
+            nerf.native.dp_attach(self.rank, self.world, [h for _, h, _ in info])
+            self.fused = True
 
     def allreduce_grads(self, nerf: "Nerf"):
         self.dist.all_reduce(nerf.native.tensor(ffn_native.BUF_GRADS), op=self.dist.ReduceOp.SUM, group=self.group)
@@ -812,10 +850,10 @@ class Nerf:
     def table_immediate(self) -> bool:
         return self.table_update == "immediate" and self.table_optimizer == "sgd" and self.dp is None
 
-    def enable_data_parallel(self, group=None, ray_offset: int | None = None):
+    def enable_data_parallel(self, group=None, ray_offset: int | None = None, fused: bool | None = None):
         """Shards batches across the ranks of ``group``: this rank's rays start at global index
         ``ray_offset`` (default rank * num_rays of the current batch)."""
-        self.dp = DataParallel(group)
+        self.dp = DataParallel(group, fused=fused)
         self.ray_offset = ray_offset
 
     @staticmethod
@@ -881,7 +919,15 @@ class Nerf:
                     e1.record(q.stream)
                     self.fb_events.append((e0, e1))
                 if self.dp is not None:
-                    self.dp.allreduce_grads(self)
+                    self.dp.ensure_attached(self)
+                    if self.dp.fused:
+                        nat.dp_reduce_apply(s, q.stream)
+                        s = ffn_native.make_step(lr_f=lr_f, lr_t=lr_t, sh_mult=sh_multiplier,
+                                                 color_rel_lr=color_MLP_rel_lr, occ_strength=occ_update_strength,
+                                                 rng_u32=int(rng_u32), ray_offset=offset, table_lr_t=lr_t,
+                                                 spr=io.samples_per_ray, table_applied=True)
+                    else:
+                        self.dp.allreduce_grads(self)
                 if do_maint:
                     if self.dp is not None:
                         self.dp.merge_occupancy(self)

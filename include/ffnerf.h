@@ -25,8 +25,8 @@
  *   ffn_occ_maintenance           enqueue of occ_nibble_decay_write_both_q24
  *                                 (ffnerf_tools.py:1452-1476; decay_occ_grid_in-st.cl:13-113)
  *   ffn_grad_buffer,              (no reference counterpart: the reference has one device) the
- *   ffn_occ_st_bytes              gradient buffer and the occupancy proposals merged across
- *                                 data-parallel ranks
+ *   ffn_occ_st_bytes,             gradient buffer and the occupancy proposals merged across
+ *   ffn_dp_*                      data-parallel ranks, and the fused NVLink exchange
  */
 #ifndef FFNERF_H
 #define FFNERF_H
@@ -102,6 +102,9 @@ typedef struct ffn_step_scalars {
  * ffn_apply_updates skips the table pass.  Needs table_optimizer = 0; not for data-parallel runs,
  * whose table gradients must be all-reduced first. */
 #define FFN_STEP_TABLE_IMMEDIATE 1u
+/* ffn_step_scalars.flags: the table SGD step of this step was applied by ffn_dp_reduce_apply;
+ * ffn_apply_updates skips its table pass (MLP Adam only). */
+#define FFN_STEP_TABLE_APPLIED 2u
 
 typedef struct ffn_ctx ffn_ctx;
 
@@ -157,6 +160,20 @@ int ffn_hash_encode_bwd(ffn_ctx* ctx, const float* pts, const float* denc, int64
 /* Reads and clears the context's device status word (waits for the device): 0 when every kernel
  * since the last call completed normally; bit 2 = a tensor-core wait exceeded its bound. */
 int ffn_status(ffn_ctx* ctx, uint32_t* status);
+
+/* Data-parallel exchange over NVLink peer memory (no reference counterpart: the reference runs on
+ * one device).  One process per GPU, every rank with an identical context.  ffn_dp_ipc_handles
+ * writes 3 CUDA IPC handles (3 x 64 bytes: gradient buffer, table, flag words) that the caller
+ * exchanges between ranks (e.g. an all-gather), then ffn_dp_attach maps every peer's buffers
+ * (handles: world x 3 x 64 bytes, rank order).  After ffn_forward_backward (deferred table update),
+ * ffn_dp_reduce_apply sums every rank's gradients, applies the table SGD step to this rank's shard
+ * and writes it into every rank's table, leaves the summed MLP gradient in every rank's gradient
+ * buffer and clears the table gradients -- the all-reduce and the table pass in one kernel.  Then
+ * ffn_apply_updates with FFN_STEP_TABLE_APPLIED runs the MLP Adam.  Every rank must call it in
+ * the same steps; its cross-rank waits are bounded (status bit 8 on a timeout).  SGD table only. */
+int ffn_dp_ipc_handles(ffn_ctx* ctx, void* handles_out);
+int ffn_dp_attach(ffn_ctx* ctx, int rank, int world, const void* handles);
+int ffn_dp_reduce_apply(ffn_ctx* ctx, const ffn_step_scalars* s, void* stream);
 
 /* Plain Adam over n float32 parameters (vectorised; beta/eps as given). */
 int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float beta1,

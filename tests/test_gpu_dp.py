@@ -1,0 +1,119 @@
+"""The fused data-parallel exchange (ffn_dp_reduce_apply: gradient sum over NVLink peer memory,
+table SGD on each rank's shard, broadcast of the updated table) against the NCCL path (all-reduce
+of the gradient buffer, then the table pass), on 2 GPUs.
+
+Each rank holds two identical contexts and trains both for 3 steps on its half of the batch: one
+through NCCL + ffn_apply_updates, one through ffn_dp_reduce_apply + ffn_apply_updates(TABLE_APPLIED).
+Contracts: tables and parameters of the two paths agree within rel-L2 1e-6 (only the order of the
+cross-rank float sums differs) on every rank; both ranks end with the same table; the status
+word stays 0.  Needs 2 GPUs (skipped otherwise).
+"""
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        for p in (ROOT / "ffnerf-experimental_b200", ROOT / "tests"):
+            sys.path.insert(0, str(p))
+        import datetime
+        import torch.distributed as dist
+        import ffn_native as fn
+        from _helpers import init_blob, init_occ, init_table, rays_toward_box, rel_l2, targets
+        from ffn_config import make_geometry
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        g = make_geometry(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0)
+        blob, table, occ = init_blob(g, 4), init_table(g, 4), init_occ(g, 4)
+        ctxs = []
+        for prec in ("fp16", "fp16"):
+            c = fn.Context(g, device=rank, mlp_precision=prec)
+            c.tensor(fn.BUF_PARAMS).copy_(torch.from_numpy(blob))
+            c.tensor(fn.BUF_TABLE).copy_(torch.from_numpy(table))
+            c.tensor(fn.BUF_OCC_IN).copy_(torch.from_numpy(occ.view(np.int32)))
+            c.tensor(fn.BUF_OCC_ST).copy_(torch.from_numpy(occ.view(np.int32)))
+            ctxs.append(c)
+        nccl_ctx, fused_ctx = ctxs
+        handles = fused_ctx.dp_ipc_handles()
+        allh = [None] * world
+        dist.all_gather_object(allh, handles)
+        fused_ctx.dp_attach(rank, world, allh)
+        n = 256
+        half = n // world
+        dev = torch.device("cuda", rank)
+        for step in range(1, 4):
+            rays = torch.from_numpy(rays_toward_box(n, 100 + step, radius=2.0, n_miss=2)[rank * half:(rank + 1) * half]).to(dev)
+            tg = torch.from_numpy(targets(n, 100 + step)[rank * half:(rank + 1) * half]).to(dev)
+            kw = dict(lr_f=2e-2, lr_t=1e-3, color_rel_lr=0.5, rng_u32=step * 977, ray_offset=rank * half)
+            s = fn.make_step(**kw)
+            out = torch.zeros((half, 4), device=dev)
+            nccl_ctx.forward_backward(rays, tg, out, half, s)
+            dist.all_reduce(nccl_ctx.tensor(fn.BUF_GRADS), op=dist.ReduceOp.SUM)
+            nccl_ctx.apply_updates(s)
+            out2 = torch.zeros((half, 4), device=dev)
+            fused_ctx.forward_backward(rays, tg, out2, half, s)
+            fused_ctx.dp_reduce_apply(s)
+            fused_ctx.apply_updates(fn.make_step(**kw, table_applied=True))
+            torch.cuda.synchronize()
+        t_a = nccl_ctx.tensor(fn.BUF_TABLE).cpu().numpy()
+        t_b = fused_ctx.tensor(fn.BUF_TABLE).cpu().numpy()
+        p_a = nccl_ctx.tensor(fn.BUF_PARAMS).cpu().numpy()
+        p_b = fused_ctx.tensor(fn.BUF_PARAMS).cpu().numpy()
+        res = dict(table=rel_l2(t_b - table, t_a - table), params=rel_l2(p_b - blob, p_a - blob),
+                   grads_clear=not fused_ctx.tensor(fn.BUF_GRADS).any().item(),
+                   status=(nccl_ctx.status(), fused_ctx.status()), checksum=float(np.float64(t_b).sum()))
+        sums = [None] * world
+        dist.all_gather_object(sums, res["checksum"])
+        res["same_table"] = len(set(sums)) == 1
+        for c in ctxs:
+            c.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok", res))
+    except Exception as exc:
+        import traceback
+        q.put((rank, "err", f"{exc}\n{traceback.format_exc()}"))
+
+
+def test_fused_exchange_matches_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, st, res = q.get(timeout=240)
+            results[rank] = (st, res)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank, (st, res) in results.items():
+        assert st == "ok", res
+        assert res["table"] < 1e-6 and res["params"] < 1e-6, res
+        assert res["grads_clear"] and res["same_table"] and res["status"] == (0, 0), res
