@@ -4,9 +4,10 @@ of the gradient buffer, then the table pass), on 2 GPUs.
 
 Each rank holds two identical contexts and trains both for 3 steps on its half of the batch: one
 through NCCL + ffn_apply_updates, one through ffn_dp_reduce_apply + ffn_apply_updates(TABLE_APPLIED).
-Contracts: tables and parameters of the two paths agree within rel-L2 1e-6 (only the order of the
-cross-rank float sums differs) on every rank; both ranks end with the same table; the status
-word stays 0.  Needs 2 GPUs (skipped otherwise).
+Contracts: the table and parameter updates of the two paths agree within rel-L2 1e-4 on every rank
+(the one-step gradient tolerance: the two contexts' table gradients differ in the order of their
+float atomic adds, and the cross-rank sums in summation order); both ranks end with the same
+table; the gradient buffers are clear; the status word stays 0.  Needs 2 GPUs (skipped otherwise).
 """
 import os
 import socket
@@ -115,5 +116,5 @@ def test_fused_exchange_matches_nccl():
                 p.kill()
     for rank, (st, res) in results.items():
         assert st == "ok", res
-        assert res["table"] < 1e-6 and res["params"] < 1e-6, res
+        assert res["table"] < 1e-4 and res["params"] < 1e-4, res
         assert res["grads_clear"] and res["same_table"] and res["status"] == (0, 0), res
