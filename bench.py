@@ -490,6 +490,8 @@ def main():
     # with the previous step's table lines in L2.
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
+    host_s = []
+
     def timed_steps(n_steps: int, start: int, host: bool, flush: bool = True):
         pairs, outs = [], []
         for i in range(n_steps):
@@ -498,7 +500,9 @@ def main():
                     flush_buf.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(queue.stream)
+            h0 = time.perf_counter()
             out = one_step(start + i, host=host)
+            host_s.append(time.perf_counter() - h0)
             b.record(queue.stream)
             pairs.append((a, b))
             outs.append(out)
@@ -516,12 +520,15 @@ def main():
     with ClockSampler(local) as clk:
         # (1) device-resident inputs: value, and the fused kernel's own events (roofline)
         nerf.fb_events = []
+        nerf.ex_events = []
         launches0 = nerf.native.launches
         ms_sum, _ = timed_steps(args.steps, args.warmup, host=False)
+        host_ms = 1e3 * statistics.median(host_s)
         barrier()
         ms_total = max_over_ranks(ms_sum)
         launches = nerf.native.launches - launches0
         fb_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in nerf.fb_events))
+        ex_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in nerf.ex_events)) if nerf.ex_events else 0.0
         nerf.fb_events = None
         # (2) the same steps back to back without the flush (the table stays in L2 across steps)
         barrier()
@@ -545,7 +552,11 @@ def main():
         if rank == 0:
             print(json.dumps({"metric": METRIC, "value": n_glob * spr * args.steps / (ms_total * 1e-3),
                               "unit": "samples/s", "note": "profiling run (no e2e, no baseline)",
-                              "gpu_launches": launches, "fused_ms": fb_ms}), flush=True)
+                              "gpu_launches": launches, "fused_ms": fb_ms, "exchange_ms": ex_ms,
+                              "exchange": ("nvls" if nerf.dp.nvls else "p2p" if nerf.dp.fused else "nccl")
+                              if nerf.dp is not None else None,
+                              "host_ms_per_step": host_ms,
+                              "ms_per_step": ms_total / args.steps}), flush=True)
         if dist is not None:
             dist.destroy_process_group()
         return
@@ -572,7 +583,10 @@ def main():
             "config": {"workload": wl["desc"], "global_batch_rays": n_glob, "samples_per_ray": spr,
                        "samples_per_step": samples_per_step, "parallelism": f"dp{world}",
                        "table_update": "immediate (Hogwild, in the fused kernel)" if nerf.table_immediate
-                                       else ("deferred; fused NVLink exchange kernel (peer loads/stores: gradient "
+                                       else ("deferred; fused exchange kernel over NVSwitch multicast (multimem "
+                                             "ld_reduce gradient sum + table SGD + multimem st broadcast)"
+                                             if (nerf.dp is not None and nerf.dp.nvls) else
+                                             "deferred; fused exchange kernel over NVLink peer loads/stores (gradient "
                                              "sum + table SGD + broadcast)" if (nerf.dp is not None and nerf.dp.fused)
                                              else "deferred; NCCL all-reduce + table SGD pass"),
                        "l2": "flushed between timed steps (256 MB write outside the step's events)"},
@@ -581,6 +595,8 @@ def main():
             "e2e": {"value": e2e_val, "unit": "samples/s", "h2d_bytes_per_step": n_loc * (32 + 16) * world,
                     "d2h_bytes_per_step": n_loc * 16 * world, "final_mse": losses[-1]},
             "gpu_launches": launches,
+            "host_ms_per_step": host_ms,
+            "exchange_ms": ex_ms,
             "roofline": {"bound": "hbm", "kernel": "fused_step_kernel (+ partial-gradient reduce)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": traffic, "peak_source": peak_kind,

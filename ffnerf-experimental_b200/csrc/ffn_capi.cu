@@ -47,6 +47,8 @@ struct ffn_ctx {
     float4* pn_stage = nullptr;
     uint4* ray_stage = nullptr;
     DpState* dp = nullptr;       // data-parallel peer mappings (ffn_dp_attach)
+    bool ext_table = false;      // table / gradient buffer bound from outside (ffn_bind_external)
+    bool ext_grads = false;
     std::string err;
 };
 
@@ -320,8 +322,8 @@ int ffn_destroy(ffn_ctx* c) {
     if (c->dp) {
         for (int p = 0; p < c->dp->peers.world; ++p) {
             if (!c->dp->opened[p]) continue;
-            cudaIpcCloseMemHandle(c->dp->peers.grads[p]);
-            cudaIpcCloseMemHandle(c->dp->peers.table[p]);
+            if (c->dp->peers.grads[p]) cudaIpcCloseMemHandle(c->dp->peers.grads[p]);
+            if (c->dp->peers.table[p]) cudaIpcCloseMemHandle(c->dp->peers.table[p]);
             cudaIpcCloseMemHandle(c->dp->peers.flags[p]);
         }
         if (c->dp->flags) cudaFree(c->dp->flags);
@@ -329,9 +331,9 @@ int ffn_destroy(ffn_ctx* c) {
         delete c->dp;
         c->dp = nullptr;
     }
-    void* ptrs[] = {c->params, c->adam_m, c->adam_v, c->table, c->table_m, c->table_v, c->occ_in,
-                    c->occ_st, c->grads, c->partials, c->status, c->x0_stage, c->tdt_stage, c->pn_stage,
-                    c->ray_stage};
+    void* ptrs[] = {c->params, c->adam_m, c->adam_v, c->ext_table ? nullptr : c->table, c->table_m, c->table_v,
+                    c->occ_in, c->occ_st, c->ext_grads ? nullptr : c->grads, c->partials, c->status, c->x0_stage,
+                    c->tdt_stage, c->pn_stage, c->ray_stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -535,7 +537,11 @@ int ffn_dp_ipc_handles(ffn_ctx* c, void* out) {
         if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(c, e, "flag initialisation");
     }
     cudaIpcMemHandle_t h[3];
-    if ((e = cudaIpcGetMemHandle(&h[0], c->grads)) != cudaSuccess || (e = cudaIpcGetMemHandle(&h[1], c->table)) != cudaSuccess ||
+    std::memset(h, 0, sizeof(h));
+    // buffers bound from outside (multicast-capable allocations) are not exported: the NVLS exchange
+    // reaches them through their multicast address
+    if ((!c->ext_grads && (e = cudaIpcGetMemHandle(&h[0], c->grads)) != cudaSuccess) ||
+        (!c->ext_table && (e = cudaIpcGetMemHandle(&h[1], c->table)) != cudaSuccess) ||
         (e = cudaIpcGetMemHandle(&h[2], c->dp->flags)) != cudaSuccess)
         return cuda_fail(c, e, "IPC handle");
     std::memcpy(out, h, sizeof(h));
@@ -557,9 +563,10 @@ int ffn_dp_attach(ffn_ctx* c, int rank, int world, const void* handles) {
             continue;
         }
         void *g = nullptr, *t = nullptr, *f = nullptr;
-        cudaError_t e;
-        if ((e = cudaIpcOpenMemHandle(&g, h[3 * p], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess ||
-            (e = cudaIpcOpenMemHandle(&t, h[3 * p + 1], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess ||
+        cudaError_t e = cudaSuccess;
+        const bool flags_only = c->ext_grads || c->ext_table;   // NVLS exchange: peers' buffers via multicast
+        if ((!flags_only && (e = cudaIpcOpenMemHandle(&g, h[3 * p], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) ||
+            (!flags_only && (e = cudaIpcOpenMemHandle(&t, h[3 * p + 1], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) ||
             (e = cudaIpcOpenMemHandle(&f, h[3 * p + 2], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) {
             if (g) cudaIpcCloseMemHandle(g);
             if (t) cudaIpcCloseMemHandle(t);
@@ -570,6 +577,36 @@ int ffn_dp_attach(ffn_ctx* c, int rank, int world, const void* handles) {
     }
     P.rank = rank;
     P.world = world;
+    return FFN_OK;
+}
+
+int ffn_bind_external(ffn_ctx* c, int id, void* dev_ptr, size_t bytes) {
+    if (!c || !dev_ptr) return fail(c, FFN_E_CONFIG, "null argument");
+    if (id != FFN_BUF_TABLE && id != FFN_BUF_GRADS) return fail(c, FFN_E_NAME, "only the table and the gradient buffer can be bound");
+    if (c->dp && c->dp->peers.world) return fail(c, FFN_E_STATE, "bind buffers before ffn_dp_attach");
+    if (!aligned16(dev_ptr)) return fail(c, FFN_E_CONFIG, "buffer must be 16-byte aligned");
+    const size_t need = (c->table_floats + (id == FFN_BUF_GRADS ? (size_t)c->Pw : 0)) * sizeof(float);
+    if (bytes < need) return fail(c, FFN_E_CAPACITY, "buffer smaller than the context's");
+    DeviceGuard guard(c->device);
+    float*& slot = id == FFN_BUF_TABLE ? c->table : c->grads;
+    bool& ext = id == FFN_BUF_TABLE ? c->ext_table : c->ext_grads;
+    cudaError_t e;
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess ||
+        (e = cudaMemcpy(dev_ptr, slot, need, cudaMemcpyDeviceToDevice)) != cudaSuccess)
+        return cuda_fail(c, e, "copy into the bound buffer");
+    if (!ext) cudaFree(slot);
+    slot = static_cast<float*>(dev_ptr);
+    ext = true;
+    return FFN_OK;
+}
+
+int ffn_dp_attach_multicast(ffn_ctx* c, void* mc_grads, void* mc_table) {
+    if (!c || !mc_grads || !mc_table) return fail(c, FFN_E_CONFIG, "null argument");
+    if (!c->dp || !c->dp->peers.world) return fail(c, FFN_E_STATE, "ffn_dp_attach must be called first");
+    if (!c->ext_grads || !c->ext_table) return fail(c, FFN_E_STATE, "bind the multicast-backed buffers first");
+    if (!aligned16(mc_grads) || !aligned16(mc_table)) return fail(c, FFN_E_CONFIG, "multicast addresses must be 16-byte aligned");
+    c->dp->mc_grads = static_cast<float*>(mc_grads);
+    c->dp->mc_table = static_cast<float*>(mc_table);
     return FFN_OK;
 }
 
@@ -590,8 +627,15 @@ int ffn_dp_reduce_apply(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
     const uint32_t total4 = (uint32_t)((c->table_floats + (size_t)c->Pw) / 4);
     const int sms = c->max_grid / c->ctas_per_sm;
     const uint32_t epoch = ++c->dp->epoch;
-    ffn::dp_reduce_apply_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, table4, total4, lc, epoch, c->status,
-                                                         c->dp->done_counter);
+    if (c->dp->mc_grads)
+        ffn::dp_reduce_apply_nvls_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, c->dp->mc_grads, c->dp->mc_table,
+                                                                  c->table, table4, total4, lc, epoch, c->status,
+                                                                  c->dp->done_counter);
+    else if (c->ext_grads || c->ext_table)
+        return fail(c, FFN_E_STATE, "externally bound buffers need ffn_dp_attach_multicast");
+    else
+        ffn::dp_reduce_apply_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, table4, total4, lc, epoch, c->status,
+                                                             c->dp->done_counter);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "exchange launch");
     // every rank has read this rank's table gradients: clear them for the next step

@@ -112,12 +112,74 @@ __global__ void __launch_bounds__(256) dp_reduce_apply_kernel(const DpPeers P, u
     }
 }
 
+// The same exchange through the NVSwitch (NVLS): the gradient buffer and the table of every rank are
+// bound to one multicast object each, so multimem.ld_reduce on the multicast address returns the
+// sum over all ranks (the switch adds) and multimem.st writes one value into every rank's copy.
+// Each rank moves only its shard once in each direction.  Flags and waits as above.
+__device__ __forceinline__ float4 mc_ld_reduce_add(const float* mc) {
+    float4 v;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(mc) : "memory");
+    return v;
+}
+__device__ __forceinline__ void mc_st(float* mc, float4 v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+                 :: "l"(mc), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+
+__global__ void __launch_bounds__(256) dp_reduce_apply_nvls_kernel(const DpPeers P, float* mc_grads, float* mc_table,
+                                                                   const float* __restrict__ table, uint32_t table4,
+                                                                   uint32_t total4, const LevelCoef lc, uint32_t epoch,
+                                                                   int* status, unsigned int* done_counter) {
+    __shared__ int ok;
+    const int W = P.world, r = P.rank;
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0) {
+            __threadfence_system();
+            for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + r, epoch);
+        }
+        ok = dp_wait(P.flags[r], 0, W, epoch) ? 1 : 0;
+        if (!ok) atomicOr(status, ST_DP_TIMEOUT);
+    }
+    __syncthreads();
+    if (ok) {
+        const uint32_t per = (total4 + (uint32_t)W - 1) / (uint32_t)W;
+        const uint32_t lo = (uint32_t)r * per;
+        const uint32_t hi = lo + per < total4 ? lo + per : total4;
+        for (uint32_t i = lo + blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += gridDim.x * blockDim.x) {
+            const float4 s = mc_ld_reduce_add(mc_grads + 4 * (size_t)i);
+            if (i < table4) {
+                const float cf = lc.coef[level_of(lc, i * 4u)];
+                float4 t = reinterpret_cast<const float4*>(table)[i];
+                t.x = fa(t.x, fm(cf, s.x)); t.y = fa(t.y, fm(cf, s.y));
+                t.z = fa(t.z, fm(cf, s.z)); t.w = fa(t.w, fm(cf, s.w));
+                mc_st(mc_table + 4 * (size_t)i, t);
+            } else {
+                mc_st(mc_grads + 4 * (size_t)i, s);
+            }
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int prev = atomicAdd(done_counter, 1u);
+        if (prev == gridDim.x - 1) {
+            *done_counter = 0u;
+            __threadfence_system();
+            for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + W + r, epoch);
+            if (!dp_wait(P.flags[r], W, W, epoch)) atomicOr(status, ST_DP_TIMEOUT);
+        }
+    }
+}
+
 }  // namespace ffn
 
 namespace {
 
 struct DpState {
     ffn::DpPeers peers{};
+    float* mc_grads = nullptr;              // multicast addresses (NVLS exchange), or null
+    float* mc_table = nullptr;
     uint32_t* flags = nullptr;              // this rank's flag words [2 * world]
     unsigned int* done_counter = nullptr;
     bool opened[ffn::DP_MAX_RANKS] = {};    // which peer mappings this rank opened (and closes)

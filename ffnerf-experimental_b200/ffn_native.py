@@ -73,6 +73,8 @@ _SIGS = {
     "ffn_dp_ipc_handles": (C.c_int, [_VP, _VP]),
     "ffn_dp_attach": (C.c_int, [_VP, C.c_int, C.c_int, _VP]),
     "ffn_dp_reduce_apply": (C.c_int, [_VP, C.POINTER(FfnStep), _VP]),
+    "ffn_bind_external": (C.c_int, [_VP, C.c_int, _VP, C.c_size_t]),
+    "ffn_dp_attach_multicast": (C.c_int, [_VP, _VP, _VP]),
 }
 EXPORTED = tuple(_SIGS)
 
@@ -258,6 +260,18 @@ class Context:
             raise ValueError("one 192-byte handle block per rank is required")
         buf = (C.c_char * len(blob)).from_buffer_copy(blob)
         self._check(self.lib.ffn_dp_attach(self.h, int(rank), int(world), buf), "ffn_dp_attach")
+
+    def bind_external(self, buf_id: int, tensor):
+        """Moves the table or gradient buffer into ``tensor`` (a CUDA float32 tensor this object keeps
+        alive), copying the contents."""
+        self._check(self.lib.ffn_bind_external(self.h, int(buf_id), _ptr(tensor), tensor.numel() * tensor.element_size()),
+                    "ffn_bind_external")
+        self._views.pop(buf_id, None)
+        self._external = getattr(self, "_external", []) + [tensor]
+
+    def dp_attach_multicast(self, mc_grads: int, mc_table: int):
+        self._check(self.lib.ffn_dp_attach_multicast(self.h, C.c_void_p(int(mc_grads)), C.c_void_p(int(mc_table))),
+                    "ffn_dp_attach_multicast")
 
     def dp_reduce_apply(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_dp_reduce_apply(self.h, C.byref(step), self._stream(stream)), "ffn_dp_reduce_apply")

@@ -429,35 +429,68 @@ class DataParallel:
         self.world = dist.get_world_size(group)
         self.want_fused = fused
         self.fused = False
+        self.nvls = False
         self._ctx = None
 
     def ensure_attached(self, nerf: "Nerf"):
         """(Re-)maps the peers after the device context was (re)created; collective."""
         if self._ctx is not nerf.native:
             self.fused = False
+            self.nvls = False
             self.attach(nerf)
             self._ctx = nerf.native
 
     def attach(self, nerf: "Nerf"):
-        """Maps every rank's gradient buffer, table and flag words (CUDA IPC) when the fused
-        exchange can run: SGD table, at most 8 ranks, every GPU pair peer-accessible, same decision
-        on every rank."""
+        """Sets up the fused exchange when it can run: SGD table, 2..8 ranks, every GPU pair
+        peer-accessible, the same decision on every rank.  When the NVSwitch offers multicast
+        (NVLS), the table and the gradient buffer move into symmetric multicast memory and the
+        exchange reduces and broadcasts through the switch; otherwise it uses peer loads/stores."""
         import torch
         want = self.want_fused
         if want is None:
             want = os.environ.get("FFNERF_DP_FUSED", "1") != "0"
         ok = bool(want) and nerf.table_optimizer == "sgd" and 2 <= self.world <= 8
         dev = int(nerf.native.device)
-        handles = nerf.native.dp_ipc_handles() if ok else b""
         info = [None] * self.world
-        self.dist.all_gather_object(info, (dev, handles, ok), group=self.group)
-        ok = all(i[2] for i in info) and all(
-            d == dev or torch.cuda.can_device_access_peer(dev, d) for d, _, _ in info)
+        self.dist.all_gather_object(info, (dev, ok), group=self.group)
+        ok = all(i[1] for i in info) and all(d == dev or torch.cuda.can_device_access_peer(dev, d) for d, _ in info)
+        if not self._agree(ok, dev):
+            return
+        self.nvls = os.environ.get("FFNERF_DP_NVLS", "1") != "0" and self._bind_multicast(nerf, dev)
+        handles = [None] * self.world
+        self.dist.all_gather_object(handles, nerf.native.dp_ipc_handles(), group=self.group)
+        nerf.native.dp_attach(self.rank, self.world, handles)
+        if self.nvls:
+            nerf.native.dp_attach_multicast(*self._mc)
+        self.fused = True
+
+    def _agree(self, ok: bool, dev: int) -> bool:
+        import torch
         flag = torch.tensor([1 if ok else 0], device=f"cuda:{dev}")
         self.dist.all_reduce(flag, op=self.dist.ReduceOp.MIN, group=self.group)
-        if int(flag.item()) == 1:
-            nerf.native.dp_attach(self.rank, self.world, [h for _, h, _ in info])
-            self.fused = True
+        return int(flag.item()) == 1
+
+    def _bind_multicast(self, nerf: "Nerf", dev: int) -> bool:
+        """Allocates the gradient buffer and the table in symmetric memory with a multicast
+        address on every rank (collective); binds them into the context if every rank got one."""
+        import torch
+        bufs = []
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            grp = self.group if self.group is not None else self.dist.group.WORLD
+            for bid in (ffn_native.BUF_GRADS, ffn_native.BUF_TABLE):
+                t = symm_mem.empty(nerf.native.tensor(bid).numel(), dtype=torch.float32, device=f"cuda:{dev}")
+                bufs.append((t, symm_mem.rendezvous(t, grp.group_name)))
+            good = all(int(getattr(h, "multicast_ptr", 0) or 0) != 0 for _, h in bufs)
+        except Exception:
+            good = False
+        if not self._agree(good, dev):
+            return False
+        nerf.native.bind_external(ffn_native.BUF_GRADS, bufs[0][0])
+        nerf.native.bind_external(ffn_native.BUF_TABLE, bufs[1][0])
+        self._symm = bufs
+        self._mc = (int(bufs[0][1].multicast_ptr), int(bufs[1][1].multicast_ptr))
+        return True
 
     def allreduce_grads(self, nerf: "Nerf"):
         self.dist.all_reduce(nerf.native.tensor(ffn_native.BUF_GRADS), op=self.dist.ReduceOp.SUM, group=self.group)
@@ -534,6 +567,7 @@ class Nerf:
         self._shapes = {}
         self.native: ffn_native.Context | None = None
         self.dp: DataParallel | None = None
+        self.ex_events: list = []      # (start, end) CUDA events of the fused exchange, when fb_events is on
         self.ray_offset = 0
         self._occ_bytes = None
         self.fb_events = None      # list -> (start, end) CUDA events around every forward/backward launch
@@ -921,7 +955,14 @@ class Nerf:
                 if self.dp is not None:
                     self.dp.ensure_attached(self)
                     if self.dp.fused:
+                        if self.fb_events is not None:
+                            x0 = torch.cuda.Event(enable_timing=True)
+                            x0.record(q.stream)
                         nat.dp_reduce_apply(s, q.stream)
+                        if self.fb_events is not None:
+                            x1 = torch.cuda.Event(enable_timing=True)
+                            x1.record(q.stream)
+                            self.ex_events.append((x0, x1))
                         s = ffn_native.make_step(lr_f=lr_f, lr_t=lr_t, sh_mult=sh_multiplier,
                                                  color_rel_lr=color_MLP_rel_lr, occ_strength=occ_update_strength,
                                                  rng_u32=int(rng_u32), ray_offset=offset, table_lr_t=lr_t,

@@ -174,6 +174,15 @@ int ffn_status(ffn_ctx* ctx, uint32_t* status);
 int ffn_dp_ipc_handles(ffn_ctx* ctx, void* handles_out);
 int ffn_dp_attach(ffn_ctx* ctx, int rank, int world, const void* handles);
 int ffn_dp_reduce_apply(ffn_ctx* ctx, const ffn_step_scalars* s, void* stream);
+/* NVSwitch (NVLS) variant of the exchange.  ffn_bind_external moves the context's table or
+ * gradient buffer (FFN_BUF_TABLE / FFN_BUF_GRADS) into caller-owned device memory of at least the
+ * same size -- here, memory bound to a multicast object on every rank -- copying the contents; the
+ * caller keeps it alive until ffn_destroy.  Bind both before ffn_dp_attach (which then maps only
+ * the peers' flag words), then ffn_dp_attach_multicast gives the two multicast addresses:
+ * ffn_dp_reduce_apply then reads the cross-rank gradient sum with multimem.ld_reduce and writes
+ * the updated table shard with multimem.st, moving each shard once through the switch. */
+int ffn_bind_external(ffn_ctx* ctx, int buffer_id, void* dev_ptr, size_t bytes);
+int ffn_dp_attach_multicast(ffn_ctx* ctx, void* mc_grads, void* mc_table);
 
 /* Plain Adam over n float32 parameters (vectorised; beta/eps as given). */
 int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float beta1,

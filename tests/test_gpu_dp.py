@@ -1,6 +1,8 @@
-"""The fused data-parallel exchange (ffn_dp_reduce_apply: gradient sum over NVLink peer memory,
-table SGD on each rank's shard, broadcast of the updated table) against the NCCL path (all-reduce
-of the gradient buffer, then the table pass), on 2 GPUs.
+"""The fused data-parallel exchange (ffn_dp_reduce_apply: gradient sum across ranks, table SGD on
+each rank's shard, broadcast of the updated table) against the NCCL path (all-reduce of the
+gradient buffer, then the table pass), on 2 GPUs, in both forms: NVLink peer loads/stores ("p2p")
+and NVSwitch multicast ("nvls": multimem.ld_reduce / multimem.st on symmetric memory; skipped
+where the switch offers no multicast).
 
 Each rank holds two identical contexts and trains both for 3 steps on its half of the batch: one
 through NCCL + ffn_apply_updates, one through ffn_dp_reduce_apply + ffn_apply_updates(TABLE_APPLIED).
@@ -29,7 +31,7 @@ def _port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, mode, q):
     try:
         for p in (ROOT / "ffnerf-experimental_b200", ROOT / "tests"):
             sys.path.insert(0, str(p))
@@ -53,10 +55,29 @@ def _worker(rank, world, port, q):
             c.tensor(fn.BUF_OCC_ST).copy_(torch.from_numpy(occ.view(np.int32)))
             ctxs.append(c)
         nccl_ctx, fused_ctx = ctxs
+        mc = None
+        if mode == "nvls":
+            import torch.distributed._symmetric_memory as symm_mem
+            bufs = []
+            for bid in (fn.BUF_GRADS, fn.BUF_TABLE):
+                t = symm_mem.empty(fused_ctx.tensor(bid).numel(), dtype=torch.float32, device=f"cuda:{rank}")
+                bufs.append((t, symm_mem.rendezvous(t, dist.group.WORLD.group_name)))
+            good = torch.tensor([int(all(int(getattr(h, "multicast_ptr", 0) or 0) != 0 for _, h in bufs))], device="cuda")
+            dist.all_reduce(good, op=dist.ReduceOp.MIN)
+            if int(good.item()) == 0:
+                dist.barrier()
+                dist.destroy_process_group()
+                q.put((rank, "skip", "no multicast support"))
+                return
+            fused_ctx.bind_external(fn.BUF_GRADS, bufs[0][0])
+            fused_ctx.bind_external(fn.BUF_TABLE, bufs[1][0])
+            mc = (int(bufs[0][1].multicast_ptr), int(bufs[1][1].multicast_ptr))
         handles = fused_ctx.dp_ipc_handles()
         allh = [None] * world
         dist.all_gather_object(allh, handles)
         fused_ctx.dp_attach(rank, world, allh)
+        if mc is not None:
+            fused_ctx.dp_attach_multicast(*mc)
         n = 256
         half = n // world
         dev = torch.device("cuda", rank)
@@ -94,14 +115,15 @@ def _worker(rank, world, port, q):
         q.put((rank, "err", f"{exc}\n{traceback.format_exc()}"))
 
 
-def test_fused_exchange_matches_nccl():
+@pytest.mark.parametrize("mode", ["p2p", "nvls"])
+def test_fused_exchange_matches_nccl(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
@@ -114,6 +136,8 @@ def test_fused_exchange_matches_nccl():
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
+    if any(st == "skip" for st, _ in results.values()):
+        pytest.skip("the NVSwitch offers no multicast here")
     for rank, (st, res) in results.items():
         assert st == "ok", res
         assert res["table"] < 1e-4 and res["params"] < 1e-4, res
