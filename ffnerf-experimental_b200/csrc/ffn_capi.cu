@@ -46,6 +46,9 @@ struct ffn_ctx {
     float2* tdt_stage = nullptr;
     float4* pn_stage = nullptr;
     uint4* ray_stage = nullptr;
+    uint64_t launches = 0;         // kernels this context has launched (ffn_kernel_launches)
+    cudaStream_t side = nullptr;   // second stream of the split step (encoder of the next part)
+    cudaEvent_t ev_main = nullptr, ev_side = nullptr;
     DpState* dp = nullptr;       // data-parallel peer mappings (ffn_dp_attach)
     bool ext_table = false;      // table / gradient buffer bound from outside (ffn_bind_external)
     bool ext_grads = false;
@@ -184,6 +187,7 @@ int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) 
     if (grid_out) *grid_out = grid;
     if (grid == 0) return FFN_OK;
     c->kernel<<<grid, c->rows, c->smem, st>>>(a);
+    ++c->launches;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "fused step launch");
     return FFN_OK;
@@ -191,14 +195,20 @@ int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// The split tensor-core step over groups of at most STAGE_SAMPLES samples: sampler, encoder,
-// then the MLP/compositing/backward kernel and the fixed-order partial reduction per group.
+// The split tensor-core step over groups of at most STAGE_SAMPLES samples: the sampler of the group,
+// then its tiles in OVERLAP_PARTS parts: the encoder of part k + 1 runs on a second stream while
+// the MLP/compositing/backward kernel and the fixed-order partial reduction of part k run on the
+// caller's stream, so the encoder's L1-bound gathers overlap the MLP kernel's tensor-core and
+// compositing phases.
+constexpr int OVERLAP_PARTS = 2;
+
 int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
                             const ffn_step_scalars* s, cudaStream_t st) {
     const int spr = s->spr ? (int)s->spr : c->cfg.spr;
     const uint32_t group_rays = (uint32_t)(STAGE_SAMPLES / spr);
     const int rpt = 128 / spr;
     const int sms = c->max_grid / c->ctas_per_sm;
+    const size_t tile_bytes = (size_t)128 * 16 * c->cfg.F * 2;
     for (uint32_t r0 = 0; r0 < n; r0 += group_rays) {
         const uint32_t m = n - r0 < group_rays ? n - r0 : group_rays;
         StepArgs a = base_args(c, static_cast<const float4*>(rays) + 2 * (size_t)r0,
@@ -208,16 +218,48 @@ int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, v
         const int n_tiles = (int)((m + (uint32_t)rpt - 1) / (uint32_t)rpt);
         const int sgrid = n_tiles < sms * 8 ? n_tiles : sms * 8;
         sample_stage_kernel<<<sgrid, 128, 0, st>>>(a, c->pn_stage, c->tdt_stage, c->ray_stage);
-        const int64_t rows = (int64_t)n_tiles * 128;
-        const int64_t items = rows * L;
-        const int eblocks = (int)((items + 255) / 256 < (int64_t)sms * 16 ? (items + 255) / 256 : (int64_t)sms * 16);
-        c->encoder<<<eblocks, 256, 0, st>>>(a.c, c->table, c->pn_stage, (int64_t)m * spr, rows, c->x0_stage);
-        a.x0_stage = c->x0_stage;
-        a.tdt_stage = c->tdt_stage;
-        a.ray_stage = c->ray_stage;
-        const int grid = n_tiles < c->max_grid ? n_tiles : c->max_grid;
-        c->kernel_staged<<<grid, c->rows, c->smem, st>>>(a);
-        reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+        ++c->launches;
+        // parts only when each still fills the GPU
+        int parts = n_tiles / c->max_grid;
+        parts = parts < 1 ? 1 : (parts > OVERLAP_PARTS ? OVERLAP_PARTS : parts);
+        const int tp = (n_tiles + parts - 1) / parts;
+        auto encode = [&](int k, cudaStream_t on) {
+            const int t0 = k * tp, t1 = t0 + tp < n_tiles ? t0 + tp : n_tiles;
+            const int64_t rows = (int64_t)(t1 - t0) * 128;
+            const int64_t valid_end = (int64_t)m * spr < (int64_t)t1 * 128 ? (int64_t)m * spr : (int64_t)t1 * 128;
+            const int64_t chunks = (rows + 255) / 256 * L;
+            const int eblocks = (int)(chunks < (int64_t)sms * 16 ? chunks : (int64_t)sms * 16);
+            c->encoder<<<eblocks, 256, 0, on>>>(a.c, c->table, c->pn_stage + (size_t)t0 * 128, valid_end - (int64_t)t0 * 128,
+                                                rows, c->x0_stage + (size_t)t0 * tile_bytes);
+            ++c->launches;
+        };
+        encode(0, st);
+        for (int k = 0; k < parts; ++k) {
+            if (k + 1 < parts) {
+                cudaEventRecord(c->ev_main, st);
+                cudaStreamWaitEvent(c->side, c->ev_main, 0);
+                encode(k + 1, c->side);
+                cudaEventRecord(c->ev_side, c->side);
+            }
+            const int t0 = k * tp, t1 = t0 + tp < n_tiles ? t0 + tp : n_tiles;
+            const uint32_t q0 = (uint32_t)t0 * rpt;
+            const uint32_t q1 = (uint32_t)t1 * rpt < m ? (uint32_t)t1 * rpt : m;
+            StepArgs b = a;
+            b.rays = a.rays + 2 * (size_t)q0;
+            b.targets = a.targets + q0;
+            b.out = a.out + q0;
+            b.n_rays = q1 - q0;
+            b.ray_offset = a.ray_offset + q0;
+            b.x0_stage = c->x0_stage + (size_t)t0 * tile_bytes;
+            b.tdt_stage = c->tdt_stage + (size_t)t0 * 128;
+            b.ray_stage = c->ray_stage + q0;
+            const int grid = (t1 - t0) < c->max_grid ? (t1 - t0) : c->max_grid;
+            c->kernel_staged<<<grid, c->rows, c->smem, st>>>(b);
+            ++c->launches;
+            reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+            ++c->launches;
+            if (k + 1 < parts) cudaStreamWaitEvent(st, c->ev_side, 0);
+        }
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(c, e, "split step launch");
     }
@@ -301,6 +343,12 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
             {(void**)&c->ray_stage, (size_t)(STAGE_SAMPLES / 16) * sizeof(uint4)}};
         for (auto& al : st_allocs)
             if ((e = cudaMalloc(al.p, al.n)) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "device allocation"); }
+        if ((e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&c->ev_main, cudaEventDisableTiming)) != cudaSuccess ||
+            (e = cudaEventCreateWithFlags(&c->ev_side, cudaEventDisableTiming)) != cudaSuccess) {
+            ffn_destroy(c);
+            return cuda_fail(nullptr, e, "stream creation");
+        }
     }
     if (cfg->table_optimizer == 1) {
         if ((e = cudaMalloc((void**)&c->table_m, Tb)) != cudaSuccess || (e = cudaMalloc((void**)&c->table_v, Tb)) != cudaSuccess) {
@@ -336,6 +384,9 @@ int ffn_destroy(ffn_ctx* c) {
                     c->tdt_stage, c->pn_stage, c->ray_stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    if (c->ev_main) cudaEventDestroy(c->ev_main);
+    if (c->ev_side) cudaEventDestroy(c->ev_side);
+    if (c->side) cudaStreamDestroy(c->side);
     delete c;
     return FFN_OK;
 }
@@ -393,6 +444,7 @@ int ffn_forward_backward(ffn_ctx* c, const void* rays, const void* targets, void
     int grid = 0;
     if ((rc = launch_fused(c, a, st, &grid)) != FFN_OK) return rc;
     reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+    ++c->launches;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "gradient reduction launch");
 }
@@ -406,6 +458,7 @@ int ffn_apply_updates(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
                                                          c->adam_v, c->Pw, c->lo.off[P_WC_IN], c->lo.off[P_BD_0],
                                                          c->lo.off[P_BC_0], s->lr_t, s->color_rel_lr,
                                                          g.adam_beta1, g.adam_beta2, g.adam_eps);
+    ++c->launches;
     LevelCoef lc{};
     for (int l = 0; l < L; ++l) {
         lc.start[l] = g.level_offset[l] * (uint32_t)g.F;
@@ -417,11 +470,14 @@ int ffn_apply_updates(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
     const int blocks = (int)((n4 + 255) / 256 < 148u * 16u ? (n4 + 255) / 256 : 148u * 16u);
     if (s->flags & (FFN_STEP_TABLE_IMMEDIATE | FFN_STEP_TABLE_APPLIED)) {
         // the table was updated inside the forward/backward pass or by ffn_dp_reduce_apply
-    } else if (g.table_optimizer == 1)
+    } else if (g.table_optimizer == 1) {
         table_adam_kernel<<<blocks, 256, 0, st>>>(c->table, c->grads, c->table_m, c->table_v, n4, lc,
                                                    g.adam_beta1, g.adam_beta2, g.table_adam_eps);
-    else
+        ++c->launches;
+    } else {
         table_sgd_kernel<<<blocks, 256, 0, st>>>(c->table, c->grads, n4, lc);
+        ++c->launches;
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "update launch");
 }
@@ -467,6 +523,7 @@ int ffn_occ_st_bytes(ffn_ctx* c, uint8_t* bytes, int to_bytes, void* stream) {
     const uint32_t n = (uint32_t)c->cfg.G * c->cfg.G * c->cfg.G;
     const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
     occ_bytes_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(c->occ_st, bytes, n, to_bytes);
+    ++c->launches;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "occupancy byte conversion launch");
 }
@@ -478,6 +535,7 @@ int ffn_occ_maintenance(ffn_ctx* c, uint32_t decay_q24, uint32_t seed, void* str
     const uint32_t n = (uint32_t)c->cfg.G * c->cfg.G * c->cfg.G;
     const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
     occ_decay_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(c->occ_in, c->occ_st, n, decay_q24, seed);
+    ++c->launches;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "decay launch");
 }
@@ -493,6 +551,7 @@ int ffn_hash_encode(ffn_ctx* c, const float* pts, float* enc, int64_t n, void* s
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (c->cfg.F == 2) hash_fwd_kernel<2><<<blocks, 256, 0, st>>>(c->dc, c->table, pts, n, enc);
     else hash_fwd_kernel<4><<<blocks, 256, 0, st>>>(c->dc, c->table, pts, n, enc);
+    ++c->launches;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "hash encode launch");
 }
@@ -508,9 +567,12 @@ int ffn_hash_encode_bwd(ffn_ctx* c, const float* pts, const float* denc, int64_t
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (c->cfg.F == 2) hash_bwd_kernel<2><<<blocks, 256, 0, st>>>(c->dc, c->grads, pts, denc, n);
     else hash_bwd_kernel<4><<<blocks, 256, 0, st>>>(c->dc, c->grads, pts, denc, n);
+    ++c->launches;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "hash scatter launch");
 }
+
+uint64_t ffn_kernel_launches(const ffn_ctx* c) { return c ? c->launches : 0u; }
 
 int ffn_status(ffn_ctx* c, uint32_t* status) {
     if (!c || !status) return fail(c, FFN_E_CONFIG, "null argument");
@@ -626,16 +688,17 @@ int ffn_dp_reduce_apply(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
     const uint32_t table4 = (uint32_t)(c->table_floats / 4);
     const uint32_t total4 = (uint32_t)((c->table_floats + (size_t)c->Pw) / 4);
     const int sms = c->max_grid / c->ctas_per_sm;
+    if (!c->dp->mc_grads && (c->ext_grads || c->ext_table))
+        return fail(c, FFN_E_STATE, "externally bound buffers need ffn_dp_attach_multicast");
     const uint32_t epoch = ++c->dp->epoch;
     if (c->dp->mc_grads)
         ffn::dp_reduce_apply_nvls_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, c->dp->mc_grads, c->dp->mc_table,
                                                                   c->table, table4, total4, lc, epoch, c->status,
                                                                   c->dp->done_counter);
-    else if (c->ext_grads || c->ext_table)
-        return fail(c, FFN_E_STATE, "externally bound buffers need ffn_dp_attach_multicast");
     else
         ffn::dp_reduce_apply_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, table4, total4, lc, epoch, c->status,
                                                              c->dp->done_counter);
+    ++c->launches;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "exchange launch");
     // every rank has read this rank's table gradients: clear them for the next step

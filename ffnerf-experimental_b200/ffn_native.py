@@ -75,6 +75,7 @@ _SIGS = {
     "ffn_dp_reduce_apply": (C.c_int, [_VP, C.POINTER(FfnStep), _VP]),
     "ffn_bind_external": (C.c_int, [_VP, C.c_int, _VP, C.c_size_t]),
     "ffn_dp_attach_multicast": (C.c_int, [_VP, _VP, _VP]),
+    "ffn_kernel_launches": (C.c_uint64, [_VP]),
 }
 EXPORTED = tuple(_SIGS)
 
@@ -175,7 +176,6 @@ class Context:
         self.param_total = self.lib.ffn_param_layout(C.byref(self.cfg), off.ctypes.data, sz.ctypes.data)
         self.layout = {n: (int(o), int(s)) for n, o, s in zip(PARAM_NAMES, off, sz)}
         self._views = {}
-        self.launches = 0          # kernels this context has launched (for benchmark accounting)
 
     # -- lifetime
     def close(self):
@@ -225,28 +225,21 @@ class Context:
             return torch.cuda.current_stream().cuda_stream
         return getattr(stream, "cuda_stream", stream)
 
-    def _fb_launches(self, n_rays: int, step: FfnStep) -> int:
-        """Kernels one ffn_forward_backward launches: fused kernel + partial reduction (fp32 MLP), or
-        per group of 2^20 samples sampler + encoder + MLP kernel + reduction (tensor-core MLP)."""
-        if self.mlp_precision != "fp16" or n_rays == 0:
-            return 2 if n_rays else 0
-        spr = int(step.spr) or int(self.geom["spr"])
-        groups = -(-(int(n_rays) * spr) // STAGE_SAMPLES)
-        return 4 * groups
+    @property
+    def launches(self) -> int:
+        """Kernels this context has launched so far, as counted by the library."""
+        return int(self.lib.ffn_kernel_launches(self.h)) if getattr(self, "h", None) else 0
 
     def forward_backward(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_forward_backward(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                                   C.byref(step), self._stream(stream)), "ffn_forward_backward")
-        self.launches += self._fb_launches(n_rays, step)
 
     def apply_updates(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_apply_updates(self.h, C.byref(step), self._stream(stream)), "ffn_apply_updates")
-        self.launches += 1 if step.flags & (STEP_TABLE_IMMEDIATE | STEP_TABLE_APPLIED) else 2
 
     def train_step(self, rays, targets, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_train_step(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays),
                                             C.byref(step), self._stream(stream)), "ffn_train_step")
-        self.launches += self._fb_launches(n_rays, step) + (1 if step.flags & STEP_TABLE_IMMEDIATE else 2)
 
     # -- data-parallel exchange over NVLink peer memory
     def dp_ipc_handles(self) -> bytes:
@@ -275,39 +268,32 @@ class Context:
 
     def dp_reduce_apply(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_dp_reduce_apply(self.h, C.byref(step), self._stream(stream)), "ffn_dp_reduce_apply")
-        self.launches += 1
 
     def render(self, rays, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_render(self.h, _ptr(rays), _ptr(out), int(n_rays), C.byref(step),
                                         self._stream(stream)), "ffn_render")
-        self.launches += 1
 
     def occ_maintenance(self, decay_q24: int, seed: int, stream=None):
         self._check(self.lib.ffn_occ_maintenance(self.h, int(decay_q24), int(seed) & 0xFFFFFFFF,
                                                  self._stream(stream)), "ffn_occ_maintenance")
-        self.launches += 1
 
     def probe(self, rays, targets, out, n_rays: int, step: FfnStep, bypass=None, t=None, dt=None, idx=None,
               flags=None, sigma=None, rgb=None, trans=None, stream=None):
         self._check(self.lib.ffn_probe(self.h, _ptr(rays), _ptr(targets), _ptr(out), int(n_rays), C.byref(step),
                                        _ptr(bypass), _ptr(t), _ptr(dt), _ptr(idx), _ptr(flags), _ptr(sigma),
                                        _ptr(rgb), _ptr(trans), self._stream(stream)), "ffn_probe")
-        self.launches += 1
 
     def hash_encode(self, pts, enc, n: int, stream=None):
         self._check(self.lib.ffn_hash_encode(self.h, _ptr(pts), _ptr(enc), int(n), self._stream(stream)),
                     "ffn_hash_encode")
-        self.launches += 1
 
     def hash_encode_bwd(self, pts, denc, n: int, stream=None):
         self._check(self.lib.ffn_hash_encode_bwd(self.h, _ptr(pts), _ptr(denc), int(n), self._stream(stream)),
                     "ffn_hash_encode_bwd")
-        self.launches += 1
 
     def occ_st_bytes(self, buf, to_bytes: bool, stream=None):
         self._check(self.lib.ffn_occ_st_bytes(self.h, _ptr(buf), 1 if to_bytes else 0, self._stream(stream)),
                     "ffn_occ_st_bytes")
-        self.launches += 1
 
     def status(self) -> int:
         """Device status word since the last call (0 = every kernel completed normally)."""

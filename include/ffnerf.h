@@ -157,6 +157,8 @@ int ffn_probe(ffn_ctx* ctx, const void* rays, const void* targets, void* out, ui
 int ffn_hash_encode(ffn_ctx* ctx, const float* pts, float* enc, int64_t n, void* stream);
 int ffn_hash_encode_bwd(ffn_ctx* ctx, const float* pts, const float* denc, int64_t n,
                         void* stream);
+/* Kernels this context has launched so far (all entry points; no reference counterpart). */
+uint64_t ffn_kernel_launches(const ffn_ctx* ctx);
 /* Reads and clears the context's device status word (waits for the device): 0 when every kernel
  * since the last call completed normally; bit 2 = a tensor-core wait exceeded its bound. */
 int ffn_status(ffn_ctx* ctx, uint32_t* status);

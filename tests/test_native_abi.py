@@ -15,7 +15,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def test_header_symbols_exported():
     header = (ROOT / "include" / "ffnerf.h").read_text()
-    declared = set(re.findall(r"^\s*(?:int|const char\*)\s+(ffn_\w+)\s*\(", header, flags=re.M))
+    declared = set(re.findall(r"^\s*(?:int|uint64_t|const char\*)\s+(ffn_\w+)\s*\(", header, flags=re.M))
     assert declared, "no declarations parsed"
     lib = fn.load_library()
     for name in declared:
