@@ -47,8 +47,6 @@ struct ffn_ctx {
     float4* pn_stage = nullptr;
     uint4* ray_stage = nullptr;
     uint64_t launches = 0;         // kernels this context has launched (ffn_kernel_launches)
-    cudaStream_t side = nullptr;   // second stream of the split step (encoder of the next part)
-    cudaEvent_t ev_main = nullptr, ev_side = nullptr;
     DpState* dp = nullptr;       // data-parallel peer mappings (ffn_dp_attach)
     bool ext_table = false;      // table / gradient buffer bound from outside (ffn_bind_external)
     bool ext_grads = false;
@@ -195,20 +193,16 @@ int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// The split tensor-core step over groups of at most STAGE_SAMPLES samples: the sampler of the group,
-// then its tiles in OVERLAP_PARTS parts: the encoder of part k + 1 runs on a second stream while
-// the MLP/compositing/backward kernel and the fixed-order partial reduction of part k run on the
-// caller's stream, so the encoder's L1-bound gathers overlap the MLP kernel's tensor-core and
-// compositing phases.
-constexpr int OVERLAP_PARTS = 2;
-
+// The split tensor-core step over groups of at most STAGE_SAMPLES samples: sampler, encoder,
+// then the MLP/compositing/backward kernel and the fixed-order partial reduction per group.
+// (Running the encoder of the next half-group on a second stream beside the MLP kernel was slower:
+// its blocks hold SM resources the MLP kernel's CTAs need.)
 int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
                             const ffn_step_scalars* s, cudaStream_t st) {
     const int spr = s->spr ? (int)s->spr : c->cfg.spr;
     const uint32_t group_rays = (uint32_t)(STAGE_SAMPLES / spr);
     const int rpt = 128 / spr;
     const int sms = c->max_grid / c->ctas_per_sm;
-    const size_t tile_bytes = (size_t)128 * 16 * c->cfg.F * 2;
     for (uint32_t r0 = 0; r0 < n; r0 += group_rays) {
         const uint32_t m = n - r0 < group_rays ? n - r0 : group_rays;
         StepArgs a = base_args(c, static_cast<const float4*>(rays) + 2 * (size_t)r0,
@@ -219,47 +213,19 @@ int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, v
         const int sgrid = n_tiles < sms * 8 ? n_tiles : sms * 8;
         sample_stage_kernel<<<sgrid, 128, 0, st>>>(a, c->pn_stage, c->tdt_stage, c->ray_stage);
         ++c->launches;
-        // parts only when each still fills the GPU
-        int parts = n_tiles / c->max_grid;
-        parts = parts < 1 ? 1 : (parts > OVERLAP_PARTS ? OVERLAP_PARTS : parts);
-        const int tp = (n_tiles + parts - 1) / parts;
-        auto encode = [&](int k, cudaStream_t on) {
-            const int t0 = k * tp, t1 = t0 + tp < n_tiles ? t0 + tp : n_tiles;
-            const int64_t rows = (int64_t)(t1 - t0) * 128;
-            const int64_t valid_end = (int64_t)m * spr < (int64_t)t1 * 128 ? (int64_t)m * spr : (int64_t)t1 * 128;
-            const int64_t chunks = (rows + 255) / 256 * L;
-            const int eblocks = (int)(chunks < (int64_t)sms * 16 ? chunks : (int64_t)sms * 16);
-            c->encoder<<<eblocks, 256, 0, on>>>(a.c, c->table, c->pn_stage + (size_t)t0 * 128, valid_end - (int64_t)t0 * 128,
-                                                rows, c->x0_stage + (size_t)t0 * tile_bytes);
-            ++c->launches;
-        };
-        encode(0, st);
-        for (int k = 0; k < parts; ++k) {
-            if (k + 1 < parts) {
-                cudaEventRecord(c->ev_main, st);
-                cudaStreamWaitEvent(c->side, c->ev_main, 0);
-                encode(k + 1, c->side);
-                cudaEventRecord(c->ev_side, c->side);
-            }
-            const int t0 = k * tp, t1 = t0 + tp < n_tiles ? t0 + tp : n_tiles;
-            const uint32_t q0 = (uint32_t)t0 * rpt;
-            const uint32_t q1 = (uint32_t)t1 * rpt < m ? (uint32_t)t1 * rpt : m;
-            StepArgs b = a;
-            b.rays = a.rays + 2 * (size_t)q0;
-            b.targets = a.targets + q0;
-            b.out = a.out + q0;
-            b.n_rays = q1 - q0;
-            b.ray_offset = a.ray_offset + q0;
-            b.x0_stage = c->x0_stage + (size_t)t0 * tile_bytes;
-            b.tdt_stage = c->tdt_stage + (size_t)t0 * 128;
-            b.ray_stage = c->ray_stage + q0;
-            const int grid = (t1 - t0) < c->max_grid ? (t1 - t0) : c->max_grid;
-            c->kernel_staged<<<grid, c->rows, c->smem, st>>>(b);
-            ++c->launches;
-            reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
-            ++c->launches;
-            if (k + 1 < parts) cudaStreamWaitEvent(st, c->ev_side, 0);
-        }
+        const int64_t rows = (int64_t)n_tiles * 128;
+        const int64_t chunks = (rows + 255) / 256 * L;
+        const int eblocks = (int)(chunks < (int64_t)sms * 16 ? chunks : (int64_t)sms * 16);
+        c->encoder<<<eblocks, 256, 0, st>>>(a.c, c->table, c->pn_stage, (int64_t)m * spr, rows, c->x0_stage);
+        ++c->launches;
+        a.x0_stage = c->x0_stage;
+        a.tdt_stage = c->tdt_stage;
+        a.ray_stage = c->ray_stage;
+        const int grid = n_tiles < c->max_grid ? n_tiles : c->max_grid;
+        c->kernel_staged<<<grid, c->rows, c->smem, st>>>(a);
+        ++c->launches;
+        reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+        ++c->launches;
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(c, e, "split step launch");
     }
@@ -343,12 +309,6 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
             {(void**)&c->ray_stage, (size_t)(STAGE_SAMPLES / 16) * sizeof(uint4)}};
         for (auto& al : st_allocs)
             if ((e = cudaMalloc(al.p, al.n)) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "device allocation"); }
-        if ((e = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking)) != cudaSuccess ||
-            (e = cudaEventCreateWithFlags(&c->ev_main, cudaEventDisableTiming)) != cudaSuccess ||
-            (e = cudaEventCreateWithFlags(&c->ev_side, cudaEventDisableTiming)) != cudaSuccess) {
-            ffn_destroy(c);
-            return cuda_fail(nullptr, e, "stream creation");
-        }
     }
     if (cfg->table_optimizer == 1) {
         if ((e = cudaMalloc((void**)&c->table_m, Tb)) != cudaSuccess || (e = cudaMalloc((void**)&c->table_v, Tb)) != cudaSuccess) {
@@ -384,9 +344,6 @@ int ffn_destroy(ffn_ctx* c) {
                     c->tdt_stage, c->pn_stage, c->ray_stage};
     for (void* p : ptrs)
         if (p) cudaFree(p);
-    if (c->ev_main) cudaEventDestroy(c->ev_main);
-    if (c->ev_side) cudaEventDestroy(c->ev_side);
-    if (c->side) cudaStreamDestroy(c->side);
     delete c;
     return FFN_OK;
 }
