@@ -570,7 +570,7 @@ def main():
     achieved = bytes_launch / (fb_ms * 1e-3) / 1e9
     traffic = None
     tfile = ROOT / "profiles" / f"fused_step_{args.workload}_traffic.json"
-    if tfile.exists():
+    if tfile.exists() and world == 1 and nerf.table_immediate:   # captured on one GPU, immediate update
         t = json.loads(tfile.read_text())
         traffic = t.get("bytes_per_launch_at_samples", {}).get(str(n_loc * spr))
         if traffic is None and "bytes_per_sample" in t:
@@ -597,7 +597,9 @@ def main():
             "gpu_launches": launches,
             "host_ms_per_step": host_ms,
             "exchange_ms": ex_ms,
-            "roofline": {"bound": "hbm", "kernel": "fused_step_kernel (+ partial-gradient reduce)",
+            "roofline": {"bound": "hbm", "kernel": ("forward/backward group: sample_stage_kernel + encode_stage_kernel + "
+                                                    "fused_step_tc_kernel<staged> + reduce_partials" if args.mlp == "fp16"
+                                                    else "fused_step_kernel + reduce_partials"),
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": traffic, "peak_source": peak_kind,
                          "algorithmic_bytes_per_sample": fused_bytes_per_sample(wl["F"], spr),
