@@ -12,6 +12,7 @@
 #include "ffn_step.cu"
 #include "ffn_step_tc.cu"
 #include "ffn_dp.cu"
+#include "ffn_batch.cu"
 
 using namespace ffn;
 
@@ -530,6 +531,46 @@ int ffn_hash_encode_bwd(ffn_ctx* c, const float* pts, const float* denc, int64_t
 }
 
 uint64_t ffn_kernel_launches(const ffn_ctx* c) { return c ? c->launches : 0u; }
+
+int ffn_batch_generate(const void* images, int img_f32, int channels, const uint8_t* weights, const float* c2w,
+                       const float* K, int k_per_image, int n_img, int W, int H, uint32_t n, float uniform_frac,
+                       uint32_t seed, uint32_t max_tries, void* rays, void* targets, int32_t* im, int32_t* x,
+                       int32_t* y, void* stream) {
+    if (n == 0) return FFN_OK;
+    if (!images || !weights || !c2w || !rays || !targets) return fail(nullptr, FFN_E_CONFIG, "null argument");
+    if (n_img < 1 || W < 1 || H < 1 || channels < 3) return fail(nullptr, FFN_E_CONFIG, "need >= 1 image of >= 3 channels");
+    if ((im || x || y) && !(im && x && y)) return fail(nullptr, FFN_E_CONFIG, "im, x and y are given together");
+    if (!aligned16(rays) || !aligned16(targets)) return fail(nullptr, FFN_E_CONFIG, "rays/targets must be 16-byte aligned");
+    if (!(uniform_frac >= 0.0f && uniform_frac <= 1.0f)) return fail(nullptr, FFN_E_CONFIG, "uniform_frac must be in [0, 1]");
+    ffn::BatchGen g{images, img_f32, weights, c2w, K, k_per_image, n_img, W, H, channels, n, uniform_frac, seed, max_tries};
+    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    ffn::batch_generate_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        g, static_cast<float4*>(rays), static_cast<float4*>(targets), im, x, y);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "batch generation launch");
+}
+
+int ffn_batch_errors(const void* out, const void* targets, uint32_t n, float* err, void* stream) {
+    if (n == 0) return FFN_OK;
+    if (!out || !targets || !err) return fail(nullptr, FFN_E_CONFIG, "null argument");
+    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    ffn::batch_error_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const float4*>(out), static_cast<const float4*>(targets), n, err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "error launch");
+}
+
+int ffn_batch_feedback(uint8_t* weights, const void* images, int img_f32, int channels, int W, int H,
+                       const int32_t* im, const int32_t* x, const int32_t* y, const float* err, uint32_t n,
+                       const float* median, double ema, int bg_cap, int fg_tau, void* stream) {
+    if (n == 0) return FFN_OK;
+    if (!weights || !images || !im || !x || !y || !err || !median) return fail(nullptr, FFN_E_CONFIG, "null argument");
+    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    ffn::batch_feedback_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        weights, images, img_f32, channels, W, H, im, x, y, err, n, median, ema, bg_cap, fg_tau);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "feedback launch");
+}
 
 int ffn_status(ffn_ctx* c, uint32_t* status) {
     if (!c || !status) return fail(c, FFN_E_CONFIG, "null argument");

@@ -76,6 +76,11 @@ _SIGS = {
     "ffn_bind_external": (C.c_int, [_VP, C.c_int, _VP, C.c_size_t]),
     "ffn_dp_attach_multicast": (C.c_int, [_VP, _VP, _VP]),
     "ffn_kernel_launches": (C.c_uint64, [_VP]),
+    "ffn_batch_generate": (C.c_int, [_VP, C.c_int, C.c_int, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_uint32, C.c_float, C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "ffn_batch_errors": (C.c_int, [_VP, _VP, C.c_uint32, _VP, _VP]),
+    "ffn_batch_feedback": (C.c_int, [_VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int, _VP, _VP, _VP, _VP, C.c_uint32,
+                                     _VP, C.c_double, C.c_int, C.c_int, _VP]),
 }
 EXPORTED = tuple(_SIGS)
 

@@ -186,6 +186,27 @@ int ffn_dp_reduce_apply(ffn_ctx* ctx, const ffn_step_scalars* s, void* stream);
 int ffn_bind_external(ffn_ctx* ctx, int buffer_id, void* dev_ptr, size_t bytes);
 int ffn_dp_attach_multicast(ffn_ctx* ctx, void* mc_grads, void* mc_table);
 
+/* Training batches on the device (replace the host batch producer, run_ffnerf_OG.py:585-685, and
+ * rays_targets_from_indices, ffnerf_tools.py:175-234).  images: [n_img][H][W][channels] uint8
+ * (img_f32 = 0) or float32 in [0,1]; weights: [n_img][H][W] uint8 pixel weights (1..255); c2w:
+ * [n_img][4][4] camera-to-world; K: [3][3] (k_per_image = 0) or [n_img][3][3], or NULL for the
+ * reference's fallback focal.  Each ray takes a uniform image and, with probability uniform_frac,
+ * a uniform pixel, else a pixel by rejection against the weight map (at most max_tries proposals);
+ * rays [n][2] float4 (o, d), targets [n] float4, and optionally the drawn (im, x, y).  Rays depend
+ * only on seed and the inputs (counter-based RNG per ray). */
+int ffn_batch_generate(const void* images, int img_f32, int channels, const uint8_t* weights, const float* c2w,
+                       const float* K, int k_per_image, int n_img, int W, int H, uint32_t n_rays,
+                       float uniform_frac, uint32_t seed, uint32_t max_tries, void* rays, void* targets,
+                       int32_t* im, int32_t* x, int32_t* y, void* stream);
+/* Per-ray colour error sqrt(mean_rgb((out - targets)^2)) clipped to [0, 1] (run_ffnerf_OG.py:1383). */
+int ffn_batch_errors(const void* out, const void* targets, uint32_t n_rays, float* err, void* stream);
+/* Weight-map EMA from per-ray errors and their median (a device float), as the reference's
+ * _update_weights_u8 (run_ffnerf_OG.py:459-490) with the RGB-threshold foreground of
+ * make_fg_mask_from_rgb (run_ffnerf_OG.py:402-421, dilate = 0). */
+int ffn_batch_feedback(uint8_t* weights, const void* images, int img_f32, int channels, int W, int H,
+                       const int32_t* im, const int32_t* x, const int32_t* y, const float* err,
+                       uint32_t n_rays, const float* median, double ema, int bg_cap, int fg_tau, void* stream);
+
 /* Plain Adam over n float32 parameters (vectorised; beta/eps as given). */
 int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t, float beta1,
              float beta2, float eps, void* stream);

@@ -14,7 +14,9 @@ their host-side results are captured:
                               scalars (B, lr_t, colour lr, Adam betas/eps);
   * golden_rays.npz        -- rays_targets_from_indices / rays_from_rt_indices outputs;
   * golden_schedules.npz   -- run_ffnerf_OG's learning-rate, SH, occupancy and colour-lr
-                              schedules over a step range.
+                              schedules over a step range;
+  * golden_batch_feedback.npz -- run_ffnerf_OG's pixel-weight feedback (_update_weights_u8 with
+                              the make_fg_mask_from_rgb foreground) on small uint8 images.
 The tests compare this repository's host module against these arrays bit for bit.
 """
 from __future__ import annotations
@@ -187,6 +189,30 @@ def schedules_fixture(ref: Path):
                 color=np.array([float(run.color_MLP_rel_lr_function(s)) for s in steps]))
 
 
+def batch_fixture(ref: Path):
+    """The trainer's weight-map feedback (_update_weights_u8, run_ffnerf_OG.py:459-490) and its
+    RGB-threshold foreground (make_fg_mask_from_rgb, :402-421) on small uint8 images."""
+    for mod in ("cv2", "tqdm"):
+        importlib.import_module(mod)
+    run = importlib.import_module("run_ffnerf_OG")
+    rng = np.random.default_rng(11)
+    N, H, W = 3, 8, 12
+    Ims = rng.integers(0, 256, (N, H, W, 3), dtype=np.uint8)
+    Ims[:, :3, :4] = rng.integers(0, 9, (N, 3, 4, 3), dtype=np.uint8)   # dark (background) corner
+    weights = [rng.integers(1, 256, (H, W), dtype=np.uint8) for _ in range(N)]
+    before = np.stack(weights).copy()
+    fg = run.make_fg_mask_from_rgb(Ims, tau=8, dilate=0)
+    flat = rng.choice(N * H * W, 120, replace=False)        # distinct pixels: the update is order-free
+    im = (flat // (H * W)).astype(np.int32)
+    y = ((flat // W) % H).astype(np.int32)
+    x = (flat % W).astype(np.int32)
+    err = rng.uniform(0.0, 0.6, flat.size).astype(np.float32)
+    err[:7] = 0.0
+    run._update_weights_u8(weights, fg, im, x, y, err, ema=0.05, bg_cap=16)
+    return dict(Ims=Ims, w_before=before, w_after=np.stack(weights), fg=np.stack(fg), im=im, x=x, y=y, err=err,
+                median=np.float32(np.median(err)))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description="golden fixtures from the reference host code")
     ap.add_argument("--reference", type=Path, required=True)
@@ -200,6 +226,7 @@ def main(argv=None):
     np.savez_compressed(OUT / "golden_host_steps.npz", **steps)
     np.savez_compressed(OUT / "golden_rays.npz", **rays_fixture(ft))
     np.savez_compressed(OUT / "golden_schedules.npz", **schedules_fixture(a.reference))
+    np.savez_compressed(OUT / "golden_batch_feedback.npz", **batch_fixture(a.reference))
     print("wrote", sorted(p.name for p in OUT.glob("golden_*.npz")))
 
 
