@@ -5,9 +5,10 @@ Contracts:
   * rays and targets of the drawn (image, x, y) equal rays_targets_from_indices (the host mirror,
     pinned bit for bit to the reference by golden_rays.npz) within 2 ulp-scale (abs 1e-6) on the
     direction, exactly on origin and colour; K given, per-image K and the no-K fallback;
-  * the rejection draw follows the weight map: with weight 255 on 1/16 of the pixels and 1
-    elsewhere, 255/270 of the weighted draws land there (+-0.01); uniform draws cover pixels and
-    images evenly (+-0.01);
+  * the rejection draw follows the weight map: a proposal is accepted when a uniform byte is <= its
+    weight, i.e. with probability (w + 1) / 256, so with weight 255 on 1/16 of the pixels and 1
+    elsewhere 16 / (16 + 15/8) = 0.895 of the weighted draws land there (+-0.01); uniform draws cover
+    pixels and images evenly (+-0.01);
   * a batch depends only on its seed and inputs (two producers with one seed agree bit for bit);
   * the weight-map feedback reproduces the reference's _update_weights_u8 bit for bit on the
     golden fixture (distinct pixels), including the background cap and the median scale.
@@ -83,7 +84,7 @@ def test_rejection_follows_weights():
     torch.cuda.synchronize()
     x, y, im = prod.x.cpu().numpy(), prod.y.cpu().numpy(), prod.im.cpu().numpy()
     hot = np.mean((x < 16) & (y < 16))
-    assert abs(hot - 255.0 / 270.0) < 0.01, hot
+    assert abs(hot - 16.0 / (16.0 + 15.0 / 8.0)) < 0.01, hot
     assert np.all(np.abs(np.bincount(im, minlength=N) / n - 1.0 / N) < 0.01)
     uni = bg.GpuBatchProducer(Ims, c2w, None, W, H, batch_rays=n, rng_seed=4, uniform_frac=1.0)
     uni.weights.copy_(prod.weights)
