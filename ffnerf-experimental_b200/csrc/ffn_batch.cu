@@ -86,6 +86,43 @@ __global__ void __launch_bounds__(256) batch_generate_kernel(const BatchGen g, f
     }
 }
 
+// Rays through pixels first .. first + n - 1 of a W x H view in row-major order (x fastest): the
+// view rays of the reference's renderer (rays_from_rt_indices, ffnerf_tools.py:237-272) with the
+// same pinhole arithmetic as batch_generate_kernel.
+struct ViewCam {
+    float c2w[16];
+    float k[9];
+    int has_k;
+    int W, H;
+};
+
+__global__ void __launch_bounds__(256) camera_rays_kernel(const ViewCam v, uint32_t first, uint32_t n,
+                                                          float4* __restrict__ rays) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const uint32_t p = first + i;
+        const int x = (int)(p % (uint32_t)v.W), y = (int)(p / (uint32_t)v.W);
+        float cx_, cy_, cz_;
+        if (v.has_k) {
+            cx_ = __fdiv_rn(__fsub_rn(__fadd_rn((float)x, 0.5f), v.k[2]), v.k[0]);
+            cy_ = __fdiv_rn(__fsub_rn(__fadd_rn((float)y, 0.5f), v.k[5]), v.k[4]);
+            cz_ = 1.0f;
+        } else {
+            cx_ = __fadd_rn(__fsub_rn((float)x, (float)v.W * 0.5f), 0.5f);
+            cy_ = __fadd_rn(__fsub_rn((float)y, (float)v.H * 0.5f), 0.5f);
+            cz_ = __fsqrt_rn((float)v.H * (float)v.W);
+        }
+        float d[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+            d[r] = __fadd_rn(__fadd_rn(__fmul_rn(v.c2w[4 * r], cx_), __fmul_rn(v.c2w[4 * r + 1], cy_)),
+                             __fmul_rn(v.c2w[4 * r + 2], cz_));
+        const float nrm = __fadd_rn(__fsqrt_rn(__fadd_rn(__fadd_rn(__fmul_rn(d[0], d[0]), __fmul_rn(d[1], d[1])),
+                                                         __fmul_rn(d[2], d[2]))), 1e-12f);
+        rays[2 * (size_t)i] = make_float4(v.c2w[3], v.c2w[7], v.c2w[11], 1.0f);
+        rays[2 * (size_t)i + 1] = make_float4(__fdiv_rn(d[0], nrm), __fdiv_rn(d[1], nrm), __fdiv_rn(d[2], nrm), 0.0f);
+    }
+}
+
 // Per-ray colour error sqrt(mean_rgb((out - target)^2)) clipped to [0, 1]
 // (run_ffnerf_OG.py:1383).
 __global__ void batch_error_kernel(const float4* __restrict__ out, const float4* __restrict__ targets, uint32_t n,

@@ -550,6 +550,25 @@ int ffn_batch_generate(const void* images, int img_f32, int channels, const uint
     return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "batch generation launch");
 }
 
+int ffn_camera_rays(const float* c2w, const float* K, int W, int H, uint32_t first, uint32_t n, void* rays,
+                    void* stream) {
+    if (n == 0) return FFN_OK;
+    if (!c2w || !rays) return fail(nullptr, FFN_E_CONFIG, "null argument");
+    if (W < 1 || H < 1 || (uint64_t)first + n > (uint64_t)W * (uint64_t)H)
+        return fail(nullptr, FFN_E_CONFIG, "pixel range outside the view");
+    if (!aligned16(rays)) return fail(nullptr, FFN_E_CONFIG, "rays must be 16-byte aligned");
+    ffn::ViewCam v{};
+    std::memcpy(v.c2w, c2w, sizeof(v.c2w));
+    if (K) std::memcpy(v.k, K, sizeof(v.k));
+    v.has_k = K != nullptr;
+    v.W = W;
+    v.H = H;
+    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    ffn::camera_rays_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(v, first, n, static_cast<float4*>(rays));
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "camera rays launch");
+}
+
 int ffn_batch_errors(const void* out, const void* targets, uint32_t n, float* err, void* stream) {
     if (n == 0) return FFN_OK;
     if (!out || !targets || !err) return fail(nullptr, FFN_E_CONFIG, "null argument");

@@ -79,6 +79,7 @@ _SIGS = {
     "ffn_batch_generate": (C.c_int, [_VP, C.c_int, C.c_int, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_uint32, C.c_float, C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP, _VP, _VP]),
     "ffn_batch_errors": (C.c_int, [_VP, _VP, C.c_uint32, _VP, _VP]),
+    "ffn_camera_rays": (C.c_int, [_VP, _VP, C.c_int, C.c_int, C.c_uint32, C.c_uint32, _VP, _VP]),
     "ffn_batch_feedback": (C.c_int, [_VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int, _VP, _VP, _VP, _VP, C.c_uint32,
                                      _VP, C.c_double, C.c_int, C.c_int, _VP]),
 }

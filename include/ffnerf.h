@@ -198,6 +198,11 @@ int ffn_batch_generate(const void* images, int img_f32, int channels, const uint
                        const float* K, int k_per_image, int n_img, int W, int H, uint32_t n_rays,
                        float uniform_frac, uint32_t seed, uint32_t max_tries, void* rays, void* targets,
                        int32_t* im, int32_t* x, int32_t* y, void* stream);
+/* Rays of a view for pixels first .. first + n_rays - 1 (row-major, x fastest), written to device
+ * memory [n_rays][2] float4: the renderer's rays_from_rt_indices (ffnerf_tools.py:237-272).  c2w
+ * (4x4 row-major) and K (3x3, or NULL for the fallback focal) are HOST arrays. */
+int ffn_camera_rays(const float* c2w, const float* K, int W, int H, uint32_t first, uint32_t n_rays, void* rays,
+                    void* stream);
 /* Per-ray colour error sqrt(mean_rgb((out - targets)^2)) clipped to [0, 1] (run_ffnerf_OG.py:1383). */
 int ffn_batch_errors(const void* out, const void* targets, uint32_t n_rays, float* err, void* stream);
 /* Weight-map EMA from per-ray errors and their median (a device float), as the reference's
