@@ -258,6 +258,21 @@ def rays_from_rt_indices(RT, idx, idy, W, H, K=None):
     return rays
 
 
+def _write_npz(path: Path, payload: dict, level: int = 1):
+    """An .npz archive (a zip of .npy members, deflate) readable by np.load like the reference's
+    np.savez_compressed output, written with deflate level 1 (several times faster than savez_compressed's
+    default on table data) to a temporary name and renamed into place, so a reader never sees a
+    half-written checkpoint."""
+    import zipfile
+    path = Path(path)
+    tmp = path.with_name(path.name + ".tmp")
+    with zipfile.ZipFile(tmp, "w", compression=zipfile.ZIP_DEFLATED, compresslevel=level) as zf:
+        for key, val in payload.items():
+            with zf.open(key + ".npy", "w", force_zip64=True) as f:
+                np.lib.format.write_array(f, np.asanyarray(val), allow_pickle=False)
+    os.replace(tmp, path)
+
+
 # ---------------------------------------------------------------------------- IO bundle
 @dataclass
 class RayBatch:
@@ -792,15 +807,20 @@ class Nerf:
         td.mkdir(parents=True, exist_ok=True)
         return td / f"{save_id}_weights_latest.npz", sorted(td.glob(f"{save_id}_weights_*.npz"))
 
-    def save(self, min_new_file_seconds: int = 300) -> Path:
+    def save(self, min_new_file_seconds: int = 300, async_write: bool = False):
         """Device -> host, then the reference's NPZ layout (ffnerf_tools.py:989-1086): a new
         timestamped file (also copied to ``_latest``) or, within min_new_file_seconds of the last
-        one, an overwrite of ``_latest``.  Under data parallelism only rank 0 writes."""
+        one, an overwrite of ``_latest``.  Under data parallelism only rank 0 writes.
+
+        ``async_write``: the device state is copied inside the queue's stream order into a device
+        snapshot (a few hundred microseconds for a 67 MB table), read back on a side stream into
+        pinned memory and written by a background thread, so training continues meanwhile; returns
+        the path the thread will write (``wait_saved()`` joins it)."""
         self.steps_trained = int(self.steps_trained)
         self.meta = self._build_meta()
-        if self.native is not None:
-            self.sync_params_from_device()
         if self.dp is not None and self.dp.rank != 0:
+            if self.native is not None and not async_write:
+                self.sync_params_from_device()
             return None
         latest, _ = self._model_paths(self.model_id)
         make_new = True
@@ -811,8 +831,73 @@ class Nerf:
                 make_new = True
         ts = datetime.now().strftime("%Y%m%d-%H%M%S")
         fname = (self.training_dir / f"{self.model_id}_weights_{ts}.npz") if make_new else latest
+        targets = [fname] + ([latest] if make_new else [])
+        if async_write and self.native is not None:
+            self.wait_saved()
+            grab = self._snapshot_device_async()
+            steps = self.steps_trained
+
+            def work():
+                grab()
+                payload = self._payload(ts, steps)
+                for t in targets:
+                    _write_npz(t, payload)
+            import threading
+            self._save_thread = threading.Thread(target=work, name="ffn-save", daemon=False)
+            self._save_thread.start()
+            return fname
+        if self.native is not None:
+            self.sync_params_from_device()
+        payload = self._payload(ts, self.steps_trained)
+        for t in targets:
+            _write_npz(t, payload)
+        return fname
+
+    def wait_saved(self):
+        """Waits for an asynchronous save to finish writing."""
+        t = getattr(self, "_save_thread", None)
+        if t is not None:
+            t.join()
+            self._save_thread = None
+
+    def _snapshot_device_async(self):
+        """Copies the device state to a device snapshot in stream order and starts its read-back
+        into pinned host memory on a side stream; returns a callable that waits for the read-back
+        and moves it into state_i32."""
+        import torch
+        nat = self.native
+        ids = (ffn_native.BUF_TABLE, ffn_native.BUF_PARAMS, ffn_native.BUF_ADAM_M, ffn_native.BUF_ADAM_V,
+               ffn_native.BUF_OCC_IN, ffn_native.BUF_OCC_ST)
+        if getattr(self, "_snap_dev", None) is None:
+            self._snap_dev = {i: torch.empty_like(nat.tensor(i)) for i in ids}
+            self._snap_host = {i: torch.empty(nat.tensor(i).shape, dtype=nat.tensor(i).dtype).pin_memory() for i in ids}
+            self._snap_stream = torch.cuda.Stream(device=f"cuda:{nat.device}")
+        with torch.cuda.stream(self.queue.stream):
+            for i in ids:
+                self._snap_dev[i].copy_(nat.tensor(i), non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.queue.stream)
+        self._snap_stream.wait_event(ev)
+        with torch.cuda.stream(self._snap_stream):
+            for i in ids:
+                self._snap_host[i].copy_(self._snap_dev[i], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(self._snap_stream)
+
+        def grab():
+            done.synchronize()
+            h = {i: self._snap_host[i].numpy() for i in ids}
+            self.state_i32["table"] = h[ffn_native.BUF_TABLE].view(np.int32).copy()
+            self._state_from_blob(h[ffn_native.BUF_PARAMS])
+            self._state_from_blob(h[ffn_native.BUF_ADAM_M], "m")
+            self._state_from_blob(h[ffn_native.BUF_ADAM_V], "v")
+            self.state_i32["occ_grid_in_u32"] = h[ffn_native.BUF_OCC_IN].copy()
+            self.state_i32["occ_grid_st_u32"] = h[ffn_native.BUF_OCC_ST].copy()
+        return grab
+
+    def _payload(self, ts: str, steps_trained: int) -> dict:
         payload = dict(
-            timestamp=ts, model_id=self.model_id, steps_trained=np.int32(self.steps_trained),
+            timestamp=ts, model_id=self.model_id, steps_trained=np.int32(steps_trained),
             transfer_fmt=np.array(self.transfer_fmt), ND=np.int32(self.ND), NC=np.int32(self.NC),
             table_i=np.asarray(self.state_i32["table"], dtype=np.int32),
             table_size_entries=np.int32(self.table_size_entries), table_f_per_level=np.int32(self.f_per_level),
@@ -832,10 +917,7 @@ class Nerf:
             payload[name + "_i"] = np.asarray(self.state_i32[name], dtype=np.int32)
             payload["m" + name + "_i"] = np.asarray(self.state_i32["m" + name], dtype=np.int32)
             payload["v" + name + "_i"] = np.asarray(self.state_i32["v" + name], dtype=np.int32)
-        np.savez_compressed(fname, **payload)
-        if make_new:
-            np.savez_compressed(latest, **payload)
-        return fname
+        return payload
 
     def load_latest(self, load_id: str):
         """Loads the most recently modified checkpoint of ``load_id`` (ffnerf_tools.py:1088-1172)."""
