@@ -30,6 +30,19 @@ def median_like_numpy(x):
     return ((s[n // 2 - 1] + s[n // 2]) / 2).reshape(1)
 
 
+def batch_metrics(out, targets, n: int, stream=None):
+    """The trainer's periodic loss figures (run_ffnerf_OG.py:1389-1391) for one batch, computed on
+    the device without a host round trip: a CUDA float64 tensor [mse, rmse, l2]."""
+    import torch
+    lib = ffn_native.load_library()
+    s = torch.zeros(1, dtype=torch.float64, device=out.device)
+    rc = lib.ffn_batch_errors(_ptr(out), _ptr(targets), int(n), None, _ptr(s), ffn_native.Context._stream(stream))
+    if rc != 0:
+        raise RuntimeError(f"ffn_batch_errors failed ({rc}): {lib.ffn_last_error(None).decode()}")
+    mse = s / (3.0 * n)
+    return torch.cat([mse, mse.sqrt(), (s / n).sqrt()])
+
+
 class GpuBatchProducer:
     """Draws batches of ``batch_rays`` rays from ``Ims`` ([N, H, W, >=3] uint8 or float32 in [0, 1]),
     ``RTs`` ([N, 4, 4] camera-to-world) and ``K`` ([3, 3], [N, 3, 3] or None), with the reference's
@@ -95,7 +108,7 @@ class GpuBatchProducer:
         its ``targets``: per-ray error, its median (as np.median), then the EMA."""
         n = self.batch_rays
         st = ffn_native.Context._stream(stream)
-        self._check(self.lib.ffn_batch_errors(_ptr(out), _ptr(targets), n, _ptr(self.err), st), "ffn_batch_errors")
+        self._check(self.lib.ffn_batch_errors(_ptr(out), _ptr(targets), n, _ptr(self.err), None, st), "ffn_batch_errors")
         self.apply_errors(stream)
 
     def apply_errors(self, stream=None):

@@ -123,15 +123,31 @@ __global__ void __launch_bounds__(256) camera_rays_kernel(const ViewCam v, uint3
     }
 }
 
-// Per-ray colour error sqrt(mean_rgb((out - target)^2)) clipped to [0, 1]
-// (run_ffnerf_OG.py:1383).
-__global__ void batch_error_kernel(const float4* __restrict__ out, const float4* __restrict__ targets, uint32_t n,
-                                   float* __restrict__ err) {
+// Per-ray colour error sqrt(mean_rgb((out - target)^2)) clipped to [0, 1] (run_ffnerf_OG.py:1383),
+// and optionally the batch's sum of squared colour differences (double, one atomic add per block),
+// from which the trainer's periodic metrics follow: mse = S / (3 n), rmse = sqrt(mse),
+// l2 = sqrt(S / n) (run_ffnerf_OG.py:1389-1391).
+__global__ void __launch_bounds__(256) batch_error_kernel(const float4* __restrict__ out,
+                                                          const float4* __restrict__ targets, uint32_t n,
+                                                          float* __restrict__ err, double* __restrict__ sum_sq) {
+    __shared__ double part[8];
+    double acc = 0.0;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float4 o = out[i], t = targets[i];
         const float a = __fsub_rn(o.x, t.x), b = __fsub_rn(o.y, t.y), c = __fsub_rn(o.z, t.z);
-        const float msq = __fdiv_rn(__fadd_rn(__fadd_rn(__fmul_rn(a, a), __fmul_rn(b, b)), __fmul_rn(c, c)), 3.0f);
-        err[i] = fminf(fmaxf(__fsqrt_rn(msq), 0.0f), 1.0f);
+        const float ss = __fadd_rn(__fadd_rn(__fmul_rn(a, a), __fmul_rn(b, b)), __fmul_rn(c, c));
+        if (err) err[i] = fminf(fmaxf(__fsqrt_rn(__fdiv_rn(ss, 3.0f)), 0.0f), 1.0f);
+        acc += (double)ss;
+    }
+    if (!sum_sq) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += part[w];
+        atomicAdd(sum_sq, s);
     }
 }
 

@@ -569,12 +569,13 @@ int ffn_camera_rays(const float* c2w, const float* K, int W, int H, uint32_t fir
     return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "camera rays launch");
 }
 
-int ffn_batch_errors(const void* out, const void* targets, uint32_t n, float* err, void* stream) {
+int ffn_batch_errors(const void* out, const void* targets, uint32_t n, float* err, double* sum_sq, void* stream) {
     if (n == 0) return FFN_OK;
-    if (!out || !targets || !err) return fail(nullptr, FFN_E_CONFIG, "null argument");
+    if (!out || !targets || (!err && !sum_sq)) return fail(nullptr, FFN_E_CONFIG, "null argument");
+    if (!aligned16(out) || !aligned16(targets)) return fail(nullptr, FFN_E_CONFIG, "out/targets must be 16-byte aligned");
     const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
     ffn::batch_error_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const float4*>(out), static_cast<const float4*>(targets), n, err);
+        static_cast<const float4*>(out), static_cast<const float4*>(targets), n, err, sum_sq);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "error launch");
 }

@@ -46,7 +46,7 @@ class FfnStep(C.Structure):
 STEP_TABLE_IMMEDIATE = 1
 STEP_TABLE_APPLIED = 2
 STAGE_SAMPLES = 1 << 20   # samples per group of the split tensor-core step (ffn_capi.cu)
-ABI_VERSION = 2          # include/ffnerf.h FFN_ABI_VERSION
+ABI_VERSION = 3          # include/ffnerf.h FFN_ABI_VERSION
 
 
 _VP = C.c_void_p
@@ -78,7 +78,7 @@ _SIGS = {
     "ffn_kernel_launches": (C.c_uint64, [_VP]),
     "ffn_batch_generate": (C.c_int, [_VP, C.c_int, C.c_int, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_uint32, C.c_float, C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP, _VP, _VP]),
-    "ffn_batch_errors": (C.c_int, [_VP, _VP, C.c_uint32, _VP, _VP]),
+    "ffn_batch_errors": (C.c_int, [_VP, _VP, C.c_uint32, _VP, _VP, _VP]),
     "ffn_camera_rays": (C.c_int, [_VP, _VP, C.c_int, C.c_int, C.c_uint32, C.c_uint32, _VP, _VP]),
     "ffn_batch_feedback": (C.c_int, [_VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int, _VP, _VP, _VP, _VP, C.c_uint32,
                                      _VP, C.c_double, C.c_int, C.c_int, _VP]),

@@ -38,7 +38,7 @@ extern "C" {
 #endif
 
 #define FFN_N_LEVELS 16
-#define FFN_ABI_VERSION 2   /* 2: ffn_step_scalars.flags */
+#define FFN_ABI_VERSION 3   /* 2: ffn_step_scalars.flags; 3: batch/exchange entry points */
 
 enum {
     FFN_OK = 0,
@@ -203,8 +203,12 @@ int ffn_batch_generate(const void* images, int img_f32, int channels, const uint
  * (4x4 row-major) and K (3x3, or NULL for the fallback focal) are HOST arrays. */
 int ffn_camera_rays(const float* c2w, const float* K, int W, int H, uint32_t first, uint32_t n_rays, void* rays,
                     void* stream);
-/* Per-ray colour error sqrt(mean_rgb((out - targets)^2)) clipped to [0, 1] (run_ffnerf_OG.py:1383). */
-int ffn_batch_errors(const void* out, const void* targets, uint32_t n_rays, float* err, void* stream);
+/* Per-ray colour error sqrt(mean_rgb((out - targets)^2)) clipped to [0, 1] (run_ffnerf_OG.py:1383)
+ * into err (may be NULL), and, when sum_sq is given, adds the batch's sum S of squared colour
+ * differences to *sum_sq (a device double): mse = S / (3 n), l2 = sqrt(S / n)
+ * (run_ffnerf_OG.py:1389-1391). */
+int ffn_batch_errors(const void* out, const void* targets, uint32_t n_rays, float* err, double* sum_sq,
+                     void* stream);
 /* Weight-map EMA from per-ray errors and their median (a device float), as the reference's
  * _update_weights_u8 (run_ffnerf_OG.py:459-490) with the RGB-threshold foreground of
  * make_fg_mask_from_rgb (run_ffnerf_OG.py:402-421, dilate = 0). */

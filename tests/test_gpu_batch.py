@@ -11,7 +11,8 @@ Contracts:
     pixels and images evenly (+-0.01);
   * a batch depends only on its seed and inputs (two producers with one seed agree bit for bit);
   * the weight-map feedback reproduces the reference's _update_weights_u8 bit for bit on the
-    golden fixture (distinct pixels), including the background cap and the median scale.
+    golden fixture (distinct pixels), including the background cap and the median scale;
+  * the device loss figures (mse, rmse, l2) equal the trainer's formulas within 1e-6 relative.
 """
 from pathlib import Path
 
@@ -114,6 +115,18 @@ def test_feedback_matches_reference_update():
     tg = torch.zeros((n, 4), device="cuda")
     out = tg.clone()
     out[:, :3] = torch.from_numpy(g["err"]).cuda()[:, None]
-    prod.lib.ffn_batch_errors(bg._ptr(out), bg._ptr(tg), n, bg._ptr(prod.err), None)
+    prod.lib.ffn_batch_errors(bg._ptr(out), bg._ptr(tg), n, bg._ptr(prod.err), None, None)
     torch.cuda.synchronize()
     assert torch.allclose(prod.err.cpu(), torch.from_numpy(g["err"]), rtol=1e-6, atol=0)
+
+
+def test_batch_metrics_match_trainer_formulas():
+    rng = np.random.default_rng(4)
+    n = 100003
+    pred = rng.random((n, 4), dtype=np.float32)
+    targ = rng.random((n, 4), dtype=np.float32)
+    m = bg.batch_metrics(torch.from_numpy(pred).cuda(), torch.from_numpy(targ).cuda(), n).cpu().numpy()
+    d = pred[:, :3].astype(np.float64) - targ[:, :3]
+    mse = np.mean(d ** 2)
+    ref = [mse, np.sqrt(mse), np.sqrt(np.mean(np.sum(d ** 2, axis=1)))]
+    np.testing.assert_allclose(m, ref, rtol=1e-6)
