@@ -19,7 +19,9 @@ import ffn_native
 def render_frame(nerf, c2w, K, W: int, H: int, chunk_rays: int = 1 << 16, rng_u32: int = 0, stream=None):
     """Renders the W x H view of camera-to-world ``c2w`` (4x4) with intrinsics ``K`` (3x3 or None:
     the reference's fallback focal) and returns the [H, W, 3] float32 colours as a CUDA tensor.
-    Ray i of the view (row-major) keys its sampling RNG with global ray id i."""
+    Ray i of the view (row-major) keys its sampling RNG with global ray id i.  The work runs on
+    ``stream`` (default: the model's queue); torch's current stream is made to wait for it, so the
+    returned tensor can be used there directly."""
     import torch
     if nerf.native is None:
         nerf.setup_buffers(min(int(chunk_rays), W * H), nerf.samples_per_ray if getattr(nerf, "samples_per_ray", None)
@@ -44,6 +46,10 @@ def render_frame(nerf, c2w, K, W: int, H: int, chunk_rays: int = 1 << 16, rng_u3
             raise RuntimeError(f"ffn_camera_rays failed ({rc}): {lib.ffn_last_error(None).decode()}")
         step = ffn_native.make_step(sh_mult=1.0, rng_u32=int(rng_u32), ray_offset=first, spr=nerf.samples_per_ray)
         nat.render(rays, frame[first:first + n], n, step, st)
+    if isinstance(st, torch.cuda.Stream):
+        torch.cuda.current_stream(dev).wait_stream(st)
+    else:
+        torch.cuda.synchronize(dev)
     return frame[:, :3].reshape(H, W, 3)
 
 

@@ -112,7 +112,22 @@ def synthetic_run(workload: str = "cfg1", steps: int = 3000, mlp_precision: str 
                    verbose=False)
     prod = GpuBatchProducer(images, cams, K, wl["W"], wl["H"], batch_rays=512, rng_seed=seed)
     cfg = TrainConfig(steps=steps, batch_rays=512, samples_per_ray=64, period=100, log=log, rng_seed=seed)
-    return nerf, train(nerf, prod, cfg)
+    hist = train(nerf, prod, cfg)
+    return nerf, hist, (images, cams, K, wl["W"], wl["H"])
+
+
+def evaluate_psnr(nerf, images, cams, K, W: int, H: int) -> float:
+    """PSNR (dB) of the model's renders of the training views against the 8-bit images, over all
+    pixels of all views (inference rule, black background; render_gpu.render_frame)."""
+    import torch
+    from render_gpu import render_frame
+    se, count = 0.0, 0
+    for i, c in enumerate(cams):
+        frame = render_frame(nerf, c, K, W, H, rng_u32=i)
+        ref = torch.from_numpy(images[i].astype(np.float32) / 255.0).to(frame.device)
+        se += float(((frame.clamp(0, 1) - ref) ** 2).sum())
+        count += frame.numel()
+    return -10.0 * np.log10(max(se / count, 1e-12))
 
 
 def main(argv=None):
@@ -124,8 +139,9 @@ def main(argv=None):
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
     t = time.time()
-    _, hist = synthetic_run(a.workload, a.steps, a.mlp, a.seed)
-    print(f"{a.steps} steps in {time.time() - t:.1f} s; final mse {hist[-1][1]:.5f}")
+    nerf, hist, data = synthetic_run(a.workload, a.steps, a.mlp, a.seed)
+    print(f"{a.steps} steps in {time.time() - t:.1f} s; final batch mse {hist[-1][1]:.5f}; "
+          f"PSNR of the training views {evaluate_psnr(nerf, *data):.2f} dB")
 
 
 if __name__ == "__main__":
