@@ -194,41 +194,51 @@ def default_ray_dtype() -> np.dtype:
     return ray_dtype
 
 
+def _pixel_dirs_cam(u: np.ndarray, v: np.ndarray, W: int, H: int, fx=None, fy=None, cx=None, cy=None) -> np.ndarray:
+    """Camera-frame direction (OpenCV: x right, y down, z forward) through each pixel centre, float32:
+    ((u + 0.5 - cx) / fx, (v + 0.5 - cy) / fy, 1) with intrinsics, else the reference's fallback
+    (u - W/2 + 0.5, v - H/2 + 0.5, sqrt(H W)).  The operation order is the reference's: it decides
+    the float32 rounding the golden fixtures pin."""
+    uf = np.asarray(u).astype(np.float32)
+    vf = np.asarray(v).astype(np.float32)
+    if fx is None:
+        return np.stack([uf - W / 2.0 + 0.5, vf - H / 2.0 + 0.5, np.full(uf.size, np.sqrt(H * W), dtype=np.float32)], 1)
+    return np.stack([(uf + 0.5 - cx) / fx, (vf + 0.5 - cy) / fy, np.ones(uf.size, dtype=np.float32)], 1)
+
+
+def _pack_rays(origins: np.ndarray, dirs: np.ndarray) -> np.ndarray:
+    """Unit directions (d / (|d| + 1e-12) in float32) and origins into the 32-byte Ray records."""
+    norm = np.linalg.norm(dirs, axis=1, keepdims=True).astype(np.float32)
+    out = np.zeros((dirs.shape[0],), dtype=ray_dtype)
+    out["o"][:, :3] = origins
+    out["o"][:, 3] = 1.0
+    out["d"][:, :3] = dirs / (norm + 1e-12)
+    return out
+
+
 def rays_targets_from_indices(im_idx, u_idx, v_idx, Ims, c2w_all, W, H, K=None):
     """Rays through pixels (u right, v down) of the given images and their colours
-    (ffnerf_tools.py:175-234): OpenCV camera axes, unit directions, origin w = 1."""
+    (ffnerf_tools.py:175-234): one camera-to-world pose per ray, K shared ([3,3]), per image
+    ([N,3,3]) or None; colours of uint8 images are divided by 255."""
     im_idx = np.asarray(im_idx, dtype=np.int32)
     u_idx = np.asarray(u_idx, dtype=np.int32)
     v_idx = np.asarray(v_idx, dtype=np.int32)
-    n = im_idx.size
     assert Ims.ndim == 4 and Ims.shape[1] == H and Ims.shape[2] == W, (Ims.shape, H, W)
     assert c2w_all.shape[0] == Ims.shape[0]
-    uf = u_idx.astype(np.float32)
-    vf = v_idx.astype(np.float32)
-    if K is not None:
-        if K.ndim == 2:
-            fx, fy, cx, cy = float(K[0, 0]), float(K[1, 1]), float(K[0, 2]), float(K[1, 2])
-        else:
-            Ki = K[im_idx].astype(np.float32)
-            fx, fy, cx, cy = Ki[:, 0, 0], Ki[:, 1, 1], Ki[:, 0, 2], Ki[:, 1, 2]
-        cam = np.stack([(uf + 0.5 - cx) / fx, (vf + 0.5 - cy) / fy, np.ones((n,), np.float32)], axis=1)
+    if K is None:
+        cam = _pixel_dirs_cam(u_idx, v_idx, W, H)
+    elif K.ndim == 2:
+        cam = _pixel_dirs_cam(u_idx, v_idx, W, H, float(K[0, 0]), float(K[1, 1]), float(K[0, 2]), float(K[1, 2]))
     else:
-        cam = np.stack([uf - (W / 2.0) + 0.5, vf - (H / 2.0) + 0.5,
-                        np.full((n,), np.sqrt(H * W), dtype=np.float32)], axis=1)
-    R = c2w_all[im_idx, :3, :3].astype(np.float32)
-    t = c2w_all[im_idx, :3, 3].astype(np.float32)
-    d = np.einsum("nij,nj->ni", R, cam)
-    d /= (np.linalg.norm(d, axis=1, keepdims=True) + 1e-12).astype(np.float32)
-    rays = np.zeros((n,), dtype=ray_dtype)
-    rays["o"][:, :3] = t
-    rays["o"][:, 3] = 1.0
-    rays["d"][:, :3] = d
-    rays["d"][:, 3] = 0.0
+        Kr = K[im_idx].astype(np.float32)
+        cam = _pixel_dirs_cam(u_idx, v_idx, W, H, Kr[:, 0, 0], Kr[:, 1, 1], Kr[:, 0, 2], Kr[:, 1, 2])
+    pose = c2w_all[im_idx].astype(np.float32)
+    # per-ray rotation as the reference computes it (a batched einsum; its summation order matters)
+    dirs = np.einsum("nij,nj->ni", pose[:, :3, :3], cam)
+    rays = _pack_rays(pose[:, :3, 3], dirs)
     rgb = Ims[im_idx, v_idx, u_idx, :3]
-    if rgb.dtype != np.float32:
-        rgb = rgb.astype(np.float32) / 255.0
-    targets = np.zeros((n, 4), dtype=np.float32)
-    targets[:, :3] = rgb
+    targets = np.zeros((im_idx.size, 4), dtype=np.float32)
+    targets[:, :3] = rgb if rgb.dtype == np.float32 else rgb.astype(np.float32) / 255.0
     return rays, targets
 
 
@@ -241,21 +251,13 @@ def rays_from_rt_indices(RT, idx, idy, W, H, K=None):
     idy = np.asarray(idy, dtype=np.int32).reshape(-1)
     if idx.size != idy.size:
         raise ValueError("idx and idy must have the same length.")
-    n = idx.size
     if K is None:
-        cam = np.stack([idx.astype(np.float32) - W / 2.0 + 0.5, idy.astype(np.float32) - H / 2.0 + 0.5,
-                        np.full(n, np.sqrt(H * W), dtype=np.float32)], axis=1)
+        cam = _pixel_dirs_cam(idx, idy, W, H)
     else:
-        cam = np.stack([(idx.astype(np.float32) + 0.5 - K[0, 2]) / K[0, 0],
-                        (idy.astype(np.float32) + 0.5 - K[1, 2]) / K[1, 1], np.ones(n, dtype=np.float32)], axis=1)
-    d = cam @ RT[:3, :3].astype(np.float32).T
-    d = d / (np.linalg.norm(d, axis=1, keepdims=True).astype(np.float32) + 1e-12)
-    rays = np.zeros((n,), dtype=ray_dtype)
-    rays["o"][:, :3] = np.broadcast_to(RT[:3, 3][None, :], (n, 3))
-    rays["o"][:, 3] = 1.0
-    rays["d"][:, :3] = d
-    rays["d"][:, 3] = 0.0
-    return rays
+        cam = _pixel_dirs_cam(idx, idy, W, H, K[0, 0], K[1, 1], K[0, 2], K[1, 2])
+    # one pose for every ray: a matrix product, as the reference computes it
+    dirs = cam @ RT[:3, :3].T
+    return _pack_rays(np.broadcast_to(RT[:3, 3][None, :], (idx.size, 3)), dirs)
 
 
 def _write_npz(path: Path, payload: dict, level: int = 1):
