@@ -195,12 +195,19 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
 }
 
 // Hash-grid gradient from the ACC region (scaled deltas times Wd_in), 16 features at a time,
-// scattered with vector atomics (ffnerf_OG.cl:2090-2173).
+// scattered with vector atomics (ffnerf_OG.cl:2090-2173).  On the coarse levels (lvl < DEDUP_LEVELS)
+// the lanes of a warp -- consecutive samples of one ray -- often sit in the same grid cell and would
+// add to the same 8 table entries: such lanes are grouped (match on the cell), each writes its 8 x F
+// contributions to its row of `scratch` (shared memory, 8 F floats per thread), and the group's
+// first lane adds the group's sums with one set of atomics.  Finer levels add directly.
+constexpr int DEDUP_LEVELS = 6;
 template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
-                                                  V3 p, float unscale, const float* coef) {
+                                                  V3 p, float unscale, const float* coef, float* scratch) {
     constexpr int LPOS = L * F, LV = 16 / F;
     const uint32_t lane = (threadIdx.x & ~31u) << 16;
+    const int lid = threadIdx.x & 31;
+    float* row = scratch + threadIdx.x * (8 * F);
 #pragma unroll 1
     for (int j = 0; j < LPOS; j += 16) {
         float g[16];
@@ -219,16 +226,52 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
             }
             if (!any) continue;
             Corner8 k;
-            level_corners<F>(c, p, lvl, k);
+            uint32_t key;
+            level_corners<F>(c, p, lvl, k, &key);
+            unsigned grp = 1u << lid;
+            if (lvl < DEDUP_LEVELS) grp = __match_any_sync(__activemask(), key);
+            if (grp == (1u << lid)) {
 #pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-                const float w = k.w[cc];
-                if constexpr (F == 2)
-                    atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
-                else
-                    atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
-                              make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+                for (int cc = 0; cc < 8; ++cc) {
+                    const float w = k.w[cc];
+                    if constexpr (F == 2)
+                        atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
+                    else
+                        atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
+                                  make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+                }
+                continue;
             }
+            float v[8 * F];
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc)
+#pragma unroll
+                for (int f = 0; f < F; ++f) v[cc * F + f] = gf[f] * k.w[cc];
+#pragma unroll
+            for (int q = 0; q < 8 * F; q += 4) *reinterpret_cast<float4*>(row + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+            __syncwarp(grp);
+            if (lid == __ffs(grp) - 1) {
+                unsigned rest = grp & (grp - 1u);   // the other members
+                while (rest) {
+                    const int m = __ffs(rest) - 1;
+                    rest &= rest - 1u;
+                    const float* r = scratch + ((threadIdx.x & ~31u) + m) * (8 * F);
+#pragma unroll
+                    for (int q = 0; q < 8 * F; q += 4) {
+                        const float4 t = *reinterpret_cast<const float4*>(r + q);
+                        v[q] += t.x; v[q + 1] += t.y; v[q + 2] += t.z; v[q + 3] += t.w;
+                    }
+                }
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc) {
+                    if constexpr (F == 2)
+                        atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(v[2 * cc], v[2 * cc + 1]));
+                    else
+                        atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
+                                  make_float4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]));
+                }
+            }
+            __syncwarp(grp);
         }
     }
 }
@@ -554,7 +597,10 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         }
         sync_mma();
         dw_started = true;
-        if (hit && valid) scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef);
+        // the activation tiles are dead once the last MMAs completed: C1 holds the scatter's exchange rows
+        if (hit && valid)
+            scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef,
+                                 reinterpret_cast<float*>(tC1));
         tc::fence_before_sync();
         __syncthreads();
     }
