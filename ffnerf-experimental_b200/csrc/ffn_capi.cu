@@ -194,6 +194,22 @@ int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) 
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Blocks for a grid-stride launch over `work` items of `per_block`: at most per_sm blocks per SM of
+// the current device (SM count cached per device).
+int grid_for(uint64_t work, int per_block, int per_sm) {
+    static int sms_of[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = dev >= 0 && dev < 64 ? sms_of[dev] : 0;
+    if (sms == 0) {
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+        if (dev >= 0 && dev < 64) sms_of[dev] = sms;
+    }
+    const uint64_t need = (work + (uint64_t)per_block - 1) / (uint64_t)per_block;
+    const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
+    return (int)(need < cap ? (need ? need : 1) : cap);
+}
+
 // The split tensor-core step over groups of at most STAGE_SAMPLES samples: sampler, encoder,
 // then the MLP/compositing/backward kernel and the fixed-order partial reduction per group.
 // (Running the encoder of the next half-group on a second stream beside the MLP kernel was slower:
@@ -425,7 +441,7 @@ int ffn_apply_updates(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
     }
     lc.start[L] = (uint32_t)c->table_floats;
     const uint32_t n4 = (uint32_t)(c->table_floats / 4);
-    const int blocks = (int)((n4 + 255) / 256 < 148u * 16u ? (n4 + 255) / 256 : 148u * 16u);
+    const int blocks = grid_for(n4, 256, 16);
     if (s->flags & (FFN_STEP_TABLE_IMMEDIATE | FFN_STEP_TABLE_APPLIED)) {
         // the table was updated inside the forward/backward pass or by ffn_dp_reduce_apply
     } else if (g.table_optimizer == 1) {
@@ -479,7 +495,7 @@ int ffn_occ_st_bytes(ffn_ctx* c, uint8_t* bytes, int to_bytes, void* stream) {
     if (!aligned16(bytes)) return fail(c, FFN_E_CONFIG, "bytes must be 16-byte aligned");
     DeviceGuard guard(c->device);
     const uint32_t n = (uint32_t)c->cfg.G * c->cfg.G * c->cfg.G;
-    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    const int blocks = grid_for(n, 256, 8);
     occ_bytes_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(c->occ_st, bytes, n, to_bytes);
     ++c->launches;
     cudaError_t e = cudaGetLastError();
@@ -491,7 +507,7 @@ int ffn_occ_maintenance(ffn_ctx* c, uint32_t decay_q24, uint32_t seed, void* str
     if (decay_q24 > (1u << 24)) return fail(c, FFN_E_CONFIG, "decay_q24 must be in [0, 2^24]");
     DeviceGuard guard(c->device);
     const uint32_t n = (uint32_t)c->cfg.G * c->cfg.G * c->cfg.G;
-    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    const int blocks = grid_for(n, 256, 8);
     occ_decay_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(c->occ_in, c->occ_st, n, decay_q24, seed);
     ++c->launches;
     cudaError_t e = cudaGetLastError();
@@ -543,7 +559,7 @@ int ffn_batch_generate(const void* images, int img_f32, int channels, const uint
     if (!aligned16(rays) || !aligned16(targets)) return fail(nullptr, FFN_E_CONFIG, "rays/targets must be 16-byte aligned");
     if (!(uniform_frac >= 0.0f && uniform_frac <= 1.0f)) return fail(nullptr, FFN_E_CONFIG, "uniform_frac must be in [0, 1]");
     ffn::BatchGen g{images, img_f32, weights, c2w, K, k_per_image, n_img, W, H, channels, n, uniform_frac, seed, max_tries};
-    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    const int blocks = grid_for(n, 256, 8);
     ffn::batch_generate_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         g, static_cast<float4*>(rays), static_cast<float4*>(targets), im, x, y);
     cudaError_t e = cudaGetLastError();
@@ -563,7 +579,7 @@ int ffn_camera_rays(const float* c2w, const float* K, int W, int H, uint32_t fir
     v.has_k = K != nullptr;
     v.W = W;
     v.H = H;
-    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    const int blocks = grid_for(n, 256, 8);
     ffn::camera_rays_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(v, first, n, static_cast<float4*>(rays));
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(nullptr, e, "camera rays launch");
@@ -573,7 +589,7 @@ int ffn_batch_errors(const void* out, const void* targets, uint32_t n, float* er
     if (n == 0) return FFN_OK;
     if (!out || !targets || (!err && !sum_sq)) return fail(nullptr, FFN_E_CONFIG, "null argument");
     if (!aligned16(out) || !aligned16(targets)) return fail(nullptr, FFN_E_CONFIG, "out/targets must be 16-byte aligned");
-    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    const int blocks = grid_for(n, 256, 8);
     ffn::batch_error_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const float4*>(out), static_cast<const float4*>(targets), n, err, sum_sq);
     cudaError_t e = cudaGetLastError();
@@ -585,7 +601,7 @@ int ffn_batch_feedback(uint8_t* weights, const void* images, int img_f32, int ch
                        const float* median, double ema, int bg_cap, int fg_tau, void* stream) {
     if (n == 0) return FFN_OK;
     if (!weights || !images || !im || !x || !y || !err || !median) return fail(nullptr, FFN_E_CONFIG, "null argument");
-    const int blocks = (int)((n + 255) / 256 < 148u * 8u ? (n + 255) / 256 : 148u * 8u);
+    const int blocks = grid_for(n, 256, 8);
     ffn::batch_feedback_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         weights, images, img_f32, channels, W, H, im, x, y, err, n, median, ema, bg_cap, fg_tau);
     cudaError_t e = cudaGetLastError();
@@ -731,7 +747,7 @@ int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t
     if (!p || !g || !m || !v) return FFN_E_CONFIG;
     if (!aligned16(p) || !aligned16(g) || !aligned16(m) || !aligned16(v)) return FFN_E_CONFIG;
     const int64_t n4 = (n + 3) / 4;
-    const int blocks = (int)((n4 + 255) / 256 < 148 * 16 ? (n4 + 255) / 256 : 148 * 16);
+    const int blocks = grid_for((uint64_t)n4, 256, 16);
     adam_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p, g, m, v, n, lr_t, b1, b2, eps);
     return cudaGetLastError() == cudaSuccess ? FFN_OK : FFN_E_CUDA;
 }
