@@ -95,6 +95,8 @@ void bind_kernel(ffn_ctx* c) {
         return;
     }
     c->kernel = fused_step_kernel<F, ND, NC, ROWS>;
+    c->kernel_staged = fused_step_kernel<F, ND, NC, ROWS, true>;
+    c->encoder = encode_stage_f32_kernel<F>;
     c->rows = ROWS;
     c->smem = (size_t)Smem<F, ND, NC, ROWS>::floats(c->Pw) * sizeof(float);
     c->ctas_per_sm = 1;
@@ -238,7 +240,8 @@ int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, v
         a.x0_stage = c->x0_stage;
         a.tdt_stage = c->tdt_stage;
         a.ray_stage = c->ray_stage;
-        const int grid = n_tiles < c->max_grid ? n_tiles : c->max_grid;
+        const int mtiles = (int)((m + (uint32_t)(c->rows / spr) - 1) / (uint32_t)(c->rows / spr));   // MLP-kernel tiles
+        const int grid = mtiles < c->max_grid ? mtiles : c->max_grid;
         c->kernel_staged<<<grid, c->rows, c->smem, st>>>(a);
         ++c->launches;
         reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
@@ -320,7 +323,7 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
     }
     if (c->kernel_staged) {
         struct { void** p; size_t n; } st_allocs[] = {
-            {(void**)&c->x0_stage, (size_t)STAGE_SAMPLES * 16 * cfg->F * 2},
+            {(void**)&c->x0_stage, (size_t)STAGE_SAMPLES * 16 * cfg->F * (cfg->mlp_precision == 1 ? 2 : 4)},
             {(void**)&c->tdt_stage, (size_t)STAGE_SAMPLES * sizeof(float2)},
             {(void**)&c->pn_stage, (size_t)STAGE_SAMPLES * sizeof(float4)},
             {(void**)&c->ray_stage, (size_t)(STAGE_SAMPLES / 16) * sizeof(uint4)}};

@@ -143,7 +143,7 @@ struct Smem {
     }
 };
 
-template <int F, int ND, int NC, int ROWS>
+template <int F, int ND, int NC, int ROWS, bool STAGED = false>
 __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
     using S = Smem<F, ND, NC, ROWS>;
     constexpr int LPOS = S::LPOS, LDA0 = S::LDA0, LDH = S::LDH, LDC = S::LDC;
@@ -211,8 +211,21 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
         RayTile R{sCand, sCdf, sTs, sDTs, sTr, sKey, sSeg, sAffS, sAffE, sChg, sRay, tid, spr, rl, lid, rbase,
                   ray_idx, ray_id, valid, train, probe, o, d, bmin, bmax, bsize, inv_box, Gf, inv_n};
         bool hit;
-        int idx_sel;
-        ray_sampler(a, R, hit, idx_sel);
+        int idx_sel = 0;
+        const size_t s_glob = (size_t)ray_idx * spr + lid;   // sample index within this launch
+        if constexpr (STAGED) {
+            // sampled and encoded by sample_stage_kernel / encode_stage_f32_kernel
+            float2 tdt = make_float2(0.f, 0.f);
+            uint4 rst = make_uint4(0u, 0u, 0u, 0u);
+            if (valid) { tdt = a.tdt_stage[s_glob]; rst = a.ray_stage[ray_idx]; }
+            sTs[tid] = tdt.x;
+            sDTs[tid] = tdt.y;
+            if (lid == 0) { sChg[rl * 2] = rst.x; sChg[rl * 2 + 1] = rst.y; }
+            hit = rst.z != 0u;
+            __syncthreads();
+        } else {
+            ray_sampler(a, R, hit, idx_sel);
+        }
         const float* rs = sRay + rl * 16;
 
         // ------------------------------------------------ per-sample forward (:1257-1496)
@@ -227,8 +240,13 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
             sigma = b.x; rgb[0] = b.y; rgb[1] = b.z; rgb[2] = b.w;
         } else {
             float* a0row = sA0 + tid * LDA0;
-            if (hit) encode<F, true>(c, a.table, pn, a0row);   // rays that miss the box contribute nothing
-            else {
+            if (STAGED && valid) {
+                const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x0_stage) + s_glob * LPOS);
+#pragma unroll
+                for (int i = 0; i < LPOS; i += 4) *reinterpret_cast<float4*>(a0row + i) = __ldcs(src + i / 4);
+            } else if (!STAGED && hit) {
+                encode<F, true>(c, a.table, pn, a0row);   // rays that miss the box contribute nothing
+            } else {
 #pragma unroll
                 for (int i = 0; i < LPOS; i += 4) *reinterpret_cast<float4*>(a0row + i) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
@@ -557,6 +575,51 @@ __global__ void occ_bytes_kernel(uint32_t* __restrict__ grid, uint8_t* __restric
             }
             grid[i] = w;
         }
+    }
+}
+
+// Hash encoding of the staged sample positions into fp32 rows [sample][16 F] for the staged fp32
+// kernel: one thread per (sample, level), level-major sweep with consecutive samples per warp (as
+// encode_stage_kernel), the accumulation order of encode().  Rows of samples whose ray misses the
+// box are zero.
+template <int F>
+__global__ void __launch_bounds__(256) encode_stage_f32_kernel(const DevConfig c, const float* __restrict__ table,
+                                                               const float4* __restrict__ pn_in, int64_t n_valid,
+                                                               int64_t n_rows, unsigned char* __restrict__ out_bytes) {
+    constexpr int LPOS = L * F;
+    float* out = reinterpret_cast<float*>(out_bytes);
+    const int n_chunks = (int)((n_valid + 255) / 256);
+    const int items = n_chunks * L;
+    (void)n_rows;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int lvl = item / n_chunks;
+        const int64_t i = (int64_t)(item - lvl * n_chunks) * 256 + threadIdx.x;
+        if (i >= n_valid) continue;
+        float v[F];
+#pragma unroll
+        for (int f = 0; f < F; ++f) v[f] = 0.0f;
+        const float4 q = pn_in[i];
+        if (q.w != 0.0f) {
+            Corner8 k;
+            level_corners<F>(c, v3(q.x, q.y, q.z), lvl, k);
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                if constexpr (F == 2) {
+                    const float2 t = __ldg(reinterpret_cast<const float2*>(table + k.base[cc]));
+                    v[0] = fmaf(k.w[cc], t.x, v[0]);
+                    v[1] = fmaf(k.w[cc], t.y, v[1]);
+                } else {
+                    const float4 t = __ldg(reinterpret_cast<const float4*>(table + k.base[cc]));
+                    v[0] = fmaf(k.w[cc], t.x, v[0]);
+                    v[1] = fmaf(k.w[cc], t.y, v[1]);
+                    v[2] = fmaf(k.w[cc], t.z, v[2]);
+                    v[3] = fmaf(k.w[cc], t.w, v[3]);
+                }
+            }
+        }
+        float* dst = out + i * LPOS + lvl * F;
+        if constexpr (F == 2) *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
+        else *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 
