@@ -200,7 +200,7 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
 // add to the same 8 table entries: such lanes are grouped (match on the cell), each writes its 8 x F
 // contributions to its row of `scratch` (shared memory, 8 F floats per thread), and the group's
 // first lane adds the group's sums with one set of atomics.  Finer levels add directly.
-constexpr int DEDUP_LEVELS = 6;
+constexpr int DEDUP_LEVELS = 10;
 template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
                                                   V3 p, float unscale, const float* coef, float* scratch) {
