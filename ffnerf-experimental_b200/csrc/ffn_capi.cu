@@ -244,7 +244,8 @@ int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, v
         const int grid = mtiles < c->max_grid ? mtiles : c->max_grid;
         c->kernel_staged<<<grid, c->rows, c->smem, st>>>(a);
         ++c->launches;
-        reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+        reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats,
+                                                            c->status);
         ++c->launches;
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(c, e, "split step launch");
@@ -420,7 +421,8 @@ int ffn_forward_backward(ffn_ctx* c, const void* rays, const void* targets, void
     a.do_train = 1;
     int grid = 0;
     if ((rc = launch_fused(c, a, st, &grid)) != FFN_OK) return rc;
-    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats);
+    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats,
+                                                            c->status);
     ++c->launches;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "gradient reduction launch");

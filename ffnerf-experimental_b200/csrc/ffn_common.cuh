@@ -167,6 +167,7 @@ __device__ __forceinline__ float own_powr(float x, float y) {
 
 // ------------------------------------------------------------------------- error word
 // Bits set by kernels in the context's device status word (read asynchronously by the host).
-enum { ST_NONFINITE_LOSS = 1, ST_BAD_LAUNCH = 2 };
+// device status word bits (ffn_status)
+enum { ST_NONFINITE = 1, ST_TC_TIMEOUT = 4, ST_DP_TIMEOUT = 8 };
 
 }  // namespace ffn

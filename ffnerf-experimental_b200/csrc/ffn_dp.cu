@@ -27,7 +27,6 @@ namespace ffn {
 
 constexpr int DP_MAX_RANKS = 8;
 constexpr uint32_t DP_WAIT_LIMIT = 1u << 24;   // polls of ~1 us each (~16 s) before giving up
-constexpr int ST_DP_TIMEOUT = 8;
 
 struct DpPeers {
     float* grads[DP_MAX_RANKS];      // every rank's gradient buffer (this rank's included)

@@ -371,9 +371,12 @@ __device__ __forceinline__ void ray_composite(const StepArgs& a, const RayTile& 
         rw[RS_TFIN] = T_final;
         rw[RS_GRX] = gr[0]; rw[RS_GRY] = gr[1]; rw[RS_GRZ] = gr[2];
         rw[RS_GTEND] = fa(fa(fm(gr[0], bg[0]), fm(gr[1], bg[1])), fm(gr[2], bg[2]));
-        if (valid)
+        if (valid) {
             a.out[ray_idx] = make_float4(fclamp(cf[0], 0.f, 1.f), fclamp(cf[1], 0.f, 1.f),
                                          fclamp(cf[2], 0.f, 1.f), (train && !probe) ? 4.0f : 0.0f);
+            // a NaN / Inf colour means the model diverged: flag it for the host (ffn_status)
+            if (a.status && !(isfinite(cf[0]) && isfinite(cf[1]) && isfinite(cf[2]))) atomicOr(a.status, ST_NONFINITE);
+        }
     }
     __syncthreads();
     const float gr0 = rs[RS_GRX], gr1 = rs[RS_GRY], gr2 = rs[RS_GRZ], gT_end = rs[RS_GTEND];

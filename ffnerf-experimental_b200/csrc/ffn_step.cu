@@ -424,12 +424,15 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
 }
 
 // Fixed-order sum of the per-CTA weight-gradient partials into the MLP gradient.
-__global__ void reduce_partials(const float* __restrict__ partials, int n_parts, int Pw, float* __restrict__ grad) {
+// A non-finite sum (NaN/Inf reaching the MLP gradient: the model diverged) sets ST_NONFINITE.
+__global__ void reduce_partials(const float* __restrict__ partials, int n_parts, int Pw, float* __restrict__ grad,
+                                int* status = nullptr) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= Pw) return;
     float s = 0.0f;
     for (int p = 0; p < n_parts; ++p) s += partials[(size_t)p * Pw + i];
     grad[i] += s;
+    if (status && !isfinite(s)) atomicOr(status, ST_NONFINITE);
 }
 
 // adam_update_1_i32 (weight_update.cl:177-201); the gradient is cleared after use.

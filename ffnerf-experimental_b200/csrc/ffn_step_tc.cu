@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         if (!*abort_flag) {
             if (!tc::mbar_wait(mbar, phase, WAIT_LIMIT)) {
                 *abort_flag = 1;
-                if (a.status) atomicOr(a.status, 4);
+                if (a.status) atomicOr(a.status, ST_TC_TIMEOUT);
             }
         }
         phase ^= 1u;

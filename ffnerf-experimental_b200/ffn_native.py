@@ -45,6 +45,7 @@ class FfnStep(C.Structure):
 
 STEP_TABLE_IMMEDIATE = 1
 STEP_TABLE_APPLIED = 2
+STATUS_NONFINITE, STATUS_TC_TIMEOUT, STATUS_DP_TIMEOUT = 1, 4, 8   # ffn_status bits
 STAGE_SAMPLES = 1 << 20   # samples per group of the split tensor-core step (ffn_capi.cu)
 ABI_VERSION = 3          # include/ffnerf.h FFN_ABI_VERSION
 

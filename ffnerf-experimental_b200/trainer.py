@@ -64,6 +64,10 @@ def train(nerf, producer: GpuBatchProducer, cfg: TrainConfig, start_step: int = 
             pending.append((step, m, float(lr_f)))
         if len(pending) > 4 or (pending and k == cfg.steps - 1):
             nerf.queue.finish()
+            st = nerf.native.status()
+            if st:
+                raise RuntimeError(f"device status {st:#x} by step {step}: "
+                                   + ("non-finite colours (the model diverged)" if st & 1 else "a bounded wait ran out"))
             for s, m, lr in pending:
                 mse, rmse, l2 = (float(v) for v in m.cpu().numpy())
                 cfg.history.append((s, mse, rmse, l2, lr))

@@ -160,7 +160,9 @@ int ffn_hash_encode_bwd(ffn_ctx* ctx, const float* pts, const float* denc, int64
 /* Kernels this context has launched so far (all entry points; no reference counterpart). */
 uint64_t ffn_kernel_launches(const ffn_ctx* ctx);
 /* Reads and clears the context's device status word (waits for the device): 0 when every kernel
- * since the last call completed normally; bit 2 = a tensor-core wait exceeded its bound. */
+ * since the last call completed normally; bit 0 = a ray colour or an MLP gradient was not finite
+ * (the model diverged: NaN/Inf weights); bit 2 = a tensor-core wait exceeded its bound; bit 3 = a cross-rank wait of the
+ * data-parallel exchange ran out. */
 int ffn_status(ffn_ctx* ctx, uint32_t* status);
 
 /* Data-parallel exchange over NVLink peer memory (no reference counterpart: the reference runs on

@@ -294,3 +294,18 @@ def test_invalid_config_rejected():
     g["spr"] = 48
     with pytest.raises(ValueError):
         fn.Context(g)
+
+
+def test_nonfinite_gradient_sets_status():
+    """NaN weights of the colour head reach the MLP gradient (fp32 MLP): status bit 0, cleared on read."""
+    g, ctx, blob, table, occ, rays, tg = _make("cfg1", seed=13)
+    bad = blob.copy()
+    off, size = ctx.layout["Wc_out"]
+    bad[off:off + size] = np.nan
+    ctx.tensor(fn.BUF_PARAMS).copy_(_cuda(bad))
+    n = rays.shape[0]
+    dout = torch.zeros((n, 4), device="cuda")
+    ctx.forward_backward(_cuda(rays), _cuda(tg), dout, n, fn.make_step(lr_f=1e-3, rng_u32=3))
+    torch.cuda.synchronize()
+    assert ctx.status() & fn.STATUS_NONFINITE
+    assert ctx.status() == 0
