@@ -67,7 +67,8 @@ def train(nerf, producer: GpuBatchProducer, cfg: TrainConfig, start_step: int = 
             st = nerf.native.status()
             if st:
                 raise RuntimeError(f"device status {st:#x} by step {step}: "
-                                   + ("non-finite colours (the model diverged)" if st & 1 else "a bounded wait ran out"))
+                                   + ("non-finite colours or gradients (the model diverged)" if st & 1
+                                      else "a bounded wait ran out"))
             for s, m, lr in pending:
                 mse, rmse, l2 = (float(v) for v in m.cpu().numpy())
                 cfg.history.append((s, mse, rmse, l2, lr))
