@@ -62,16 +62,24 @@ MICRO = {
     "cfg4-T22": dict(kind="hash", points=1 << 22, F=2, log2T=22, rmax=2048.0,
                      desc="cfg4: hash encode fwd+bwd, 2^22 points U[0,1]^3, L=16 F=2 T=2^22 fp32 table, "
                           "upstream grads N(0,1) [2^22, 32] fp32"),
+    "cfg4-f16": dict(kind="hash", points=1 << 22, F=2, log2T=19, rmax=2048.0, table="f16",
+                     desc="cfg4: hash encode fwd+bwd, 2^22 points U[0,1]^3, L=16 F=2 T=2^19 fp16 table "
+                          "(fp16 encoding out), upstream grads N(0,1) [2^22, 32] fp32"),
+    "cfg4-T22-f16": dict(kind="hash", points=1 << 22, F=2, log2T=22, rmax=2048.0, table="f16",
+                         desc="cfg4: hash encode fwd+bwd, 2^22 points U[0,1]^3, L=16 F=2 T=2^22 fp16 table "
+                              "(fp16 encoding out), upstream grads N(0,1) [2^22, 32] fp32"),
     "cfg5-adam": dict(kind="adam", n=1 << 24, desc="cfg5: Adam over 2^24 fp32 parameters, grads N(0,1e-3), "
                                                     "beta1 0.9 beta2 0.99 eps 1e-15 lr 1e-2"),
 }
 
 
-def hash_bytes_per_point(F: int):
-    """Algorithmic bytes per point: forward = xyz + 16 levels x 8 corners x F x 4 B gathered + 16 F x 4 B
-    written; backward = xyz + 16 F x 4 B upstream + 16 x 8 x F x 4 B atomic read-modify-write."""
-    gather = 16 * 8 * F * 4
-    return 12 + gather + 16 * F * 4, 12 + 16 * F * 4 + 2 * gather
+def hash_bytes_per_point(F: int, s_tab: int = 4):
+    """Algorithmic bytes per point for table entries of s_tab bytes per feature (4: fp32, 2: fp16;
+    the encoding is written in the table's type): forward = xyz + 16 levels x 8 corners x F x s_tab
+    gathered + 16 F x s_tab written; backward = xyz + 16 F x 4 B fp32 upstream + 16 x 8 x F x s_tab
+    atomic read-modify-write (fp32: 1164 / 2188 B at F=2; fp16: 588 / 1164 B)."""
+    gather = 16 * 8 * F * s_tab
+    return 12 + gather + 16 * F * s_tab, 12 + 16 * F * 4 + 2 * gather
 
 
 def run_micro(args, name: str) -> dict:
@@ -107,12 +115,20 @@ def run_micro(args, name: str) -> dict:
         g = make_geometry(F=wl["F"], ND=1, NC=2, spr=64, G=16, log2_entries=wl["log2T"], rmax=wl["rmax"])
         ctx = fn.Context(g, device=0)
         n = wl["points"]
+        f16 = wl.get("table") == "f16"
+        s_tab = 2 if f16 else 4
         ctx.tensor(fn.BUF_TABLE).uniform_(-1e-4, 1e-4, generator=gen)
         pts = torch.rand((n, 3), device=dev, generator=gen)
-        enc = torch.empty((n, 16 * wl["F"]), device=dev)
+        enc = torch.empty((n, 16 * wl["F"]), device=dev, dtype=torch.float16 if f16 else torch.float32)
         denc = torch.randn((n, 16 * wl["F"]), device=dev, generator=gen)
-        fwd = lambda: ctx.hash_encode(pts, enc, n, stream=st)            # noqa: E731
-        bwd = lambda: ctx.hash_encode_bwd(pts, denc, n, stream=st)       # noqa: E731
+        if f16:
+            table16 = ctx.tensor(fn.BUF_TABLE).half()
+            grad16 = torch.zeros_like(table16)
+            fwd = lambda: ctx.hash_encode_f16(table16, pts, enc, n, stream=st)       # noqa: E731
+            bwd = lambda: ctx.hash_encode_bwd_f16(grad16, pts, denc, n, stream=st)   # noqa: E731
+        else:
+            fwd = lambda: ctx.hash_encode(pts, enc, n, stream=st)            # noqa: E731
+            bwd = lambda: ctx.hash_encode_bwd(pts, denc, n, stream=st)       # noqa: E731
         for _ in range(args.warmup):
             with torch.cuda.stream(st):
                 fwd(); bwd()
@@ -130,7 +146,7 @@ def run_micro(args, name: str) -> dict:
                 fwd(); bwd()
                 h_enc.copy_(enc, non_blocking=True)
             (t_e2e,) = timed([e2e])
-        bf, bb = hash_bytes_per_point(wl["F"])
+        bf, bb = hash_bytes_per_point(wl["F"], s_tab)
         gbs_f = bf * n / (t_fwd / args.steps * 1e-3) / 1e9
         gbs_b = bb * n / (t_bwd / args.steps * 1e-3) / 1e9
         gbs = (bf + bb) * n / ((t_fwd + t_bwd) / args.steps * 1e-3) / 1e9
@@ -150,29 +166,32 @@ def run_micro(args, name: str) -> dict:
             o.hash_fwd(cfg, table_h, p_h, e_h)
             o.hash_bwd(cfg, p_h, d_h, tg_h)
             reps += 1
-        cpu_gbs = (bf + bb) * m * reps / (time.perf_counter() - t0) / 1e9
+        bf32, bb32 = hash_bytes_per_point(wl["F"])          # the oracle works on an fp32 table
+        cpu_gbs = (bf32 + bb32) * m * reps / (time.perf_counter() - t0) / 1e9
         ctx.close()
         line = {
             "metric": "hash-grid GB/s (encode fwd+bwd, algorithmic bytes)", "value": gbs, "unit": "GB/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": (t_fwd + t_bwd) / args.steps, "higher_is_better": True, "scaling": "none",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f16 table, f32 accumulation" if f16 else "f32", "data": "synthetic",
             "config": {"workload": wl["desc"], "points": n, "l2": "flushed between iterations (256 MB write)",
-                       "table_bytes": g["table_entries"] * wl["F"] * 4},
+                       "table_bytes": g["table_entries"] * wl["F"] * s_tab},
             "fwd": {"ms": t_fwd / args.steps, "GB/s": gbs_f, "points/s": n / (t_fwd / args.steps * 1e-3),
                     "bytes_per_point": bf},
             "bwd": {"ms": t_bwd / args.steps, "GB/s": gbs_b, "points/s": n / (t_bwd / args.steps * 1e-3),
                     "bytes_per_point": bb},
             "e2e": {"value": e2e_gbs, "unit": "GB/s", "h2d_bytes_per_step": n * (12 + 16 * wl["F"] * 4),
-                    "d2h_bytes_per_step": n * 16 * wl["F"] * 4},
+                    "d2h_bytes_per_step": n * 16 * wl["F"] * s_tab},
             "gpu_launches": args.steps * 2,
-            "roofline": {"bound": "hbm" if g["table_entries"] * wl["F"] * 4 > 100e6 else "l2",
-                         "kernel": "hash_fwd_kernel + hash_bwd_kernel", "achieved": gbs, "peak": hbm,
+            "roofline": {"bound": "hbm" if g["table_entries"] * wl["F"] * s_tab > 100e6 else "l2",
+                         "kernel": "hash_fwd_f16_kernel + hash_bwd_f16_kernel" if f16
+                         else "hash_fwd_kernel + hash_bwd_kernel", "achieved": gbs, "peak": hbm,
                          "unit": "GB/s", "frac": gbs / hbm, "traffic": None, "peak_source": peak_kind,
                          "note": "peak = measured HBM copy bandwidth; random 8 B gathers move 32 B sectors"},
             "clocks": clk.summary(),
             "cpu_baseline": {"value": cpu_gbs, "unit": "GB/s", "cores": 1, "kind": "port",
-                             "sample": f"{m} points fwd+bwd, oracle restatement, repeated for 10 s"},
+                             "sample": f"{m} points fwd+bwd, oracle restatement (fp32 table; its GB/s counts "
+                                       f"fp32 bytes), repeated for 10 s"},
         }
         return line
     # Adam

@@ -551,6 +551,41 @@ int ffn_hash_encode_bwd(ffn_ctx* c, const float* pts, const float* denc, int64_t
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "hash scatter launch");
 }
 
+int ffn_hash_encode_f16(ffn_ctx* c, const void* table16, const float* pts, void* enc16, int64_t n, void* stream) {
+    if (!c || (n > 0 && (!table16 || !pts || !enc16))) return fail(c, FFN_E_CONFIG, "null argument");
+    if (n <= 0) return FFN_OK;
+    if (!aligned16(table16) || !aligned16(enc16)) return fail(c, FFN_E_CONFIG, "table16 and enc16 must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    const int64_t items = (n + 15) / 16;   // blocks of 16 points x 16 levels
+    const int sms = c->max_grid / c->ctas_per_sm;
+    const int blocks = (int)(items < (int64_t)sms * 16 ? items : (int64_t)sms * 16);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const __half* tab = static_cast<const __half*>(table16);
+    __half* enc = static_cast<__half*>(enc16);
+    if (c->cfg.F == 2) hash_fwd_f16_kernel<2><<<blocks, 256, 0, st>>>(c->dc, tab, pts, n, enc);
+    else hash_fwd_f16_kernel<4><<<blocks, 256, 0, st>>>(c->dc, tab, pts, n, enc);
+    ++c->launches;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "fp16 hash encode launch");
+}
+
+int ffn_hash_encode_bwd_f16(ffn_ctx* c, void* grad16, const float* pts, const float* denc, int64_t n, void* stream) {
+    if (!c || (n > 0 && (!grad16 || !pts || !denc))) return fail(c, FFN_E_CONFIG, "null argument");
+    if (n <= 0) return FFN_OK;
+    if (!aligned16(grad16) || !aligned16(denc)) return fail(c, FFN_E_CONFIG, "grad16 and denc must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    const int64_t items = (n + 15) / 16;
+    const int sms = c->max_grid / c->ctas_per_sm;
+    const int blocks = (int)(items < (int64_t)sms * 16 ? items : (int64_t)sms * 16);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    __half* g = static_cast<__half*>(grad16);
+    if (c->cfg.F == 2) hash_bwd_f16_kernel<2><<<blocks, 256, 0, st>>>(c->dc, g, pts, denc, n);
+    else hash_bwd_f16_kernel<4><<<blocks, 256, 0, st>>>(c->dc, g, pts, denc, n);
+    ++c->launches;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "fp16 hash scatter launch");
+}
+
 uint64_t ffn_kernel_launches(const ffn_ctx* c) { return c ? c->launches : 0u; }
 
 int ffn_batch_generate(const void* images, int img_f32, int channels, const uint8_t* weights, const float* c2w,

@@ -24,6 +24,7 @@
 #include "ffn_raymarch.cuh"
 
 #include <cfloat>
+#include <cuda_fp16.h>
 
 namespace ffn {
 
@@ -710,6 +711,97 @@ __global__ void __launch_bounds__(256) hash_bwd_kernel(const DevConfig c, float*
             else
                 atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
                           make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+        }
+    }
+}
+
+// fp16-table variants of the two kernels above (the fp16 table case of the hash microbenchmark;
+// the reference's table is fp32 only).  Entries are F halves (F=2: one __half2, 4 B); the gather
+// accumulates in fp32 and writes the encoding as fp16; the scatter takes fp32 upstream gradients
+// and adds with packed half2 atomics (red.add.noftz.f16x2).
+template <int F>
+__device__ __forceinline__ void table_ld_f16(const __half* p, float* t) {
+    if constexpr (F == 2) {
+        const float2 v = __half22float2(__ldg(reinterpret_cast<const __half2*>(p)));
+        t[0] = v.x; t[1] = v.y;
+    } else {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        t[0] = a.x; t[1] = a.y; t[2] = b.x; t[3] = b.y;
+    }
+}
+
+template <int F, int LG = 16>
+__global__ void __launch_bounds__(256) hash_fwd_f16_kernel(const DevConfig c, const __half* __restrict__ table,
+                                                           const float* __restrict__ pts, int64_t n,
+                                                           __half* __restrict__ enc) {
+    constexpr int CH = 256 / LG;
+    const int64_t n_chunks = (n + CH - 1) / CH;
+    const int64_t items = n_chunks * (L / LG);
+    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+        const int grp = (int)(item / n_chunks);
+        const int64_t i = (item - grp * n_chunks) * CH + threadIdx.x / LG;
+        const int lvl = grp * LG + (int)(threadIdx.x % LG);
+        if (i >= n) continue;
+        const float hi = 1.0f - 1.0e-6f;
+        const V3 p = v3(fclamp(pts[3 * i], 0.f, hi), fclamp(pts[3 * i + 1], 0.f, hi), fclamp(pts[3 * i + 2], 0.f, hi));
+        Corner8 k;
+        level_corners<F>(c, p, lvl, k);
+        float acc[F];
+#pragma unroll
+        for (int f = 0; f < F; ++f) acc[f] = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            float t[F];
+            table_ld_f16<F>(table + k.base[cc], t);
+#pragma unroll
+            for (int f = 0; f < F; ++f) acc[f] = fmaf(k.w[cc], t[f], acc[f]);
+        }
+        __half2* dst = reinterpret_cast<__half2*>(enc + i * (L * F) + lvl * F);
+#pragma unroll
+        for (int f = 0; f < F; f += 2) __stcs(dst + f / 2, __floats2half2_rn(acc[f], acc[f + 1]));
+    }
+}
+
+template <int F, int LG = 16>
+__global__ void __launch_bounds__(256) hash_bwd_f16_kernel(const DevConfig c, __half* __restrict__ grad,
+                                                           const float* __restrict__ pts,
+                                                           const float* __restrict__ denc, int64_t n) {
+    constexpr int CH = 256 / LG;
+    const int64_t n_chunks = (n + CH - 1) / CH;
+    const int64_t items = n_chunks * (L / LG);
+    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+        const int grp = (int)(item / n_chunks);
+        const int64_t i = (item - grp * n_chunks) * CH + threadIdx.x / LG;
+        const int lvl = grp * LG + (int)(threadIdx.x % LG);
+        if (i >= n) continue;
+        const float* g = denc + i * (L * F) + lvl * F;
+        float gf[F];
+        bool any = false;
+        if constexpr (F == 2) {
+            const float2 t = __ldcs(reinterpret_cast<const float2*>(g));
+            gf[0] = t.x; gf[1] = t.y;
+        } else {
+            const float4 t = __ldcs(reinterpret_cast<const float4*>(g));
+            gf[0] = t.x; gf[1] = t.y; gf[2] = t.z; gf[3] = t.w;
+        }
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+            gf[f] = isfinite(gf[f]) ? gf[f] : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
+            any |= gf[f] != 0.0f;
+        }
+        if (!any) continue;
+        const float hi = 1.0f - 1.0e-6f;
+        const V3 p = v3(fclamp(pts[3 * i], 0.f, hi), fclamp(pts[3 * i + 1], 0.f, hi), fclamp(pts[3 * i + 2], 0.f, hi));
+        Corner8 k;
+        level_corners<F>(c, p, lvl, k);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const float w = k.w[cc];
+            __half2* dst = reinterpret_cast<__half2*>(grad + k.base[cc]);
+#pragma unroll
+            for (int f = 0; f < F; f += 2) atomicAdd(dst + f / 2, __floats2half2_rn(gf[f] * w, gf[f + 1] * w));
         }
     }
 }

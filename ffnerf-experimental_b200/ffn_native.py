@@ -68,6 +68,8 @@ _SIGS = {
     "ffn_probe": (C.c_int, [_VP, _VP, _VP, _VP, C.c_uint32, C.POINTER(FfnStep), _VP] + [_VP] * 7 + [_VP]),
     "ffn_hash_encode": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_hash_encode_bwd": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
+    "ffn_hash_encode_f16": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, _VP]),
+    "ffn_hash_encode_bwd_f16": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_adam": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_float, _VP]),
     "ffn_status": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
     "ffn_forward_backward_noalloc": (C.c_int, [C.POINTER(FfnConfig)] + [_VP] * 9 + [C.c_uint32, C.POINTER(FfnStep), _VP]),
@@ -297,6 +299,16 @@ class Context:
     def hash_encode_bwd(self, pts, denc, n: int, stream=None):
         self._check(self.lib.ffn_hash_encode_bwd(self.h, _ptr(pts), _ptr(denc), int(n), self._stream(stream)),
                     "ffn_hash_encode_bwd")
+
+    def hash_encode_f16(self, table16, pts, enc16, n: int, stream=None):
+        """Encoding from a caller-owned fp16 table (FFN_BUF_TABLE's layout) into fp16 enc16 [n, 16F]."""
+        self._check(self.lib.ffn_hash_encode_f16(self.h, _ptr(table16), _ptr(pts), _ptr(enc16), int(n),
+                                                 self._stream(stream)), "ffn_hash_encode_f16")
+
+    def hash_encode_bwd_f16(self, grad16, pts, denc, n: int, stream=None):
+        """Scatter-adds fp32 upstream gradients denc [n, 16F] into the caller-owned fp16 table grad16."""
+        self._check(self.lib.ffn_hash_encode_bwd_f16(self.h, _ptr(grad16), _ptr(pts), _ptr(denc), int(n),
+                                                     self._stream(stream)), "ffn_hash_encode_bwd_f16")
 
     def occ_st_bytes(self, buf, to_bytes: bool, stream=None):
         self._check(self.lib.ffn_occ_st_bytes(self.h, _ptr(buf), 1 if to_bytes else 0, self._stream(stream)),

@@ -157,6 +157,14 @@ int ffn_probe(ffn_ctx* ctx, const void* rays, const void* targets, void* out, ui
 int ffn_hash_encode(ffn_ctx* ctx, const float* pts, float* enc, int64_t n, void* stream);
 int ffn_hash_encode_bwd(ffn_ctx* ctx, const float* pts, const float* denc, int64_t n,
                         void* stream);
+/* The same two operations on an fp16 table owned by the caller (table16 / grad16: the context's
+ * table layout, FFN_BUF_TABLE's element count, as IEEE half; enc16 is [n][16*F] half; denc stays
+ * fp32).  The fp16-table case of the hash microbenchmark; no reference counterpart (the
+ * reference's table is fp32).  Gathers accumulate in fp32; the scatter adds packed half2. */
+int ffn_hash_encode_f16(ffn_ctx* ctx, const void* table16, const float* pts, void* enc16, int64_t n,
+                        void* stream);
+int ffn_hash_encode_bwd_f16(ffn_ctx* ctx, void* grad16, const float* pts, const float* denc, int64_t n,
+                            void* stream);
 /* Kernels this context has launched so far (all entry points; no reference counterpart). */
 uint64_t ffn_kernel_launches(const ffn_ctx* ctx);
 /* Reads and clears the context's device status word (waits for the device): 0 when every kernel

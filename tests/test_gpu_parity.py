@@ -254,6 +254,40 @@ def test_hash_encode_fwd_bwd(oracle, F, log2T):
     assert rel_l2(tg_g, tg_o) < 1e-5
 
 
+@pytest.mark.parametrize("F", [2, 4])
+def test_hash_encode_f16_table(oracle, F):
+    """fp16-table encode/scatter: the encoding equals the oracle's fp32 encoding of the same (fp16-
+    representable) table up to the fp16 rounding of the output (rel 1e-3); the scatter's fp16
+    accumulation stays within rel-L2 5e-3 of the oracle's fp32 sums."""
+    g = make_geometry(F=F, ND=1, NC=2, log2_entries=14, rmax=2048.0)
+    ctx = fn.Context(g)
+    rng = np.random.default_rng(40 + F)
+    size = ctx.tensor(fn.BUF_TABLE).numel()
+    table16 = rng.uniform(-1.0, 1.0, size).astype(np.float16)
+    n = 4000
+    pts = rng.random((n, 3), dtype=np.float32)
+    pts[:4] = [[0, 0, 0], [1, 1, 1], [0.999999, 0.5, 0], [1.5, -0.5, 0.5]]
+    enc_o = np.zeros((n, 16 * F), np.float32)
+    oracle.hash_fwd(make_orc_config(g), table16.astype(np.float32), pts, enc_o)
+    enc16 = torch.zeros((n, 16 * F), dtype=torch.float16, device="cuda")
+    ctx.hash_encode_f16(_cuda(table16), _cuda(pts), enc16, n)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(enc16.cpu().numpy().astype(np.float32), enc_o, rtol=1e-3, atol=1e-6)
+    denc = rng.normal(size=(n, 16 * F)).astype(np.float32)
+    denc[7, :] = np.nan                                      # non-finite upstream values are skipped
+    denc_o = denc.copy()
+    denc_o[7, :] = 0.0
+    tg_o = np.zeros(size, np.float32)
+    oracle.hash_bwd(make_orc_config(g), pts, denc_o, tg_o)
+    grad16 = torch.zeros(size, dtype=torch.float16, device="cuda")
+    ctx.hash_encode_bwd_f16(grad16, _cuda(pts), _cuda(denc), n)
+    torch.cuda.synchronize()
+    tg_g = grad16.cpu().numpy().astype(np.float32)
+    assert np.isfinite(tg_g).all()
+    assert rel_l2(tg_g, tg_o) < 5e-3
+    assert not ctx.tensor(fn.BUF_GRADS).any(), "the fp16 scatter writes only the caller's table"
+
+
 def test_render_matches_oracle_inference(oracle):
     g, ctx, blob, table, occ, rays, tg = _make("cfg1", seed=9)
     n = rays.shape[0]
