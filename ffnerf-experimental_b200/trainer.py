@@ -85,40 +85,59 @@ def train(nerf, producer: GpuBatchProducer, cfg: TrainConfig, start_step: int = 
     return cfg.history
 
 
-def synthetic_run(workload: str = "cfg1", steps: int = 3000, mlp_precision: str = "fp16", seed: int = 0,
-                  log: bool = True, training_dir: str | None = None):
-    """Trains on the seeded synthetic Gaussian-blob scene of the benchmark configurations (cfg1: 8
-    cameras at 64x64, T=2^14, Rmax 512, occupancy 64^3; cfg2: 56 cameras at 450x800, T=2^19,
-    Rmax 2048, occupancy 128^3), 512 rays x 64 samples per step.  Returns (nerf, history)."""
-    import tempfile
+SYNTHETIC = {"cfg1": dict(n_cams=8, W=64, H=64, log2T=14, rmax=512.0, G=64),
+             "cfg2": dict(n_cams=56, W=800, H=450, log2T=19, rmax=2048.0, G=128)}
+
+
+def synthetic_scene_views(workload: str = "cfg1", seed: int = 0):
+    """The seeded synthetic Gaussian-blob scene of the benchmark configurations (cfg1: 8 cameras
+    at 64x64 on a radius-2 sphere; cfg2: 56 cameras at 450x800 on a ring), rendered analytically
+    on the device into 8-bit images (the reference's loader quantises too).
+    Returns (images uint8 [n, H, W, 3], c2w [n, 4, 4], K [3, 3], W, H)."""
     import torch
-    import ffnerf_tools as ft
     from synthetic_scene import BlobScene, cameras_ring, cameras_sphere, intrinsics, pixel_rays
-    wl = {"cfg1": dict(n_cams=8, W=64, H=64, log2T=14, rmax=512.0, G=64),
-          "cfg2": dict(n_cams=56, W=800, H=450, log2T=19, rmax=2048.0, G=128)}[workload]
+    wl = SYNTHETIC[workload]
     scene = BlobScene(seed)
     cams = cameras_sphere(wl["n_cams"], 2.0, seed) if wl["n_cams"] <= 8 else cameras_ring(wl["n_cams"], 2.5, seed)
     K = intrinsics(wl["W"], wl["H"], 50.0)
     vv, uu = np.mgrid[0:wl["H"], 0:wl["W"]]
     images = []
-    for c in cams:      # 8-bit images rendered analytically (the reference's loader quantises too)
+    for c in cams:
         rgb = scene.render_torch(torch.from_numpy(pixel_rays(c, K, uu.ravel(), vv.ravel())).cuda(), n_quad=192)
         images.append(torch.round(rgb.clamp(0, 1) * 255).to(torch.uint8).cpu().numpy().reshape(wl["H"], wl["W"], 3))
-    images = np.stack(images)
+    return np.stack(images), np.asarray(cams, np.float32), K, wl["W"], wl["H"]
+
+
+def synthetic_nerf(workload: str = "cfg1", mlp_precision: str = "fp16", seed: int = 0,
+                   training_dir: str | None = None, table_update: str = "immediate"):
+    """A fresh ffnerf_tools.Nerf for the synthetic scene's geometry: hash L=16 F=2 (T and Rmax of
+    the workload), ND=1, NC=2, random background, box [-1, 1]^3, near clip 0.3, rng seed 777+seed."""
+    import tempfile
+    import ffnerf_tools as ft
+    wl = SYNTHETIC[workload]
     ctx = ft.Context([ft.Device(0)])
     queue = ft.CommandQueue(ctx)
     occ = ft.OccParams(G_occ=wl["G"], box_min=np.array([-1, -1, -1], np.float32),
                        box_max=np.array([1, 1, 1], np.float32), rho_min=np.float32(1.0),
                        rho_max=np.float32(16.0), t_near_clip=np.float32(0.3)).finalize()
     tdir = training_dir or tempfile.mkdtemp(prefix="ffn_train_")
-    nerf = ft.Nerf(ctx, queue, training_dir=tdir, model_id=f"synthetic_{workload}", transfer_fmt="fp32",
+    return ft.Nerf(ctx, queue, training_dir=tdir, model_id=f"synthetic_{workload}", transfer_fmt="fp32",
                    table_size_entries=16 << wl["log2T"], f_per_level=2, occ=occ, rng_seed=777 + seed,
                    background="random", finest_resolution=wl["rmax"], nd=1, nc=2, mlp_precision=mlp_precision,
-                   verbose=False)
-    prod = GpuBatchProducer(images, cams, K, wl["W"], wl["H"], batch_rays=512, rng_seed=seed)
+                   verbose=False, table_update=table_update)
+
+
+def synthetic_run(workload: str = "cfg1", steps: int = 3000, mlp_precision: str = "fp16", seed: int = 0,
+                  log: bool = True, training_dir: str | None = None):
+    """Trains on the synthetic scene (synthetic_scene_views), 512 rays x 64 samples per step, with
+    the device batch producer.  Returns (nerf, history, (images, c2w, K, W, H))."""
+    data = synthetic_scene_views(workload, seed)
+    images, cams, K, W, H = data
+    nerf = synthetic_nerf(workload, mlp_precision, seed, training_dir)
+    prod = GpuBatchProducer(images, cams, K, W, H, batch_rays=512, rng_seed=seed)
     cfg = TrainConfig(steps=steps, batch_rays=512, samples_per_ray=64, period=100, log=log, rng_seed=seed)
     hist = train(nerf, prod, cfg)
-    return nerf, hist, (images, cams, K, wl["W"], wl["H"])
+    return nerf, hist, data
 
 
 def evaluate_psnr(nerf, images, cams, K, W: int, H: int) -> float:
