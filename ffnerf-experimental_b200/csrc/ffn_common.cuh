@@ -167,6 +167,15 @@ __device__ __forceinline__ float own_powr(float x, float y) {
 
 // ------------------------------------------------------------------------- error word
 // Bits set by kernels in the context's device status word (read asynchronously by the host).
+// Vector float adds to global memory without a returned value (red, not atom): nothing waits for
+// the old value, and the issuing thread's registers are free at once.
+__device__ __forceinline__ void red_add2(float* p, float a, float b) {
+    asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
 // device status word bits (ffn_status)
 enum { ST_NONFINITE = 1, ST_TC_TIMEOUT = 4, ST_DP_TIMEOUT = 8 };
 

@@ -144,10 +144,9 @@ __device__ __forceinline__ void scatter_grad(const DevConfig& c, float* __restri
         for (int cc = 0; cc < 8; ++cc) {
             const float w = k.w[cc];
             if constexpr (F == 2) {
-                atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
+                red_add2(grad + k.base[cc], gf[0] * w, gf[1] * w);
             } else {
-                atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
-                          make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+                red_add4(grad + k.base[cc], gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w);
             }
         }
     }
@@ -204,10 +203,9 @@ __device__ __forceinline__ void scatter_grad_regs(const DevConfig& c, float* __r
         for (int cc = 0; cc < 8; ++cc) {
             const float w = k.w[cc];
             if constexpr (F == 2) {
-                atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
+                red_add2(grad + k.base[cc], gf[0] * w, gf[1] * w);
             } else {
-                atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
-                          make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+                red_add4(grad + k.base[cc], gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w);
             }
         }
     }

@@ -707,10 +707,9 @@ __global__ void __launch_bounds__(256) hash_bwd_kernel(const DevConfig c, float*
         for (int cc = 0; cc < 8; ++cc) {
             const float w = k.w[cc];
             if constexpr (F == 2)
-                atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
+                red_add2(grad + k.base[cc], gf[0] * w, gf[1] * w);
             else
-                atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
-                          make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
+                red_add4(grad + k.base[cc], gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w);
         }
     }
 }
@@ -730,6 +729,12 @@ __device__ __forceinline__ void table_ld_f16(const __half* p, float* t) {
         const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
         t[0] = a.x; t[1] = a.y; t[2] = b.x; t[3] = b.y;
     }
+}
+
+// Packed half2 add without a returned value (red, not atom).
+__device__ __forceinline__ void red_add_f16x2(__half2* p, __half2 v) {
+    asm volatile("red.global.add.noftz.f16x2 [%0], %1;" ::"l"(p), "r"(*reinterpret_cast<const uint32_t*>(&v))
+                 : "memory");
 }
 
 template <int F, int LG = 16>
@@ -801,7 +806,7 @@ __global__ void __launch_bounds__(256) hash_bwd_f16_kernel(const DevConfig c, __
             const float w = k.w[cc];
             __half2* dst = reinterpret_cast<__half2*>(grad + k.base[cc]);
 #pragma unroll
-            for (int f = 0; f < F; f += 2) atomicAdd(dst + f / 2, __floats2half2_rn(gf[f] * w, gf[f + 1] * w));
+            for (int f = 0; f < F; f += 2) red_add_f16x2(dst + f / 2, __floats2half2_rn(gf[f] * w, gf[f + 1] * w));
         }
     }
 }

@@ -194,20 +194,81 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
     }
 }
 
-// Hash-grid gradient from the ACC region (scaled deltas times Wd_in), 16 features at a time,
-// scattered with vector atomics (ffnerf_OG.cl:2090-2173).  On the coarse levels (lvl < DEDUP_LEVELS)
-// the lanes of a warp -- consecutive samples of one ray -- often sit in the same grid cell and would
-// add to the same 8 table entries: such lanes are grouped (match on the cell), each writes its 8 x F
-// contributions to its row of `scratch` (shared memory, 8 F floats per thread), and the group's
-// first lane adds the group's sums with one set of atomics.  Finer levels add directly.
+// Scatter of one level's hash-grid gradient (ffnerf_OG.cl:2090-2173): the thread's F raw feature
+// gradients `gl` become (coef_l * g) * w_c at the 8 trilinear corners, added with vector atomics.
+// On the coarse levels (lvl < DEDUP_LEVELS) the lanes of a warp -- consecutive samples of one ray --
+// often sit in the same grid cell and would add to the same 8 table entries: such lanes are grouped
+// (match on the cell), each writes its 8 x F contributions to its row of `scratch` (shared memory,
+// 8 F floats per thread), and the group's first lane adds the group's sums with one set of atomics.
+// Finer levels add directly.
 constexpr int DEDUP_LEVELS = 10;
+template <int F>
+__device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restrict__ grad, V3 p, int lvl,
+                                              const float* gl, const float* coef, float* scratch) {
+    const int lid = threadIdx.x & 31;
+    float* row = scratch + threadIdx.x * (8 * F);
+    float gf[F];
+    bool any = false;
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+        const float v = gl[f];
+        gf[f] = isfinite(v) ? coef[lvl] * v : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
+        any |= gf[f] != 0.0f;
+    }
+    if (!any) return;
+    Corner8 k;
+    uint32_t key;
+    level_corners<F>(c, p, lvl, k, &key);
+    unsigned grp = 1u << lid;
+    if (lvl < DEDUP_LEVELS) grp = __match_any_sync(__activemask(), key);
+    if (grp == (1u << lid)) {
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const float w = k.w[cc];
+            if constexpr (F == 2)
+                red_add2(grad + k.base[cc], gf[0] * w, gf[1] * w);
+            else
+                red_add4(grad + k.base[cc], gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w);
+        }
+        return;
+    }
+    float v[8 * F];
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc)
+#pragma unroll
+        for (int f = 0; f < F; ++f) v[cc * F + f] = gf[f] * k.w[cc];
+#pragma unroll
+    for (int q = 0; q < 8 * F; q += 4) *reinterpret_cast<float4*>(row + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+    __syncwarp(grp);
+    if (lid == __ffs(grp) - 1) {
+        unsigned rest = grp & (grp - 1u);   // the other members
+        while (rest) {
+            const int m = __ffs(rest) - 1;
+            rest &= rest - 1u;
+            const float* r = scratch + ((threadIdx.x & ~31u) + m) * (8 * F);
+#pragma unroll
+            for (int q = 0; q < 8 * F; q += 4) {
+                const float4 t = *reinterpret_cast<const float4*>(r + q);
+                v[q] += t.x; v[q + 1] += t.y; v[q + 2] += t.z; v[q + 3] += t.w;
+            }
+        }
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            if constexpr (F == 2)
+                red_add2(grad + k.base[cc], v[2 * cc], v[2 * cc + 1]);
+            else
+                red_add4(grad + k.base[cc], v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+        }
+    }
+    __syncwarp(grp);
+}
+
+// Hash-grid gradient from the ACC region (scaled deltas times Wd_in), 16 features at a time.
 template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
                                                   V3 p, float unscale, const float* coef, float* scratch) {
     constexpr int LPOS = L * F, LV = 16 / F;
     const uint32_t lane = (threadIdx.x & ~31u) << 16;
-    const int lid = threadIdx.x & 31;
-    float* row = scratch + threadIdx.x * (8 * F);
 #pragma unroll 1
     for (int j = 0; j < LPOS; j += 16) {
         float g[16];
@@ -215,63 +276,10 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
         tc::tmem_wait_ld();
 #pragma unroll
         for (int li = 0; li < LV; ++li) {
-            const int lvl = j / F + li;
-            float gf[F];
-            bool any = false;
+            float gl[F];
 #pragma unroll
-            for (int f = 0; f < F; ++f) {
-                const float v = g[li * F + f] * unscale;
-                gf[f] = isfinite(v) ? coef[lvl] * v : 0.0f;   // non-finite features are skipped (ffnerf_OG.cl:2162)
-                any |= gf[f] != 0.0f;
-            }
-            if (!any) continue;
-            Corner8 k;
-            uint32_t key;
-            level_corners<F>(c, p, lvl, k, &key);
-            unsigned grp = 1u << lid;
-            if (lvl < DEDUP_LEVELS) grp = __match_any_sync(__activemask(), key);
-            if (grp == (1u << lid)) {
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    const float w = k.w[cc];
-                    if constexpr (F == 2)
-                        atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(gf[0] * w, gf[1] * w));
-                    else
-                        atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
-                                  make_float4(gf[0] * w, gf[1] * w, gf[2] * w, gf[3] * w));
-                }
-                continue;
-            }
-            float v[8 * F];
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc)
-#pragma unroll
-                for (int f = 0; f < F; ++f) v[cc * F + f] = gf[f] * k.w[cc];
-#pragma unroll
-            for (int q = 0; q < 8 * F; q += 4) *reinterpret_cast<float4*>(row + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-            __syncwarp(grp);
-            if (lid == __ffs(grp) - 1) {
-                unsigned rest = grp & (grp - 1u);   // the other members
-                while (rest) {
-                    const int m = __ffs(rest) - 1;
-                    rest &= rest - 1u;
-                    const float* r = scratch + ((threadIdx.x & ~31u) + m) * (8 * F);
-#pragma unroll
-                    for (int q = 0; q < 8 * F; q += 4) {
-                        const float4 t = *reinterpret_cast<const float4*>(r + q);
-                        v[q] += t.x; v[q + 1] += t.y; v[q + 2] += t.z; v[q + 3] += t.w;
-                    }
-                }
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc) {
-                    if constexpr (F == 2)
-                        atomicAdd(reinterpret_cast<float2*>(grad + k.base[cc]), make_float2(v[2 * cc], v[2 * cc + 1]));
-                    else
-                        atomicAdd(reinterpret_cast<float4*>(grad + k.base[cc]),
-                                  make_float4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]));
-                }
-            }
-            __syncwarp(grp);
+            for (int f = 0; f < F; ++f) gl[f] = g[li * F + f] * unscale;
+            scatter_level<F>(c, grad, p, j / F + li, gl, coef, scratch);
         }
     }
 }

@@ -89,10 +89,10 @@ SYNTHETIC = {"cfg1": dict(n_cams=8, W=64, H=64, log2T=14, rmax=512.0, G=64),
              "cfg2": dict(n_cams=56, W=800, H=450, log2T=19, rmax=2048.0, G=128)}
 
 
-def synthetic_scene_views(workload: str = "cfg1", seed: int = 0):
+def synthetic_scene_views(workload: str = "cfg1", seed: int = 0, device: str = "cuda"):
     """The seeded synthetic Gaussian-blob scene of the benchmark configurations (cfg1: 8 cameras
     at 64x64 on a radius-2 sphere; cfg2: 56 cameras at 450x800 on a ring), rendered analytically
-    on the device into 8-bit images (the reference's loader quantises too).
+    on `device` into 8-bit images (the reference's loader quantises too).
     Returns (images uint8 [n, H, W, 3], c2w [n, 4, 4], K [3, 3], W, H)."""
     import torch
     from synthetic_scene import BlobScene, cameras_ring, cameras_sphere, intrinsics, pixel_rays
@@ -103,20 +103,21 @@ def synthetic_scene_views(workload: str = "cfg1", seed: int = 0):
     vv, uu = np.mgrid[0:wl["H"], 0:wl["W"]]
     images = []
     for c in cams:
-        rgb = scene.render_torch(torch.from_numpy(pixel_rays(c, K, uu.ravel(), vv.ravel())).cuda(), n_quad=192)
+        rgb = scene.render_torch(torch.from_numpy(pixel_rays(c, K, uu.ravel(), vv.ravel())).to(device), n_quad=192)
         images.append(torch.round(rgb.clamp(0, 1) * 255).to(torch.uint8).cpu().numpy().reshape(wl["H"], wl["W"], 3))
     return np.stack(images), np.asarray(cams, np.float32), K, wl["W"], wl["H"]
 
 
 def synthetic_nerf(workload: str = "cfg1", mlp_precision: str = "fp16", seed: int = 0,
-                   training_dir: str | None = None, table_update: str = "immediate"):
+                   training_dir: str | None = None, table_update: str = "immediate", host_only: bool = False):
     """A fresh ffnerf_tools.Nerf for the synthetic scene's geometry: hash L=16 F=2 (T and Rmax of
-    the workload), ND=1, NC=2, random background, box [-1, 1]^3, near clip 0.3, rng seed 777+seed."""
+    the workload), ND=1, NC=2, random background, box [-1, 1]^3, near clip 0.3, rng seed 777+seed.
+    host_only: no device or queue (the host state, seeds and schedules only)."""
     import tempfile
     import ffnerf_tools as ft
     wl = SYNTHETIC[workload]
-    ctx = ft.Context([ft.Device(0)])
-    queue = ft.CommandQueue(ctx)
+    ctx = None if host_only else ft.Context([ft.Device(0)])
+    queue = None if host_only else ft.CommandQueue(ctx)
     occ = ft.OccParams(G_occ=wl["G"], box_min=np.array([-1, -1, -1], np.float32),
                        box_max=np.array([1, 1, 1], np.float32), rho_min=np.float32(1.0),
                        rho_max=np.float32(16.0), t_near_clip=np.float32(0.3)).finalize()
