@@ -42,8 +42,9 @@ struct TcPlan {
     static constexpr int C2 = C1 + ROWS * 64 * 2;             // colour hidden 2 [128 x 64]
     static constexpr int DC = C2 + ROWS * 64 * 2;             // output delta [128 x 16]
     static constexpr int ONES = DC + ROWS * 16 * 2;           // one-hot [128 x 8]
+    static constexpr int X0B = ONES + ROWS * 8 * 2;           // second X0 tile (staged form: the next tile)
     // fp16 weights, rows = outputs, columns = inputs
-    static constexpr int W_DIN = ONES + ROWS * 8 * 2;         // [64 x LPOS]
+    static constexpr int W_DIN = X0B + ROWS * LPOS * 2;       // [64 x LPOS]
     static constexpr int W_D01 = W_DIN + 64 * LPOS * 2;       // [64 x 64] (ND = 2)
     static constexpr int W_DOUT = W_D01 + (ND >= 2 ? 64 * 64 * 2 : 0);   // [16 x 64]
     static constexpr int W_CIN = W_DOUT + 16 * 64 * 2;        // [64 x 32]
@@ -284,6 +285,13 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
     }
 }
 
+// 16-byte global -> shared copies that complete in the background (cp.async, L2 only).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 template <int F, int ND, bool STAGED = false>
 __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a) {
     using PL = TcPlan<F, ND>;
@@ -389,32 +397,65 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
     uint32_t* sChg = reinterpret_cast<uint32_t*>(sAffE + 128);
     float* sRay = reinterpret_cast<float*>(sChg + 16);
 
+    // Staged form: while a tile runs, the next tile's X0 is copied into the other X0 buffer
+    // (cp.async) and its per-sample inputs are loaded into registers.
+    int xb = 0;
+    float2 nx_tdt = make_float2(0.f, 0.f);
+    uint4 nx_rst = make_uint4(0u, 0u, 0u, 0u);
+    float4 nx_ro = make_float4(0.f, 0.f, 0.f, 0.f), nx_rd = make_float4(0.f, 0.f, 1.f, 0.f);
+    auto prefetch = [&](int t, int buf) {
+        const uint32_t ri = (uint32_t)t * rays_per_tile + rl;
+        nx_tdt = make_float2(0.f, 0.f);
+        nx_rst = make_uint4(0u, 0u, 0u, 0u);
+        nx_ro = make_float4(0.f, 0.f, 0.f, 0.f);
+        nx_rd = make_float4(0.f, 0.f, 1.f, 0.f);
+        if (ri < a.n_rays) {
+            nx_tdt = a.tdt_stage[(size_t)t * 128 + tid];
+            nx_rst = a.ray_stage[ri];
+            nx_ro = a.rays[2 * ri];
+            nx_rd = a.rays[2 * ri + 1];
+        }
+        const unsigned char* src = a.x0_stage + (size_t)t * (128 * LPOS * 2);
+        const uint32_t dst = S(buf ? PL::X0B : PL::X0);
+#pragma unroll
+        for (int k = tid; k < 128 * LPOS * 2 / 16; k += 128) cp_async16(dst + 16u * (uint32_t)k, src + 16 * k);
+        cp_async_commit();
+    };
+    if constexpr (STAGED) {
+        if ((int)blockIdx.x < n_tiles) prefetch(blockIdx.x, 0);
+    }
+
     for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
         const uint32_t ray_idx = (uint32_t)tile * rays_per_tile + rl;
         const bool valid = ray_idx < a.n_rays;
         const uint32_t ray_id = a.ray_offset + ray_idx;
+        const int x0_off = STAGED && xb ? PL::X0B : PL::X0;   // this tile's X0 buffer
         float4 ro = make_float4(0.f, 0.f, 0.f, 0.f), rd = make_float4(0.f, 0.f, 1.f, 0.f);
-        if (valid) { ro = a.rays[2 * ray_idx]; rd = a.rays[2 * ray_idx + 1]; }
+        if constexpr (STAGED) {
+            ro = nx_ro;
+            rd = nx_rd;
+        } else if (valid) {
+            ro = a.rays[2 * ray_idx];
+            rd = a.rays[2 * ray_idx + 1];
+        }
         const V3 o = v3(ro.x, ro.y, ro.z), d = v3(rd.x, rd.y, rd.z);
         RayTile R{sCand, sCdf, sTs, sDTs, sTr, sKey, sSeg, sAffS, sAffE, sChg, sRay, tid, spr, rl, lid, rbase,
                   ray_idx, ray_id, valid, train, probe, o, d, bmin, bmax, bsize, inv_box, (float)c.G, 1.0f / (float)spr};
         bool hit;
         int idx_sel = 0;
         if constexpr (STAGED) {
-            // sampling and encoding were done by the stage kernels: load their results
-            const size_t s = (size_t)tile * 128 + tid;
-            float2 tdt = make_float2(0.f, 0.f);
-            uint4 rst = make_uint4(0u, 0u, 0u, 0u);
-            if (valid) { tdt = a.tdt_stage[s]; rst = a.ray_stage[ray_idx]; }
+            // sampling and encoding were done by the stage kernels: their results were prefetched
+            const float2 tdt = nx_tdt;
+            const uint4 rst = nx_rst;
             sTs[tid] = tdt.x;
             sDTs[tid] = tdt.y;
             if (lid == 0) { sChg[rl * 2] = rst.x; sChg[rl * 2 + 1] = rst.y; }
             hit = rst.z != 0u;
-            const uint4* src = reinterpret_cast<const uint4*>(a.x0_stage + (size_t)tile * (128 * LPOS * 2));
-            uint4* dst = reinterpret_cast<uint4*>(tX0);
-#pragma unroll
-            for (int k = tid; k < 128 * LPOS * 2 / 16; k += 128) dst[k] = __ldcs(src + k);
+            cp_async_wait_all();
             __syncthreads();
+            // the other buffer was last read by the previous tile's MMAs, which have completed
+            if (tile + (int)gridDim.x < n_tiles) prefetch(tile + (int)gridDim.x, xb ^ 1);
+            xb ^= 1;
         } else {
             ray_sampler(a, R, hit, idx_sel);
         }
@@ -433,7 +474,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         } else {
             if constexpr (!STAGED) encode_rows<F>(c, a.table, pn, hit, tX0);
             handoff();
-            if (tid == 0) gemm(tmem + PL::ACC, S(PL::X0), LPOS, false, S(PL::W_DIN), LPOS, false, 128, 64, LPOS, 0);
+            if (tid == 0) gemm(tmem + PL::ACC, S(x0_off), LPOS, false, S(PL::W_DIN), LPOS, false, 128, 64, LPOS, 0);
             sync_mma();
             epi_bias_relu(tmem, PL::ACC, 64, bias, tH(0), 64, 1.0f / INPUT_SCALE);
             if (ND >= 2) {
@@ -599,7 +640,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         }
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_DIN, S(PL::HD), 64, true, S(PL::X0), LPOS, true, 64, LPOS, 128, acc0);  // dWd_in
+            gemm(tmem + PL::DW_DIN, S(PL::HD), 64, true, S(x0_off), LPOS, true, 64, LPOS, 128, acc0);  // dWd_in
             gemm(tmem + PL::B_D0, S(PL::HD), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);       // dbd_0
             gemm(tmem + PL::ACC, S(PL::HD), 64, false, S(PL::W_DIN), LPOS, true, 128, LPOS, 64, 0);    // hash grads
         }
@@ -613,6 +654,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         __syncthreads();
     }
 
+    if constexpr (STAGED) cp_async_wait_all();      // a prefetch left by an early exit
     // ---- weight-gradient partials of this CTA: TMEM (M = 64 layout) -> global, unscaled
     if (backward && a.partials) {
         float* part = a.partials + (size_t)blockIdx.x * lo.total;
