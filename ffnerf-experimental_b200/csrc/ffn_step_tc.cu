@@ -199,9 +199,10 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
 // gradients `gl` become (coef_l * g) * w_c at the 8 trilinear corners, added with vector atomics.
 // On the coarse levels (lvl < DEDUP_LEVELS) the lanes of a warp -- consecutive samples of one ray --
 // often sit in the same grid cell and would add to the same 8 table entries: such lanes are grouped
-// (match on the cell), each writes its 8 x F contributions to its row of `scratch` (shared memory,
-// 8 F floats per thread), and the group's first lane adds the group's sums with one set of atomics.
-// Finer levels add directly.
+// (match on the cell) and the group's first lane adds the group's sums with one set of atomics.  The
+// sums are formed by shuffles when every group is a run of consecutive lanes, else through
+// `scratch` (each lane writes its 8 x F contributions to its shared-memory row, 8 F floats per
+// thread, and the first lane adds the other rows).  Finer levels add directly.
 constexpr int DEDUP_LEVELS = 10;
 template <int F>
 __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restrict__ grad, V3 p, int lvl,
@@ -221,7 +222,39 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
     uint32_t key;
     level_corners<F>(c, p, lvl, k, &key);
     unsigned grp = 1u << lid;
-    if (lvl < DEDUP_LEVELS) grp = __match_any_sync(__activemask(), key);
+    if (lvl < DEDUP_LEVELS) {
+        const unsigned act = __activemask();
+        grp = __match_any_sync(act, key);
+        // Groups of consecutive lanes (always, when a warp holds samples of one ray): a segmented
+        // suffix sum by shuffles leaves each group's total in its first lane, in log2(group) steps.
+        const int first = __ffs(grp) - 1, last = 31 - __clz(grp);
+        const bool contiguous = (grp >> first) == (0xffffffffu >> (31 - (last - first)));
+        if (__all_sync(act, contiguous)) {
+            const int span = (int)__reduce_max_sync(act, (unsigned)(last - first + 1));
+            if (span > 1) {
+                float v[8 * F];
+#pragma unroll
+                for (int cc = 0; cc < 8; ++cc)
+#pragma unroll
+                    for (int f = 0; f < F; ++f) v[cc * F + f] = gf[f] * k.w[cc];
+                for (int off = 1; off < span; off <<= 1) {
+#pragma unroll
+                    for (int q = 0; q < 8 * F; ++q) {
+                        const float t = __shfl_down_sync(act, v[q], off);
+                        if (lid + off <= last) v[q] += t;
+                    }
+                }
+                if (lid == first) {
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) {
+                        if constexpr (F == 2) red_add2(grad + k.base[cc], v[2 * cc], v[2 * cc + 1]);
+                        else red_add4(grad + k.base[cc], v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+                    }
+                }
+                return;
+            }
+        }
+    }
     if (grp == (1u << lid)) {
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
@@ -264,24 +297,57 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
     __syncwarp(grp);
 }
 
-// Hash-grid gradient from the ACC region (scaled deltas times Wd_in), 16 features at a time.
+// Hash-grid gradient from the ACC region (scaled deltas times Wd_in).  F = 2: the thread's 32 values are
+// first parked in its row of `gbuf` (shared memory, 32 floats per thread, float4 slots XOR-swizzled
+// by the row so that a warp's stores and loads spread over the banks), then the levels are scattered
+// one at a time by a single (not unrolled) copy of the level code: the kernel is large and its
+// instruction cache is a limit.
 template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
-                                                  V3 p, float unscale, const float* coef, float* scratch) {
-    constexpr int LPOS = L * F, LV = 16 / F;
+                                                  V3 p, float unscale, const float* coef, float* scratch, float* gbuf) {
+    constexpr int LPOS = L * F;
     const uint32_t lane = (threadIdx.x & ~31u) << 16;
+    if constexpr (F != 2) {
+        // F = 4: the parked rows would not fit the free C2 tile; levels straight from the TMEM loads
 #pragma unroll 1
+        for (int j = 0; j < LPOS; j += 16) {
+            float g[16];
+            tc::tmem_ld16(tmem + lane + col + j, g);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int li = 0; li < 16 / F; ++li) {
+                float gl[F];
+#pragma unroll
+                for (int f = 0; f < F; ++f) gl[f] = g[li * F + f] * unscale;
+                scatter_level<F>(c, grad, p, j / F + li, gl, coef, scratch);
+            }
+        }
+        return;
+    }
+    const int row = threadIdx.x, sw = row & 7;
+    float4* grow = reinterpret_cast<float4*>(gbuf + row * LPOS);
+#pragma unroll
     for (int j = 0; j < LPOS; j += 16) {
         float g[16];
         tc::tmem_ld16(tmem + lane + col + j, g);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int li = 0; li < LV; ++li) {
-            float gl[F];
-#pragma unroll
-            for (int f = 0; f < F; ++f) gl[f] = g[li * F + f] * unscale;
-            scatter_level<F>(c, grad, p, j / F + li, gl, coef, scratch);
+        for (int q = 0; q < 16; q += 4)
+            grow[((j + q) / 4) ^ (sw % (LPOS / 4))] =
+                make_float4(g[q] * unscale, g[q + 1] * unscale, g[q + 2] * unscale, g[q + 3] * unscale);
+    }
+#pragma unroll 1
+    for (int lvl = 0; lvl < L; ++lvl) {
+        const float4 t = grow[((lvl * F) / 4) ^ (sw % (LPOS / 4))];
+        float gl[F];
+        if constexpr (F == 2) {
+            const bool hi = (lvl & 1) != 0;
+            gl[0] = hi ? t.z : t.x;
+            gl[1] = hi ? t.w : t.y;
+        } else {
+            gl[0] = t.x; gl[1] = t.y; gl[2] = t.z; gl[3] = t.w;
         }
+        scatter_level<F>(c, grad, p, lvl, gl, coef, scratch);
     }
 }
 
@@ -646,10 +712,11 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         }
         sync_mma();
         dw_started = true;
-        // the activation tiles are dead once the last MMAs completed: C1 holds the scatter's exchange rows
+        // the activation tiles are dead once the last MMAs completed: C1 holds the scatter's exchange
+        // rows, C2 the parked gradients
         if (hit && valid)
             scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef,
-                                 reinterpret_cast<float*>(tC1));
+                                 reinterpret_cast<float*>(tC1), reinterpret_cast<float*>(tC2));
         tc::fence_before_sync();
         __syncthreads();
     }
