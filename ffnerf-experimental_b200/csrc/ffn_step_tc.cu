@@ -125,34 +125,40 @@ __device__ __forceinline__ void load_row_h(const unsigned char* tile, int cols, 
     for (int c = 0; c < N; c += 8) tc::ld_chunk8(tile, threadIdx.x, c, cols, v + c);
 }
 
-// Epilogue of a forward layer: row = relu(ACC * in_scale + bias) for N columns, 16 at a time.
+// Epilogue of a forward layer: row = relu(ACC * in_scale + bias) for N columns, 32 at a time (two
+// TMEM loads per wait; one copy of the loop body, to keep the kernel's code small).
 __device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N, const float* bias, unsigned char* tile,
                                               int cols, float in_scale = 1.0f) {
     const uint32_t lane = (threadIdx.x & ~31u) << 16;
-    for (int j = 0; j < N; j += 16) {
-        float v[16];
-        tc::tmem_ld16(tmem + lane + col + j, v);
+#pragma unroll 1
+    for (int j = 0; j < N; j += 32) {
+        float v[32];
+        tc::tmem_ld16(tmem + lane + col + j, *reinterpret_cast<float(*)[16]>(v));
+        tc::tmem_ld16(tmem + lane + col + j + 16, *reinterpret_cast<float(*)[16]>(v + 16));
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = fmaxf(fmaf(v[i], in_scale, bias[j + i]), 0.0f);
-        tc::st_chunk8(tile, threadIdx.x, j, cols, v);
-        tc::st_chunk8(tile, threadIdx.x, j + 8, cols, v + 8);
+        for (int i = 0; i < 32; ++i) v[i] = fmaxf(fmaf(v[i], in_scale, bias[j + i]), 0.0f);
+#pragma unroll
+        for (int q = 0; q < 32; q += 8) tc::st_chunk8(tile, threadIdx.x, j + q, cols, v + q);
     }
 }
 
-// Epilogue of a backward layer: row = ACC masked by (activation in `tile` > 0), written in place.
+// Epilogue of a backward layer: row = ACC masked by (activation in `tile` > 0), written in place,
+// 32 columns at a time.
 __device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N, unsigned char* tile, int cols) {
     const uint32_t lane = (threadIdx.x & ~31u) << 16;
-    for (int j = 0; j < N; j += 16) {
-        float v[16], act[16];
-        tc::tmem_ld16(tmem + lane + col + j, v);
-        tc::ld_chunk8(tile, threadIdx.x, j, cols, act);
-        tc::ld_chunk8(tile, threadIdx.x, j + 8, cols, act + 8);
+#pragma unroll 1
+    for (int j = 0; j < N; j += 32) {
+        float v[32], act[32];
+        tc::tmem_ld16(tmem + lane + col + j, *reinterpret_cast<float(*)[16]>(v));
+        tc::tmem_ld16(tmem + lane + col + j + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+#pragma unroll
+        for (int q = 0; q < 32; q += 8) tc::ld_chunk8(tile, threadIdx.x, j + q, cols, act + q);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = act[i] > 0.0f ? v[i] : 0.0f;
-        tc::st_chunk8(tile, threadIdx.x, j, cols, v);
-        tc::st_chunk8(tile, threadIdx.x, j + 8, cols, v + 8);
+        for (int i = 0; i < 32; ++i) v[i] = act[i] > 0.0f ? v[i] : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 32; q += 8) tc::st_chunk8(tile, threadIdx.x, j + q, cols, v + q);
     }
 }
 
