@@ -130,6 +130,78 @@ __device__ __forceinline__ void scan_excl_aff_rev(float2* s, int lid, int n) {
     }
 }
 
+// The two scans above with warp shuffles, for rays of n = 2^k samples (2 <= n <= 64): the same
+// up-sweep / down-sweep tree, so every combine sees the same operands in the same order and the
+// results are bit-identical to the shared-memory form, with one exchange through shared memory for
+// the stride that crosses two warps (n = 64) instead of a block barrier at every stride.  The element
+// at position p of the ray is held by this thread; dir = +1 when positions ascend with the lanes,
+// -1 when they descend (the reversed scan).  xchg: 2 slots of shared memory per ray.  All threads of
+// the block call it (it contains block barriers when n = 64).
+__device__ __forceinline__ float4 shfl_up4(float4 v, int s) {
+    return make_float4(__shfl_up_sync(0xffffffffu, v.x, s), __shfl_up_sync(0xffffffffu, v.y, s),
+                       __shfl_up_sync(0xffffffffu, v.z, s), __shfl_up_sync(0xffffffffu, v.w, s));
+}
+__device__ __forceinline__ float4 shfl_down4(float4 v, int s) {
+    return make_float4(__shfl_down_sync(0xffffffffu, v.x, s), __shfl_down_sync(0xffffffffu, v.y, s),
+                       __shfl_down_sync(0xffffffffu, v.z, s), __shfl_down_sync(0xffffffffu, v.w, s));
+}
+__device__ __forceinline__ float4 shfl_idx4(float4 v, int l) {
+    return make_float4(__shfl_sync(0xffffffffu, v.x, l), __shfl_sync(0xffffffffu, v.y, l),
+                       __shfl_sync(0xffffffffu, v.z, l), __shfl_sync(0xffffffffu, v.w, l));
+}
+__device__ __forceinline__ float2 shfl_up2(float2 v, int s) {
+    return make_float2(__shfl_up_sync(0xffffffffu, v.x, s), __shfl_up_sync(0xffffffffu, v.y, s));
+}
+__device__ __forceinline__ float2 shfl_down2(float2 v, int s) {
+    return make_float2(__shfl_down_sync(0xffffffffu, v.x, s), __shfl_down_sync(0xffffffffu, v.y, s));
+}
+__device__ __forceinline__ float2 shfl_idx2(float2 v, int l) {
+    return make_float2(__shfl_sync(0xffffffffu, v.x, l), __shfl_sync(0xffffffffu, v.y, l));
+}
+__device__ __forceinline__ float4 shfl_up_t(float4 v, int s) { return shfl_up4(v, s); }
+__device__ __forceinline__ float4 shfl_down_t(float4 v, int s) { return shfl_down4(v, s); }
+__device__ __forceinline__ float4 shfl_idx_t(float4 v, int l) { return shfl_idx4(v, l); }
+__device__ __forceinline__ float2 shfl_up_t(float2 v, int s) { return shfl_up2(v, s); }
+__device__ __forceinline__ float2 shfl_down_t(float2 v, int s) { return shfl_down2(v, s); }
+__device__ __forceinline__ float2 shfl_idx_t(float2 v, int l) { return shfl_idx2(v, l); }
+
+template <typename T, typename Comb>
+__device__ __forceinline__ T scan_excl_warp(T v, int p, int n, int dir, T ident, T* xchg, T& total, Comb comb) {
+    const int lim = n < 32 ? n : 32;
+    for (int s = 1; s < lim; s <<= 1) {                        // up-sweep, strides inside a warp
+        const T lo = dir > 0 ? shfl_up_t(v, s) : shfl_down_t(v, s);   // the element at p - s
+        if (((p + 1) & (2 * s - 1)) == 0) v = comb(lo, v);
+    }
+    if (n == 64) {                                             // stride 32: across the two warps
+        if (p == 31) xchg[0] = v;
+        __syncthreads();
+        if (p == 63) { v = comb(xchg[0], v); xchg[1] = v; }
+        __syncthreads();
+        total = xchg[1];
+        // down-sweep stride 32: position 31 takes position 63's value (the identity), position 63
+        // takes comb(position 31, identity)
+        if (p == 63) v = comb(xchg[0], ident);
+        else if (p == 31) v = ident;
+    } else {
+        const int lane = threadIdx.x & 31;
+        total = shfl_idx_t(v, dir > 0 ? lane - p + (n - 1) : lane + p - (n - 1));
+        if (p == n - 1) v = ident;
+    }
+    for (int s = lim >> 1; s >= 1; s >>= 1) {                  // down-sweep, strides inside a warp
+        const T lo = dir > 0 ? shfl_up_t(v, s) : shfl_down_t(v, s);   // the element at p - s
+        const T hi = dir > 0 ? shfl_down_t(v, s) : shfl_up_t(v, s);   // the element at p + s
+        if (((p + 1) & (2 * s - 1)) == 0) v = comb(lo, v);
+        else if (((p + 1 + s) & (2 * s - 1)) == 0) v = hi;
+    }
+    return v;
+}
+struct SegCombine {
+    __device__ __forceinline__ float4 operator()(float4 l, float4 r) const { return seg_combine(l, r); }
+};
+struct AffCombineRev {
+    __device__ __forceinline__ float2 operator()(float2 l, float2 r) const { return aff_combine_rev(l, r); }
+};
+
 // ray_aabb_intersect (ffnerf_OG.cl:322-343)
 __device__ __forceinline__ bool ray_aabb(V3 o, V3 d, V3 bmin, V3 bmax, float* t0, float* t1) {
     const float inf = __int_as_float(0x7f800000);
@@ -340,10 +412,20 @@ __device__ __forceinline__ void ray_composite(const StepArgs& a, const RayTile& 
     float alpha = 0.0f;
     if (dt_s > 0.0f) alpha = fs(1.0f, own_expf(fclamp(fm(-sigma, dt_s), -5.0f, 18.0f)));
     const float oma = fs(1.0f, alpha);
-    sSeg[tid] = make_float4(oma, fm(alpha, rgb[0]), fm(alpha, rgb[1]), fm(alpha, rgb[2]));
-    __syncthreads();
-    const float4 total = scan_excl_seg(sSeg + rbase, lid, spr);
-    const float T_s = sSeg[tid].x;
+    const bool warp_scan = spr >= 2 && spr <= 64 && (spr & (spr - 1)) == 0;   // uniform over the block
+    float4 total;
+    float T_s;
+    if (warp_scan) {
+        const float4 ex = scan_excl_warp(make_float4(oma, fm(alpha, rgb[0]), fm(alpha, rgb[1]), fm(alpha, rgb[2])),
+                                         lid, spr, 1, make_float4(1.0f, 0.0f, 0.0f, 0.0f), sSeg + rbase, total,
+                                         SegCombine());
+        T_s = ex.x;
+    } else {
+        sSeg[tid] = make_float4(oma, fm(alpha, rgb[0]), fm(alpha, rgb[1]), fm(alpha, rgb[2]));
+        __syncthreads();
+        total = scan_excl_seg(sSeg + rbase, lid, spr);
+        T_s = sSeg[tid].x;
+    }
     T_s_out = T_s;
     sTr[tid] = T_s;
     const float T_final = total.x;
@@ -387,10 +469,16 @@ __device__ __forceinline__ void ray_composite(const StepArgs& a, const RayTile& 
         const float B_s = fa(fa(fm(gr0, fm(alpha, rgb[0])), fm(gr1, fm(alpha, rgb[1]))), fm(gr2, fm(alpha, rgb[2])));
         const int k = spr - 1 - lid;
         sAffE[rbase + k] = make_float2(oma, B_s);
-        sAffS[rbase + k] = make_float2(oma, B_s);
+        if (warp_scan) {
+            float2 unused;
+            sAffS[rbase + k] = scan_excl_warp(make_float2(oma, B_s), k, spr, -1, make_float2(1.0f, 0.0f),
+                                              reinterpret_cast<float2*>(sSeg + rbase), unused, AffCombineRev());
+        } else {
+            sAffS[rbase + k] = make_float2(oma, B_s);
+        }
     }
     __syncthreads();
-    scan_excl_aff_rev(sAffS + rbase, lid, spr);
+    if (!warp_scan) scan_excl_aff_rev(sAffS + rbase, lid, spr);
     float dLds;
     {
         const int k = spr - 1 - lid;
