@@ -165,6 +165,10 @@ __device__ __forceinline__ float2 shfl_up_t(float2 v, int s) { return shfl_up2(v
 __device__ __forceinline__ float2 shfl_down_t(float2 v, int s) { return shfl_down2(v, s); }
 __device__ __forceinline__ float2 shfl_idx_t(float2 v, int l) { return shfl_idx2(v, l); }
 
+__device__ __forceinline__ float shfl_up_t(float v, int s) { return __shfl_up_sync(0xffffffffu, v, s); }
+__device__ __forceinline__ float shfl_down_t(float v, int s) { return __shfl_down_sync(0xffffffffu, v, s); }
+__device__ __forceinline__ float shfl_idx_t(float v, int l) { return __shfl_sync(0xffffffffu, v, l); }
+
 template <typename T, typename Comb>
 __device__ __forceinline__ T scan_excl_warp(T v, int p, int n, int dir, T ident, T* xchg, T& total, Comb comb) {
     const int lim = n < 32 ? n : 32;
@@ -194,6 +198,32 @@ __device__ __forceinline__ T scan_excl_warp(T v, int p, int n, int dir, T ident,
         else if (((p + 1 + s) & (2 * s - 1)) == 0) v = hi;
     }
     return v;
+}
+// scan_excl's combine: a[idx] = a[idx] + a[idx - stride]
+struct AddCombine {
+    __device__ __forceinline__ float operator()(float lo, float v) const { return fa(v, lo); }
+};
+// reduce_sum with warp shuffles for rays of n = 2^k samples (2 <= n <= 64): the same tree
+// (a[p] += a[p + stride], stride n/2 .. 1), the stride 32 of n = 64 through shared memory (xchg: 33
+// floats per ray); every lane of the ray gets the sum.  All threads of the block call it.
+__device__ __forceinline__ float reduce_sum_warp(float v, int p, int n, float* xchg) {
+    int s = n >> 1;
+    if (n == 64) {
+        if (p >= 32) xchg[p - 32] = v;
+        __syncthreads();
+        if (p < 32) v = fa(v, xchg[p]);
+        s = 16;
+    }
+    for (; s >= 1; s >>= 1) {
+        const float t = __shfl_down_sync(0xffffffffu, v, s);
+        if (p < s) v = fa(v, t);
+    }
+    if (n == 64) {
+        if (p == 0) xchg[32] = v;
+        __syncthreads();
+        return xchg[32];
+    }
+    return __shfl_sync(0xffffffffu, v, (int)(threadIdx.x & 31) - p);
 }
 struct SegCombine {
     __device__ __forceinline__ float4 operator()(float4 l, float4 r) const { return seg_combine(l, r); }
@@ -322,33 +352,54 @@ __device__ __forceinline__ void ray_sampler(const StepArgs& a, const RayTile& R,
         }
         sCand[tid] = tk;
         float* cdf = sCdf + rbase;
-        sCdf[tid] = wp;
-        __syncthreads();
-        scan_excl(cdf, lid, spr);
-        const float pref = sCdf[tid];
-        sCdf[tid] = wp;
-        __syncthreads();
-        const float Wtot = fmaxf(reduce_sum(cdf, lid, spr), 1.0e-12f);
-        __syncthreads();
-        const float pi = fclamp(fd(pref, Wtot), 0.0f, 1.0f);
-        const float g = fm(wp, own_expf(fm(-0.0f, pi)));        // LAMBDA_FOCUS = 0
-        sCdf[tid] = g;
-        __syncthreads();
-        const float gtot = fmaxf(reduce_sum(cdf, lid, spr), 1.0e-12f);
-        __syncthreads();
-        sCdf[tid] = active;
-        __syncthreads();
-        const float active_count = reduce_sum(cdf, lid, spr);
-        __syncthreads();
+        // scans and sums by warp shuffles for power-of-two rays (the same trees, bit-identical),
+        // else through shared memory with a barrier per stride
+        const bool warp_scan = spr >= 2 && spr <= 64 && (spr & (spr - 1)) == 0;   // uniform over the block
+        float* xs = reinterpret_cast<float*>(sSeg + rbase);   // exchange slots: scans [0, 2), sums [4, 37)
+        float pref, Wtot, g, gtot, active_count;
+        if (warp_scan) {
+            float unused;
+            pref = scan_excl_warp(wp, lid, spr, 1, 0.0f, xs, unused, AddCombine());
+            Wtot = fmaxf(reduce_sum_warp(wp, lid, spr, xs + 4), 1.0e-12f);
+            const float pi = fclamp(fd(pref, Wtot), 0.0f, 1.0f);
+            g = fm(wp, own_expf(fm(-0.0f, pi)));        // LAMBDA_FOCUS = 0
+            gtot = fmaxf(reduce_sum_warp(g, lid, spr, xs + 4), 1.0e-12f);
+            active_count = reduce_sum_warp(active, lid, spr, xs + 4);
+        } else {
+            sCdf[tid] = wp;
+            __syncthreads();
+            scan_excl(cdf, lid, spr);
+            pref = sCdf[tid];
+            sCdf[tid] = wp;
+            __syncthreads();
+            Wtot = fmaxf(reduce_sum(cdf, lid, spr), 1.0e-12f);
+            __syncthreads();
+            const float pi = fclamp(fd(pref, Wtot), 0.0f, 1.0f);
+            g = fm(wp, own_expf(fm(-0.0f, pi)));        // LAMBDA_FOCUS = 0
+            sCdf[tid] = g;
+            __syncthreads();
+            gtot = fmaxf(reduce_sum(cdf, lid, spr), 1.0e-12f);
+            __syncthreads();
+            sCdf[tid] = active;
+            __syncthreads();
+            active_count = reduce_sum(cdf, lid, spr);
+            __syncthreads();
+        }
         const float any_active = active_count > 0.5f ? 1.0f : 0.0f;
         const float inv_active = fd(1.0f, fmaxf(active_count, 1.0f));
         const float ut = fmix(inv_n, fm(active, inv_active), any_active);
         const float pt = fm(any_active, fd(g, gtot));
         const float p = fa(fm(0.3f, ut), fm(1.0f - 0.3f, pt));  // UNIFORM_PART
-        sCdf[tid] = p;
-        __syncthreads();
-        scan_excl(cdf, lid, spr);
-        sCdf[tid] = fa(sCdf[tid], p);
+        if (warp_scan) {
+            float unused;
+            const float ex = scan_excl_warp(p, lid, spr, 1, 0.0f, xs, unused, AddCombine());
+            sCdf[tid] = fa(ex, p);
+        } else {
+            sCdf[tid] = p;
+            __syncthreads();
+            scan_excl(cdf, lid, spr);
+            sCdf[tid] = fa(sCdf[tid], p);
+        }
         __syncthreads();
         float t_out = 0.0f;
         uint32_t key = 0xFFFFFFFEu;
