@@ -357,6 +357,23 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
     }
 }
 
+// Sums v[0..15] over the warp's 32 lanes by a transposed butterfly (16 shuffles instead of 80): lane
+// l ends with the sum for index (l >> 1) & 15 (lanes l and l ^ 1 hold the same sum).
+__device__ __forceinline__ float warp_sum16(const float (&v)[16]) {
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    float a[8], b[4], e[2];
+    const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0, h4 = (lane & 4) != 0, h2 = (lane & 2) != 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = (h16 ? v[i + 8] : v[i]) + __shfl_xor_sync(full, h16 ? v[i] : v[i + 8], 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = (h8 ? a[i + 4] : a[i]) + __shfl_xor_sync(full, h8 ? a[i] : a[i + 4], 8);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) e[i] = (h4 ? b[i + 2] : b[i]) + __shfl_xor_sync(full, h4 ? b[i] : b[i + 2], 4);
+    float d = (h2 ? e[1] : e[0]) + __shfl_xor_sync(full, h2 ? e[0] : e[1], 2);
+    return d + __shfl_xor_sync(full, d, 1);
+}
+
 // 16-byte global -> shared copies that complete in the background (cp.async, L2 only).
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -682,12 +699,9 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             // delta at the density output replaces the colour input's first 16 columns
 #pragma unroll
             for (int cc = 0; cc < 16; cc += 8) tc::st_chunk8(tXC, tid, cc, 32, v + cc);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                float s = v[k];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                if ((tid & 31) == 0) atomicAdd(bgrad + k, s);
+            {
+                const float sum = warp_sum16(v);
+                if ((tid & 1) == 0) atomicAdd(bgrad + ((tid >> 1) & 15), sum);
             }
         }
         const uint32_t hlast = S(PL::HD + (ND - 1) * 128 * 64 * 2);
