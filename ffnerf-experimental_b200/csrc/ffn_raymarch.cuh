@@ -426,9 +426,22 @@ __device__ __forceinline__ void ray_sampler(const StepArgs& a, const RayTile& R,
         sDTs[tid] = hit ? dtb : 0.0f;
         sKey[tid] = key;
         __syncthreads();
-        if (hit) {
+        const bool pow2 = spr <= 64 && (spr & (spr - 1)) == 0;   // uniform over the block
+        if (pow2) {
+            // run starts as a warp ballot: a warp holds 32 lanes of one ray, or whole rays when spr < 32
+            const bool start = hit && (lid == 0 || sKey[tid] != sKey[tid - 1]);
+            const unsigned m = __ballot_sync(0xffffffffu, start);
+            if (hit) {
+                if (spr >= 32) {
+                    if ((lid & 31) == 0) sChg[rl * 2 + (lid >> 5)] = m;
+                } else if (lid == 0) {
+                    sChg[rl * 2] = (m >> (tid & 31)) & ((1u << spr) - 1u);
+                }
+            }
+        } else if (hit) {
             if (lid == 0 || sKey[tid] != sKey[tid - 1]) atomicOr(sChg + rl * 2 + (lid >> 5), 1u << (lid & 31));
-        } else if (lid < 2) {
+        }
+        if (!hit && lid < 2) {
             // no hit: every sample starts a run (ffnerf_OG.cl:1058-1063)
             const int lo_bit = lid * 32;
             const int nb = min(32, max(0, spr - lo_bit));
