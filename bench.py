@@ -68,6 +68,9 @@ MICRO = {
     "cfg4-T22-f16": dict(kind="hash", points=1 << 22, F=2, log2T=22, rmax=2048.0, table="f16",
                          desc="cfg4: hash encode fwd+bwd, 2^22 points U[0,1]^3, L=16 F=2 T=2^22 fp16 table "
                               "(fp16 encoding out), upstream grads N(0,1) [2^22, 32] fp32"),
+    "cfg5-mlp": dict(kind="mlp", n=1 << 22, desc="cfg5: density (32-64-16) and colour (32-64-64-3) MLPs forward and "
+                                                  "backward with weight gradients on 2^22 samples of N(0,1) fp16 inputs, "
+                                                  "fp16 operands / fp32 accumulation"),
     "cfg5-adam": dict(kind="adam", n=1 << 24, desc="cfg5: Adam over 2^24 fp32 parameters, grads N(0,1e-3), "
                                                     "beta1 0.9 beta2 0.99 eps 1e-15 lr 1e-2"),
 }
@@ -80,6 +83,85 @@ def hash_bytes_per_point(F: int, s_tab: int = 4):
     atomic read-modify-write (fp32: 1164 / 2188 B at F=2; fp16: 588 / 1164 B)."""
     gather = 16 * 8 * F * s_tab
     return 12 + gather + 16 * F * s_tab, 12 + 16 * F * 4 + 2 * gather
+
+
+MLP_FLOP_PER_SAMPLE = 56448   # forward 18,816 (6,144 density + 12,672 colour) x 3 with the backward
+
+
+def run_mlp_micro(args, wl, dev, st, gen, timed) -> dict:
+    """cfg5's MLP half on the tensor cores: ffn_mlp_bench over 2^22 packed fp16 inputs."""
+    import torch
+    import ffn_native as fn
+    from ffn_config import make_geometry, param_layout, param_shapes
+    hbm, tflops_peak, peak_kind = peaks()
+    g = make_geometry(F=2, ND=1, NC=2, spr=64, G=16, log2_entries=12, rmax=512.0)
+    ctx = fn.Context(g, device=0, mlp_precision="fp16")
+    lay, total = param_layout(2, 1, 2)
+    shapes = param_shapes(2, 1, 2)
+    rng = np.random.default_rng(0)
+    blob = np.zeros(total, np.float32)
+    for name, (off, size) in lay.items():          # He-normal hidden layers, N(0, 0.01) heads, zero biases
+        if size and name.startswith("W"):
+            out_, in_ = shapes[name]
+            blob[off:off + size] = rng.normal(0.0, 0.01 if out_ <= 16 else np.sqrt(2.0 / in_), size)
+    ctx.tensor(fn.BUF_PARAMS).copy_(torch.from_numpy(blob))
+    n = wl["n"]
+    x16 = torch.randn((n, 32), device=dev, generator=gen).half()
+    tiles = torch.empty(n * 32 * 2, dtype=torch.uint8, device=dev)
+    ctx.pack_x0(x16, tiles, n, stream=st)
+    step = lambda: ctx.mlp_bench(tiles, n, stream=st)           # noqa: E731
+    for _ in range(args.warmup):
+        with torch.cuda.stream(st):
+            step()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    with ClockSampler(0) as clk:
+        (t,) = timed([step], flush=False)             # inputs (268 MB) exceed L2
+        launches = ctx.launches - launches0
+        h_x = x16.cpu().pin_memory()
+        h_g = torch.empty(total).pin_memory()
+
+        def e2e():
+            x16.copy_(h_x, non_blocking=True)
+            ctx.pack_x0(x16, tiles, n, stream=st)
+            step()
+            h_g.copy_(ctx.tensor(fn.BUF_GRADS)[-total:], non_blocking=True)
+        (t_e2e,) = timed([e2e], flush=False)
+    ms = t / args.steps
+    tf = MLP_FLOP_PER_SAMPLE * n / (ms * 1e-3) / 1e12
+    # CPU: the same MLP forward/backward in fp32 with torch on the host cores, a bounded sample
+    m = 1 << 16
+    xc = x16[:m].float().cpu()
+    P = {k: torch.tensor(blob[o:o + s].reshape(shapes[k]), requires_grad=True) for k, (o, s) in lay.items() if s}
+    sh = torch.tensor([0.28209479177387814] + [0.0] * 15).expand(m, 16)
+    t0 = time.perf_counter()
+    reps = 0
+    while time.perf_counter() - t0 < 5.0:
+        h1 = torch.relu(xc @ P["Wd_in"].T + P["bd_0"])
+        dout = h1 @ P["Wd_out"].T + P["bd_out"]
+        c1 = torch.relu(torch.cat([dout, sh], 1) @ P["Wc_in"].T + P["bc_0"])
+        c2 = torch.relu(c1 @ P["Wc_01"].T + P["bc_1"])
+        rgb = torch.sigmoid(0.5 * (c2 @ P["Wc_out"].T + P["bc_out"]))
+        (0.5 * (rgb - 0.5) ** 2).sum().backward()
+        reps += 1
+    cpu_tf = MLP_FLOP_PER_SAMPLE * m * reps / (time.perf_counter() - t0) / 1e12
+    ctx.close()
+    return {
+        "metric": "MLP TFLOP/s (fwd+bwd+weight gradients, 56,448 flop/sample)", "value": tf, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "f16 operands, f32 accumulation", "data": "synthetic",
+        "config": {"workload": wl["desc"], "samples": n, "l2": "inputs (268 MB) exceed L2; no flush"},
+        "e2e": {"value": MLP_FLOP_PER_SAMPLE * n / (t_e2e / args.steps * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": n * 64, "d2h_bytes_per_step": total * 4},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": "fused_step_tc_kernel<2,1,staged,mlp> + reduce_partials",
+                     "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s", "frac": tf / tflops_peak,
+                     "traffic": None, "peak_source": peak_kind,
+                     "note": "peak = measured cuBLAS bf16 burst; the MLP is 128-row tiles of 32-64 wide layers"},
+        "clocks": clk.summary(),
+        "cpu_baseline": {"value": cpu_tf, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{m} samples fwd+bwd in fp32 with torch on the host, repeated for 5 s"},
+    }
 
 
 def run_micro(args, name: str) -> dict:
@@ -194,6 +276,8 @@ def run_micro(args, name: str) -> dict:
                                        f"fp32 bytes), repeated for 10 s"},
         }
         return line
+    if wl["kind"] == "mlp":
+        return run_mlp_micro(args, wl, dev, st, gen, timed)
     # Adam
     n = wl["n"]
     p = torch.randn(n, device=dev, generator=gen)

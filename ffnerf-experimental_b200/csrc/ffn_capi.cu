@@ -586,6 +586,54 @@ int ffn_hash_encode_bwd_f16(ffn_ctx* c, void* grad16, const float* pts, const fl
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "fp16 hash scatter launch");
 }
 
+int ffn_pack_x0(ffn_ctx* c, const void* x16, void* tiles, int64_t n, void* stream) {
+    if (!c || (n > 0 && (!x16 || !tiles))) return fail(c, FFN_E_CONFIG, "null argument");
+    if (n <= 0) return FFN_OK;
+    if (n % 128 != 0) return fail(c, FFN_E_CONFIG, "n must be a multiple of 128 (the tile height)");
+    if (!aligned16(x16) || !aligned16(tiles)) return fail(c, FFN_E_CONFIG, "x16 and tiles must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t threads = n * (L * c->cfg.F / 8);
+    const int blocks = (int)((threads + 255) / 256);
+    if (c->cfg.F == 2) pack_x0_kernel<2><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x16), n,
+                                                                 static_cast<unsigned char*>(tiles));
+    else pack_x0_kernel<4><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x16), n, static_cast<unsigned char*>(tiles));
+    ++c->launches;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "pack launch");
+}
+
+int ffn_mlp_bench(ffn_ctx* c, const void* tiles, int64_t n, void* stream) {
+    if (!c || (n > 0 && !tiles)) return fail(c, FFN_E_CONFIG, "null argument");
+    if (n <= 0) return FFN_OK;
+    if (c->cfg.mlp_precision != 1 || c->cfg.F != 2 || c->cfg.ND != 1)
+        return fail(c, FFN_E_CONFIG, "the MLP microbenchmark is compiled for the tensor-core MLP with F=2, ND=1");
+    if (n % 128 != 0 || (uint64_t)n / (uint64_t)c->cfg.spr > 0xFFFFFFFFull || 128 % c->cfg.spr != 0)
+        return fail(c, FFN_E_CONFIG, "n must be a multiple of 128 and the configured samples per ray divide 128");
+    if (!aligned16(tiles)) return fail(c, FFN_E_CONFIG, "tiles must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    using PL = TcPlan<2, 1>;
+    auto kfn = fused_step_tc_kernel<2, 1, true, true>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::BYTES);
+    if (e != cudaSuccess) return cuda_fail(c, e, "MLP microbenchmark kernel attribute");
+    ffn_step_scalars s{};
+    s.sh_mult = 1.0f;
+    s.spr = (uint32_t)c->cfg.spr;
+    StepArgs a = base_args(c, nullptr, nullptr, nullptr, (uint32_t)(n / c->cfg.spr), &s);
+    a.do_train = 1;
+    a.x0_stage = static_cast<const unsigned char*>(tiles);
+    const int64_t n_tiles = n / 128;
+    const int grid = (int)(n_tiles < c->max_grid ? n_tiles : c->max_grid);
+    kfn<<<grid, 128, PL::BYTES, st>>>(a);
+    ++c->launches;
+    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats,
+                                                        c->status);
+    ++c->launches;
+    e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "MLP microbenchmark launch");
+}
+
 uint64_t ffn_kernel_launches(const ffn_ctx* c) { return c ? c->launches : 0u; }
 
 int ffn_batch_generate(const void* images, int img_f32, int channels, const uint8_t* weights, const float* c2w,

@@ -381,8 +381,13 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <int F, int ND, bool STAGED = false>
+// MLPB (the MLP microbenchmark, staged form only): the tiles hold given inputs instead of hash
+// encodings; every sample is live, the view direction is fixed at (0.36, 0.48, 0.8), and the
+// compositing is replaced by the loss sum_k 0.5 (rgb_k - 0.5)^2 per sample (no density term), so
+// the step is the two MLPs forward and backward with their weight gradients; no table scatter.
+template <int F, int ND, bool STAGED = false, bool MLPB = false>
 __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a) {
+    static_assert(!MLPB || STAGED, "the MLP microbenchmark runs the staged form");
     using PL = TcPlan<F, ND>;
     constexpr int LPOS = PL::LPOS;
     extern __shared__ __align__(1024) unsigned char smem_tc[];
@@ -498,7 +503,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         nx_rst = make_uint4(0u, 0u, 0u, 0u);
         nx_ro = make_float4(0.f, 0.f, 0.f, 0.f);
         nx_rd = make_float4(0.f, 0.f, 1.f, 0.f);
-        if (ri < a.n_rays) {
+        if (!MLPB && ri < a.n_rays) {
             nx_tdt = a.tdt_stage[(size_t)t * 128 + tid];
             nx_rst = a.ray_stage[ri];
             nx_ro = a.rays[2 * ri];
@@ -520,7 +525,9 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         const uint32_t ray_id = a.ray_offset + ray_idx;
         const int x0_off = STAGED && xb ? PL::X0B : PL::X0;   // this tile's X0 buffer
         float4 ro = make_float4(0.f, 0.f, 0.f, 0.f), rd = make_float4(0.f, 0.f, 1.f, 0.f);
-        if constexpr (STAGED) {
+        if constexpr (MLPB) {
+            rd = make_float4(0.36f, 0.48f, 0.8f, 0.f);
+        } else if constexpr (STAGED) {
             ro = nx_ro;
             rd = nx_rd;
         } else if (valid) {
@@ -539,7 +546,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             sTs[tid] = tdt.x;
             sDTs[tid] = tdt.y;
             if (lid == 0) { sChg[rl * 2] = rst.x; sChg[rl * 2 + 1] = rst.y; }
-            hit = rst.z != 0u;
+            hit = MLPB || rst.z != 0u;
             cp_async_wait_all();
             __syncthreads();
             // the other buffer was last read by the previous tile's MMAs, which have completed
@@ -608,12 +615,20 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
                 for (int k = 0; k < 3; ++k) rgb[k] = sigmoid_soft(v[k] + bias[272 + k]);
             }
         }
-        if (dt_s <= 0.0f) sigma = 0.0f;
+        if (!MLPB && dt_s <= 0.0f) sigma = 0.0f;
 
         // ---------------- compositing, loss gradient, occupancy proposals
         float T_s, dLds, dLdc[3];
         uint32_t chg0, chg1;
-        ray_composite(a, R, rs, sigma, rgb, xs, t_s, dt_s, T_s, dLds, dLdc, chg0, chg1);
+        if constexpr (MLPB) {
+            T_s = 1.0f;
+            dLds = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) dLdc[k] = rgb[k] - 0.5f;
+            chg0 = chg1 = 0u;
+        } else {
+            ray_composite(a, R, rs, sigma, rgb, xs, t_s, dt_s, T_s, dLds, dLdc, chg0, chg1);
+        }
 
         if (probe) {
             if (valid) {
@@ -645,6 +660,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             const float gate = (1.0f - sflag) * 1.0f + sflag * powf(fmaxf(xr, 1.0e-12f), 0.2f);
             float f_vol = gate * num / fmaxf(den, 1.0e-12f);
             if (!valid || !hit) f_vol = 0.0f;
+            if constexpr (MLPB) f_vol = valid ? 1.0f : 0.0f;
             const float d_sigma = f_vol * dLds;
 #pragma unroll
             for (int k = 0; k < 3; ++k) dcout[k] = (f_vol * dLdc[k]) * ((rgb[k] * (1.0f - rgb[k])) * 0.5f);
@@ -734,7 +750,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         dw_started = true;
         // the activation tiles are dead once the last MMAs completed: C1 holds the scatter's exchange
         // rows, C2 the parked gradients
-        if (hit && valid)
+        if (!MLPB && hit && valid)
             scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef,
                                  reinterpret_cast<float*>(tC1), reinterpret_cast<float*>(tC2));
         tc::fence_before_sync();
@@ -906,6 +922,27 @@ __global__ void __launch_bounds__(256) encode_stage_kernel(const DevConfig c, co
             *reinterpret_cast<uint2*>(tile + tc::tile_off(r, lvl * 4, LPOS)) = u;
         }
     }
+}
+
+// Packs row-major fp16 rows [n][16F] into the 128-row operand tiles of the MLP kernels (x INPUT_SCALE,
+// the encoder's convention); one thread per (row, 8-column chunk).
+template <int F>
+__global__ void pack_x0_kernel(const __half* __restrict__ x, int64_t n, unsigned char* __restrict__ tiles) {
+    constexpr int LPOS = L * F, CH = LPOS / 8;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * CH) return;
+    const int64_t row = i / CH;
+    const int c0 = (int)(i - row * CH) * 8;
+    const uint4 u = *reinterpret_cast<const uint4*>(x + row * LPOS + c0);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(h[k]);
+        v[2 * k] = f.x * INPUT_SCALE;
+        v[2 * k + 1] = f.y * INPUT_SCALE;
+    }
+    tc::st_chunk8(tiles + (row / 128) * (128 * LPOS * 2), (int)(row % 128), c0, LPOS, v);
 }
 
 }  // namespace ffn

@@ -69,6 +69,8 @@ _SIGS = {
     "ffn_hash_encode": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_hash_encode_bwd": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_hash_encode_f16": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, _VP]),
+    "ffn_pack_x0": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
+    "ffn_mlp_bench": (C.c_int, [_VP, _VP, C.c_int64, _VP]),
     "ffn_hash_encode_bwd_f16": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_adam": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_float, _VP]),
     "ffn_status": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
@@ -304,6 +306,15 @@ class Context:
         """Encoding from a caller-owned fp16 table (FFN_BUF_TABLE's layout) into fp16 enc16 [n, 16F]."""
         self._check(self.lib.ffn_hash_encode_f16(self.h, _ptr(table16), _ptr(pts), _ptr(enc16), int(n),
                                                  self._stream(stream)), "ffn_hash_encode_f16")
+
+    def pack_x0(self, x16, tiles, n: int, stream=None):
+        """Packs fp16 rows x16 [n, 16F] (n a multiple of 128) into the MLP kernels' operand tiles."""
+        self._check(self.lib.ffn_pack_x0(self.h, _ptr(x16), _ptr(tiles), int(n), self._stream(stream)), "ffn_pack_x0")
+
+    def mlp_bench(self, tiles, n: int, stream=None):
+        """The MLP microbenchmark over packed inputs: gradients of sum 0.5 (rgb - 0.5)^2 added to the
+        MLP part of BUF_GRADS (view direction (0.36, 0.48, 0.8), sh multiplier 1)."""
+        self._check(self.lib.ffn_mlp_bench(self.h, _ptr(tiles), int(n), self._stream(stream)), "ffn_mlp_bench")
 
     def hash_encode_bwd_f16(self, grad16, pts, denc, n: int, stream=None):
         """Scatter-adds fp32 upstream gradients denc [n, 16F] into the caller-owned fp16 table grad16."""

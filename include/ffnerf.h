@@ -165,6 +165,15 @@ int ffn_hash_encode_f16(ffn_ctx* ctx, const void* table16, const float* pts, voi
                         void* stream);
 int ffn_hash_encode_bwd_f16(ffn_ctx* ctx, void* grad16, const float* pts, const float* denc, int64_t n,
                             void* stream);
+/* The MLP microbenchmark (no reference counterpart; the MLP half of the "fused MLP + Adam"
+ * microbenchmark).  ffn_pack_x0 packs row-major fp16 inputs x16 [n][16*F] into the tensor-core
+ * operand tiles (tiles: n*16*F*2 bytes, n a multiple of 128).  ffn_mlp_bench runs the density and
+ * colour MLPs forward and backward over those inputs on the tensor cores (tensor-core MLP, F=2,
+ * ND=1 contexts), with the view direction fixed at (0.36, 0.48, 0.8), sh multiplier 1 and the loss
+ * sum_k 0.5 (rgb_k - 0.5)^2 per sample, and adds the summed MLP weight and bias gradients to the MLP
+ * part of FFN_BUF_GRADS.  The table and its gradients are not touched. */
+int ffn_pack_x0(ffn_ctx* ctx, const void* x16, void* tiles, int64_t n, void* stream);
+int ffn_mlp_bench(ffn_ctx* ctx, const void* tiles, int64_t n, void* stream);
 /* Kernels this context has launched so far (all entry points; no reference counterpart). */
 uint64_t ffn_kernel_launches(const ffn_ctx* ctx);
 /* Reads and clears the context's device status word (waits for the device): 0 when every kernel
