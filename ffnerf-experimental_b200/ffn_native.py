@@ -47,7 +47,7 @@ STEP_TABLE_IMMEDIATE = 1
 STEP_TABLE_APPLIED = 2
 STATUS_NONFINITE, STATUS_TC_TIMEOUT, STATUS_DP_TIMEOUT = 1, 4, 8   # ffn_status bits
 STAGE_SAMPLES = 1 << 20   # samples per group of the split tensor-core step (ffn_capi.cu)
-ABI_VERSION = 3          # include/ffnerf.h FFN_ABI_VERSION
+ABI_VERSION = 4          # include/ffnerf.h FFN_ABI_VERSION
 
 
 _VP = C.c_void_p
@@ -103,13 +103,15 @@ def load_library(path: Path | None = None):
         raise RuntimeError(f"{p} is missing: the CUDA library must be built (python build_native.py); "
                            "there is no CPU fallback")
     lib = C.CDLL(str(p))
+    lib.ffn_abi_version.restype = C.c_int
+    lib.ffn_abi_version.argtypes = []
+    if lib.ffn_abi_version() != ABI_VERSION:     # before binding: an older build lacks newer symbols
+        raise RuntimeError(f"{p} has ABI version {lib.ffn_abi_version()}, this module expects {ABI_VERSION}: "
+                           "rebuild it (python build_native.py)")
     for name, (res, args) in _SIGS.items():
         f = getattr(lib, name)
         f.restype = res
         f.argtypes = args
-    if lib.ffn_abi_version() != ABI_VERSION:
-        raise RuntimeError(f"{p} has ABI version {lib.ffn_abi_version()}, this module expects {ABI_VERSION}: "
-                           "rebuild it (python build_native.py)")
     if path is None:
         _lib = lib
     return lib

@@ -38,7 +38,8 @@ extern "C" {
 #endif
 
 #define FFN_N_LEVELS 16
-#define FFN_ABI_VERSION 3   /* 2: ffn_step_scalars.flags; 3: batch/exchange entry points */
+#define FFN_ABI_VERSION 4   /* 2: ffn_step_scalars.flags; 3: batch/exchange entry points;
+                                   4: fp16-table hash and MLP microbenchmark entry points */
 
 enum {
     FFN_OK = 0,
