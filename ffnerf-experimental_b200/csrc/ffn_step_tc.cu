@@ -374,6 +374,21 @@ __device__ __forceinline__ float warp_sum16(const float (&v)[16]) {
     return d + __shfl_xor_sync(full, d, 1);
 }
 
+// Sums v[0..3] over the warp's 32 lanes (6 shuffles instead of 20): lane l ends with the sum for
+// index (l >> 3) & 3.
+__device__ __forceinline__ float warp_sum4(const float (&v)[4]) {
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0;
+    float a[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) a[i] = (h16 ? v[i + 2] : v[i]) + __shfl_xor_sync(full, h16 ? v[i] : v[i + 2], 16);
+    float b = (h8 ? a[1] : a[0]) + __shfl_xor_sync(full, h8 ? a[0] : a[1], 8);
+    b += __shfl_xor_sync(full, b, 4);
+    b += __shfl_xor_sync(full, b, 2);
+    return b + __shfl_xor_sync(full, b, 1);
+}
+
 // 16-byte global -> shared copies that complete in the background (cp.async, L2 only).
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -672,13 +687,12 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;
             v[0] = dcout[0] * DELTA_SCALE; v[1] = dcout[1] * DELTA_SCALE; v[2] = dcout[2] * DELTA_SCALE;
             store_row<16>(tDC, 16, v);
-            // colour-head bias gradient: warp sums, then one shared-memory add per warp
-#pragma unroll
-            for (int k = 0; k < 3; ++k) {
-                float s = v[k];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                if ((tid & 31) == 0) atomicAdd(bgrad + 16 + k, s);
+            // colour-head bias gradient: a transposed warp butterfly, then three lanes add at once
+            {
+                const float v4[4] = {v[0], v[1], v[2], 0.0f};
+                const float sum = warp_sum4(v4);
+                const int k = (tid >> 3) & 3;
+                if ((tid & 7) == 0 && k < 3) atomicAdd(bgrad + 16 + k, sum);
             }
         }
         const uint32_t acc0 = dw_started ? 1u : 0u;
