@@ -61,3 +61,21 @@ def test_geometry_validation():
     # trainer defaults (run_ffnerf_OG.py:1050-1051)
     assert g["dt_min"] == float(np.float32(2.0 / 8192))
     assert g["dt_max"] == float(np.float32(12.8 / 64 / 6 * 2.0))
+
+
+def test_library_missing_or_of_another_abi_is_refused(tmp_path):
+    """No silent fallback: a missing library, or one built for another ABI version (which may lack
+    newer entry points), makes load_library raise before anything is bound."""
+    import shutil
+    import subprocess
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        fn.load_library(tmp_path / "absent.so")
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "old.c"
+    src.write_text(f"int ffn_abi_version(void) {{ return {fn.ABI_VERSION - 1}; }}\n")
+    so = tmp_path / "libold.so"
+    subprocess.run([cc, "-shared", "-fPIC", str(src), "-o", str(so)], check=True)
+    with pytest.raises(RuntimeError, match="ABI version"):
+        fn.load_library(so)
