@@ -132,10 +132,15 @@ def test_fused_exchange_matches_nccl(mode):
             rank, st, res = q.get(timeout=240)
             results[rank] = (st, res)
     finally:
+        # In the NVLS form a worker's table and gradient buffer are bound to NVLink multicast objects:
+        # such a rank is never ended from outside.  It ends by itself -- the exchange's waits are
+        # bounded and the process group has a 60 s timeout -- and the parent only reports it.
         for p in procs:
-            p.join(timeout=60)
-            if p.is_alive():
+            p.join(timeout=60 if mode == "p2p" else 180)
+            if p.is_alive() and mode == "p2p":
                 p.kill()
+    stuck = [r for r, p in enumerate(procs) if p.is_alive()]
+    assert not stuck, f"ranks {stuck} had not exited ({mode} form; left to end by themselves)"
     if any(st == "skip" for st, _ in results.values()):
         pytest.skip("the NVSwitch offers no multicast here")
     for rank, (st, res) in results.items():

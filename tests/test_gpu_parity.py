@@ -25,14 +25,20 @@ GEOMS = {
     "refdefault": dict(F=4, ND=2, NC=2, spr=64, G=32, log2_entries=list(REFERENCE_LEVEL_LOG2), rmax=1024.0,
                        box_min=(-3, -3, -3), box_max=(3, 3, 3)),
     "spr32": dict(F=2, ND=1, NC=2, spr=32, G=64, log2_entries=12, rmax=512.0),
+    # the benchmarked geometry (BASELINE cfg2/cfg3): T = 2^19 per level, finest level 2048, 128^3 grid
+    "cfg3": dict(F=2, ND=1, NC=2, spr=64, G=128, log2_entries=19, rmax=2048.0),
 }
+# rays per call of the single-step tests (cfg3: a 2,048-ray slice of the benchmark's batch)
+N_RAYS = {"cfg3": 2048}
 
 
 def _cuda(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def _make(name, seed=0, n_rays=96, n_miss=4):
+def _make(name, seed=0, n_rays=None, n_miss=4):
+    if n_rays is None:
+        n_rays = N_RAYS.get(name, 96)
     g = make_geometry(**GEOMS[name])
     ctx = fn.Context(g, device=0)
     blob = init_blob(g, seed)
@@ -95,7 +101,7 @@ def test_sampler_bit_exact(oracle, name):
 def test_occupancy_proposals_bit_exact(oracle, name):
     """With sigma/rgb fixed per sample (MLP bypassed) the nibble-max proposals, the transmittance
     and the composited colour are bit-identical."""
-    g, ctx, blob, table, occ, rays, tg = _make(name, seed=3, n_rays=160)
+    g, ctx, blob, table, occ, rays, tg = _make(name, seed=3, n_rays=N_RAYS.get(name, 160))
     n, spr = rays.shape[0], g["spr"]
     rng = np.random.default_rng(5)
     bypass = np.zeros((n * spr, 4), np.float32)
@@ -149,7 +155,7 @@ def _mse(out, tg):
     return float(np.mean((out[:, :3] - tg[:, :3]) ** 2))
 
 
-@pytest.mark.parametrize("name", ["cfg1", "refdefault"])
+@pytest.mark.parametrize("name", ["cfg1", "refdefault", "cfg3"])
 def test_training_run_parity(oracle, name):
     """20 full steps (forward, backward, MLP Adam, hash SGD, one occupancy maintenance):
     per-step loss rel <= 1e-3, parameters and table rel-L2 <= 1e-2 at the end."""

@@ -27,14 +27,19 @@ GEOMS = {
                   box_min=(-3, -3, -3), box_max=(3, 3, 3)),
     "f2nd2_spr32": dict(F=2, ND=2, NC=2, spr=32, G=64, log2_entries=12, rmax=512.0),
     "f4nd1_spr16": dict(F=4, ND=1, NC=2, spr=16, G=64, log2_entries=13, rmax=2048.0),
+    # the benchmarked geometry (BASELINE cfg2/cfg3): T = 2^19 per level, finest level 2048, 128^3 grid
+    "cfg3": dict(F=2, ND=1, NC=2, spr=64, G=128, log2_entries=19, rmax=2048.0),
 }
+N_RAYS = {"cfg3": 2048}   # rays per call of the single-step tests (default 192)
 
 
 def _cuda(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def _make(name, seed=0, n_rays=192, n_miss=4):
+def _make(name, seed=0, n_rays=None, n_miss=4):
+    if n_rays is None:
+        n_rays = N_RAYS.get(name, 192)
     g = make_geometry(**GEOMS[name])
     ctx = fn.Context(g, mlp_precision="fp16")
     blob, table, occ = init_blob(g, seed), init_table(g, seed), init_occ(g, seed)
@@ -76,7 +81,7 @@ def test_tc_sampler_exact_and_forward_close(oracle, name):
     assert ctx.status() == 0
 
 
-@pytest.mark.parametrize("name", ["cfg1", "f4nd2"])
+@pytest.mark.parametrize("name", ["cfg1", "f4nd2", "cfg3"])
 def test_tc_occupancy_bypass_bit_exact(oracle, name):
     g, ctx, blob, table, occ, rays, tg = _make(name, seed=3)
     n, spr = rays.shape[0], g["spr"]

@@ -17,6 +17,7 @@ VARIANTS = {
     "cfg1": dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0),
     "default": dict(F=4, ND=2, NC=2, spr=64, G=32, log2_entries=list(REFERENCE_LEVEL_LOG2), rmax=1024.0,
                     box_min=(-3, -3, -3), box_max=(3, 3, 3)),
+    "cfg3": dict(F=2, ND=1, NC=2, spr=64, G=128, log2_entries=19, rmax=2048.0),
 }
 
 
@@ -38,7 +39,7 @@ def test_oracle_matches_compiled_reference(oracle, variant, occ_strength, sh_mul
     g = make_geometry(**VARIANTS[variant])
     assert (ref.F, ref.ND, ref.NC) == (g["F"], g["ND"], g["NC"])
     n = 40
-    rays = rays_toward_box(n, 21, radius=2.0 if variant == "cfg1" else 6.0, n_miss=3)
+    rays = rays_toward_box(n, 21, radius=6.0 if variant == "default" else 2.0, n_miss=3)
     tg = targets(n, 21)
     blob = init_blob(g, 21, sigma_bias=2.0)
     table0 = init_table(g, 21)
