@@ -4,8 +4,8 @@
 // of ffn_common.cuh (explicit round-to-nearest operations, own exp/pow), so both kernels produce
 // bit-identical sample positions, transmittances and proposals.
 //
-// Both functions are called by every thread of the CTA (one thread per sample, rays of spr
-// consecutive threads) and synchronise the CTA internally.
+// Both functions are called by every thread of a 128-sample tile (one thread per sample, rays of
+// spr consecutive threads) and synchronise the tile's threads internally (tile_sync).
 #pragma once
 #include "ffn_common.cuh"
 
@@ -44,15 +44,15 @@ struct StepArgs {
 
 // ---------------------------------------------------------------------------- exact scans
 // Blelloch exclusive scan of one ray's slice (ffnerf_OG.cl:619-637); every thread of the CTA
-// calls it (one lane of one ray), levels separated by __syncthreads.
+// calls it (one lane of one ray), levels separated by tile barriers.
 __device__ __forceinline__ void scan_excl(float* a, int lid, int n) {
     for (int stride = 1; stride < n; stride <<= 1) {
         int idx = (lid + 1) * (stride << 1) - 1;
         if (idx < n) a[idx] = fa(a[idx], a[idx - stride]);
-        __syncthreads();
+        tile_sync();
     }
     if (lid == 0) a[n - 1] = 0.0f;
-    __syncthreads();
+    tile_sync();
     for (int stride = n >> 1; stride >= 1; stride >>= 1) {
         int idx = (lid + 1) * (stride << 1) - 1;
         if (idx < n) {
@@ -60,14 +60,14 @@ __device__ __forceinline__ void scan_excl(float* a, int lid, int n) {
             a[idx - stride] = a[idx];
             a[idx] = fa(a[idx], t);
         }
-        __syncthreads();
+        tile_sync();
     }
 }
 // ffnerf_OG.cl:639-646
 __device__ __forceinline__ float reduce_sum(float* a, int lid, int n) {
     for (int stride = n >> 1; stride >= 1; stride >>= 1) {
         if (lid < stride) a[lid] = fa(a[lid], a[lid + stride]);
-        __syncthreads();
+        tile_sync();
     }
     return a[0];
 }
@@ -89,12 +89,12 @@ __device__ __forceinline__ float4 scan_excl_seg(float4* s, int lid, int n) {
     for (int stride = 1; stride < n; stride <<= 1) {
         int idx = (lid + 1) * (stride << 1) - 1;
         if (idx < n) s[idx] = seg_combine(s[idx - stride], s[idx]);
-        __syncthreads();
+        tile_sync();
     }
     float4 total = s[n - 1];
-    __syncthreads();
+    tile_sync();
     if (lid == 0) s[n - 1] = make_float4(1.0f, 0.0f, 0.0f, 0.0f);
-    __syncthreads();
+    tile_sync();
     for (int stride = n >> 1; stride >= 1; stride >>= 1) {
         int idx = (lid + 1) * (stride << 1) - 1;
         if (idx < n) {
@@ -102,7 +102,7 @@ __device__ __forceinline__ float4 scan_excl_seg(float4* s, int lid, int n) {
             s[idx - stride] = s[idx];
             s[idx] = seg_combine(t, s[idx]);
         }
-        __syncthreads();
+        tile_sync();
     }
     return total;
 }
@@ -115,10 +115,10 @@ __device__ __forceinline__ void scan_excl_aff_rev(float2* s, int lid, int n) {
     for (int stride = 1; stride < n; stride <<= 1) {
         int idx = (lid + 1) * (stride << 1) - 1;
         if (idx < n) s[idx] = aff_combine_rev(s[idx - stride], s[idx]);
-        __syncthreads();
+        tile_sync();
     }
     if (lid == 0) s[n - 1] = make_float2(1.0f, 0.0f);
-    __syncthreads();
+    tile_sync();
     for (int stride = n >> 1; stride >= 1; stride >>= 1) {
         int idx = (lid + 1) * (stride << 1) - 1;
         if (idx < n) {
@@ -126,7 +126,7 @@ __device__ __forceinline__ void scan_excl_aff_rev(float2* s, int lid, int n) {
             s[idx - stride] = s[idx];
             s[idx] = aff_combine_rev(t, s[idx]);
         }
-        __syncthreads();
+        tile_sync();
     }
 }
 
@@ -178,9 +178,9 @@ __device__ __forceinline__ T scan_excl_warp(T v, int p, int n, int dir, T ident,
     }
     if (n == 64) {                                             // stride 32: across the two warps
         if (p == 31) xchg[0] = v;
-        __syncthreads();
+        tile_sync();
         if (p == 63) { v = comb(xchg[0], v); xchg[1] = v; }
-        __syncthreads();
+        tile_sync();
         total = xchg[1];
         // down-sweep stride 32: position 31 takes position 63's value (the identity), position 63
         // takes comb(position 31, identity)
@@ -210,7 +210,7 @@ __device__ __forceinline__ float reduce_sum_warp(float v, int p, int n, float* x
     int s = n >> 1;
     if (n == 64) {
         if (p >= 32) xchg[p - 32] = v;
-        __syncthreads();
+        tile_sync();
         if (p < 32) v = fa(v, xchg[p]);
         s = 16;
     }
@@ -220,7 +220,7 @@ __device__ __forceinline__ float reduce_sum_warp(float v, int p, int n, float* x
     }
     if (n == 64) {
         if (p == 0) xchg[32] = v;
-        __syncthreads();
+        tile_sync();
         return xchg[32];
     }
     return __shfl_sync(0xffffffffu, v, (int)(threadIdx.x & 31) - p);
@@ -313,7 +313,7 @@ __device__ __forceinline__ void ray_sampler(const StepArgs& a, const RayTile& R,
         rs[RS_T0] = t0; rs[RS_T1] = t1; rs[RS_DTB] = dtb; rs[RS_U0] = u0; rs[RS_HIT] = hit ? 1.f : 0.f;
     }
     if (lid < 2) sChg[rl * 2 + lid] = 0u;
-    __syncthreads();
+    tile_sync();
     const float* rs = sRay + rl * 16;
     const bool hit = rs[RS_HIT] != 0.0f;
     hit_out = hit;
@@ -367,23 +367,23 @@ __device__ __forceinline__ void ray_sampler(const StepArgs& a, const RayTile& R,
             active_count = reduce_sum_warp(active, lid, spr, xs + 4);
         } else {
             sCdf[tid] = wp;
-            __syncthreads();
+            tile_sync();
             scan_excl(cdf, lid, spr);
             pref = sCdf[tid];
             sCdf[tid] = wp;
-            __syncthreads();
+            tile_sync();
             Wtot = fmaxf(reduce_sum(cdf, lid, spr), 1.0e-12f);
-            __syncthreads();
+            tile_sync();
             const float pi = fclamp(fd(pref, Wtot), 0.0f, 1.0f);
             g = fm(wp, own_expf(fm(-0.0f, pi)));        // LAMBDA_FOCUS = 0
             sCdf[tid] = g;
-            __syncthreads();
+            tile_sync();
             gtot = fmaxf(reduce_sum(cdf, lid, spr), 1.0e-12f);
-            __syncthreads();
+            tile_sync();
             sCdf[tid] = active;
-            __syncthreads();
+            tile_sync();
             active_count = reduce_sum(cdf, lid, spr);
-            __syncthreads();
+            tile_sync();
         }
         const float any_active = active_count > 0.5f ? 1.0f : 0.0f;
         const float inv_active = fd(1.0f, fmaxf(active_count, 1.0f));
@@ -396,11 +396,11 @@ __device__ __forceinline__ void ray_sampler(const StepArgs& a, const RayTile& R,
             sCdf[tid] = fa(ex, p);
         } else {
             sCdf[tid] = p;
-            __syncthreads();
+            tile_sync();
             scan_excl(cdf, lid, spr);
             sCdf[tid] = fa(sCdf[tid], p);
         }
-        __syncthreads();
+        tile_sync();
         float t_out = 0.0f;
         uint32_t key = 0xFFFFFFFEu;
         if (hit) {
@@ -421,11 +421,11 @@ __device__ __forceinline__ void ray_sampler(const StepArgs& a, const RayTile& R,
                 key = (cell << 3) | (sub & 7u);
             }
         }
-        __syncthreads();   // every lane has read cand/cdf
+        tile_sync();   // every lane has read cand/cdf
         sTs[tid] = t_out;
         sDTs[tid] = hit ? dtb : 0.0f;
         sKey[tid] = key;
-        __syncthreads();
+        tile_sync();
         const bool pow2 = spr <= 64 && (spr & (spr - 1)) == 0;   // uniform over the block
         if (pow2) {
             // run starts as a warp ballot: a warp holds 32 lanes of one ray, or whole rays when spr < 32
@@ -447,7 +447,7 @@ __device__ __forceinline__ void ray_sampler(const StepArgs& a, const RayTile& R,
             const int nb = min(32, max(0, spr - lo_bit));
             sChg[rl * 2 + lid] = nb == 32 ? 0xFFFFFFFFu : ((1u << nb) - 1u);
         }
-        __syncthreads();
+        tile_sync();
     }
 
     idx_out = idx_sel;
@@ -486,7 +486,7 @@ __device__ __forceinline__ void ray_composite(const StepArgs& a, const RayTile& 
         T_s = ex.x;
     } else {
         sSeg[tid] = make_float4(oma, fm(alpha, rgb[0]), fm(alpha, rgb[1]), fm(alpha, rgb[2]));
-        __syncthreads();
+        tile_sync();
         total = scan_excl_seg(sSeg + rbase, lid, spr);
         T_s = sSeg[tid].x;
     }
@@ -524,7 +524,7 @@ __device__ __forceinline__ void ray_composite(const StepArgs& a, const RayTile& 
             if (a.status && !(isfinite(cf[0]) && isfinite(cf[1]) && isfinite(cf[2]))) atomicOr(a.status, ST_NONFINITE);
         }
     }
-    __syncthreads();
+    tile_sync();
     const float gr0 = rs[RS_GRX], gr1 = rs[RS_GRY], gr2 = rs[RS_GRZ], gT_end = rs[RS_GTEND];
     const float w_s = fm(T_s, alpha);
     const float dLdc[3] = {fm(w_s, gr0), fm(w_s, gr1), fm(w_s, gr2)};
@@ -541,7 +541,7 @@ __device__ __forceinline__ void ray_composite(const StepArgs& a, const RayTile& 
             sAffS[rbase + k] = make_float2(oma, B_s);
         }
     }
-    __syncthreads();
+    tile_sync();
     if (!warp_scan) scan_excl_aff_rev(sAffS + rbase, lid, spr);
     float dLds;
     {

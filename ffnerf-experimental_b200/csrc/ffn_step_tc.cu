@@ -1,21 +1,30 @@
 // ffn_step_tc.cu -- the fused training step with the MLPs on the 5th-generation tensor cores.
 //
-// Same tile structure as fused_step_kernel (one CTA = 128 samples, thread t = sample t), with
+// Same tile structure as fused_step_kernel (one tile = 128 samples, thread t = sample t), with
 // every dense layer of ffnerf_train_step (ffnerf_OG.cl:1378-1466, 1930-2082) and every per-layer
 // reduction of update_ffnerf_oneWG (weight_update.cl:210-314) issued as tcgen05.mma:
 //
-//   forward       ACC[128 x N] = X[128 x K] * W^T         X K-major, W K-major (fp16 in, fp32 acc)
-//   backward      ACC[128 x N] = D[128 x K] * W           D K-major, W read MN-major
+//   forward       ACC[128 x N] = X[128 x K] * W^T         X K-major, W K-major (fp32 accumulate),
+//                 each operand as a compensated fp16 pair: hi*hi + hi*lo + lo*hi (three MMAs)
+//   backward      ACC[128 x N] = D[128 x K] * W           D K-major, W read MN-major (fp16 hi)
 //   weight grad   dW[64 x N]  += D^T[64 x 128] * X[128 x N]   both read MN-major, accumulated in
-//                 TMEM over every tile the CTA processes; bias grads as D^T * e_0 with a constant
+//                 TMEM over every tile the group processes; bias grads as D^T * e_0 with a constant
 //                 one-hot tile.
+//
+// Why the forward is compensated: the backward masks every hidden delta with the sign of the
+// forward activation (ReLU), so a forward that is off by fp16 rounding flips masks of activations
+// near zero and moves whole delta entries; that, not the backward's own rounding, dominated the
+// gradient error of a plain fp16 forward.  With the hi/lo pairs the forward is as close to fp32 as
+// the accumulation, and the remaining error is the backward's fp16 operand rounding.
 //
 // Accumulators live in tensor memory; the epilogues (bias, ReLU, masks, fp16 packing) run in the
 // thread that owns the row (TMEM lane t = sample t).  Deltas are stored scaled by DELTA_SCALE in
 // fp16 and unscaled on the way out.  All operand tiles use the core-matrix interleaved layout
-// of ffn_tcgen05.cuh.  Shared memory ~100 KB and 256 TMEM columns (F=2, ND=1) let two CTAs share
-// an SM.  Every mbarrier wait is bounded; on a timeout the CTA flags the status word, stops issuing
-// work and releases its tensor memory.
+// of ffn_tcgen05.cuh.  With F=2, ND=1 one CTA of 256 threads runs two tiles side by side (two
+// groups of 4 warps, each with its own operand tiles, mbarrier, named barrier and 256 TMEM columns)
+// and the groups share one copy of the weights; other geometries run one group per CTA.  Every
+// mbarrier wait is bounded; on a timeout the group flags the status word, stops issuing work, and
+// the CTA releases its tensor memory.
 #include "ffn_common.cuh"
 #include "ffn_hashgrid.cuh"
 #include "ffn_raymarch.cuh"
@@ -30,35 +39,48 @@ constexpr float DELTA_SCALE = 1024.0f;
 constexpr float INPUT_SCALE = 256.0f;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;   // polls of an mbarrier before a wait is declared failed
 
+constexpr int round_up_1k(int x) { return (x + 1023) & ~1023; }
+
 template <int F, int ND>
 struct TcPlan {
     static constexpr int ROWS = 128;
     static constexpr int LPOS = 16 * F;
-    // fp16 operand tiles (bytes), each a multiple of 1 KB
-    static constexpr int X0 = 0;
-    static constexpr int HD = X0 + ROWS * LPOS * 2;           // ND density hidden tiles [128 x 64]
-    static constexpr int XC = HD + ND * ROWS * 64 * 2;        // colour input [128 x 32]
-    static constexpr int C1 = XC + ROWS * 32 * 2;             // colour hidden 1 [128 x 64]
-    static constexpr int C2 = C1 + ROWS * 64 * 2;             // colour hidden 2 [128 x 64]
-    static constexpr int DC = C2 + ROWS * 64 * 2;             // output delta [128 x 16]
-    static constexpr int ONES = DC + ROWS * 16 * 2;           // one-hot [128 x 8]
-    static constexpr int X0B = ONES + ROWS * 8 * 2;           // second X0 tile (staged form: the next tile)
-    // fp16 weights, rows = outputs, columns = inputs
-    static constexpr int W_DIN = X0B + ROWS * LPOS * 2;       // [64 x LPOS]
+    // tiles side by side per CTA: two where both groups' tiles and tensor memory fit one SM
+    static constexpr int GROUPS = (F == 2 && ND == 1) ? 2 : 1;
+    static constexpr int THREADS = ROWS * GROUPS;
+    // ---- per CTA, shared by the groups: fp16 weights (rows = outputs, columns = inputs), hi copy
+    // at W_HI, lo copy at W_LO, then the one-hot tile and the fp32 biases
+    static constexpr int W_DIN = 0;                           // [64 x LPOS]
     static constexpr int W_D01 = W_DIN + 64 * LPOS * 2;       // [64 x 64] (ND = 2)
     static constexpr int W_DOUT = W_D01 + (ND >= 2 ? 64 * 64 * 2 : 0);   // [16 x 64]
     static constexpr int W_CIN = W_DOUT + 16 * 64 * 2;        // [64 x 32]
     static constexpr int W_C01 = W_CIN + 64 * 32 * 2;         // [64 x 64]
     static constexpr int W_COUT = W_C01 + 64 * 64 * 2;        // [16 x 64], rows 3..15 zero
-    // fp32 biases and output-layer bias-gradient accumulators
-    static constexpr int BIAS = W_COUT + 16 * 64 * 2;         // bd_0[64] bd_1[64] bd_out[16] bc_0[64] bc_1[64] bc_out[16]
-    static constexpr int BGRAD = BIAS + (64 * 2 + 16 + 64 * 2 + 16) * 4;   // bd_out[16], bc_out[16]
-    // ray-phase arrays
-    static constexpr int RAY = BGRAD + 32 * 4;
+    static constexpr int W_SET = W_COUT + 16 * 64 * 2;        // bytes of one copy
+    static constexpr int W_HI = 0;
+    static constexpr int W_LO = W_SET;
+    static constexpr int ONES = 2 * W_SET;                    // one-hot [128 x 8]
+    static constexpr int BIAS = ONES + ROWS * 8 * 2;          // bd_0[64] bd_1[64] bd_out[16] bc_0[64] bc_1[64] bc_out[16]
+    static constexpr int SHARED_BYTES = round_up_1k(BIAS + (64 * 2 + 16 + 64 * 2 + 16) * 4);
+    // ---- per group, at SHARED_BYTES + group * GROUP_BYTES: fp16 operand tiles
+    static constexpr int X0 = 0;                              // encoding hi [128 x LPOS]
+    static constexpr int LO = X0 + ROWS * LPOS * 2;           // the lo tile of the operand being multiplied
+                                                              // (16 KB: any [128 x 64] or X0); the
+                                                              // output-delta tile in the backward
+    static constexpr int DC = LO;                             // output delta [128 x 16]
+    static constexpr int HD = LO + ROWS * 64 * 2;             // ND density hidden tiles [128 x 64]
+    static constexpr int XC = HD + ND * ROWS * 64 * 2;        // colour input [128 x 32]
+    static constexpr int C1 = XC + ROWS * 32 * 2;             // colour hidden 1 [128 x 64]
+    static constexpr int C2 = C1 + ROWS * 64 * 2;             // colour hidden 2 [128 x 64]
+    static constexpr int BGRAD = C2 + ROWS * 64 * 2;          // bd_out[16], bc_out[16] gradient sums
+    static constexpr int RAY = BGRAD + 32 * 4;                // ray-phase arrays
     static constexpr int RAY_BYTES = ROWS * 6 * 4 + ROWS * 16 + ROWS * 16 + 8 * 2 * 4 + 8 * 16 * 4;
-    static constexpr int MISC = RAY + RAY_BYTES;               // mbarrier (8), tmem base (4), abort (4)
-    static constexpr int BYTES = MISC + 64;
-    // tensor-memory columns
+    static constexpr int MISC = RAY + RAY_BYTES;              // mbarrier (8), tmem base (4), abort (4)
+    static constexpr int GROUP_BYTES = round_up_1k(MISC + 64);
+    static constexpr int BYTES = SHARED_BYTES + GROUPS * GROUP_BYTES;
+    // staged operand tile in global memory: hi tile then lo tile
+    static constexpr int X0_STAGE_BYTES = 2 * ROWS * LPOS * 2;
+    // tensor-memory columns of one group
     static constexpr uint32_t ACC = 0;                         // per-tile accumulator (64 cols)
     static constexpr uint32_t DW_C01 = 64;
     static constexpr uint32_t DW_DIN = 128;
@@ -71,19 +93,27 @@ struct TcPlan {
     static constexpr uint32_t DW_D01 = B_C1 + 8;               // ND = 2
     static constexpr uint32_t B_D1 = DW_D01 + 64;
     static constexpr uint32_t USED = ND >= 2 ? B_D1 + 8 : B_C1 + 8;
-    static constexpr uint32_t TMEM_COLS = USED <= 256 ? 256 : 512;
-    static constexpr int CTAS_PER_SM = (TMEM_COLS == 256 && BYTES <= 110 * 1024) ? 2 : 1;
+    static constexpr uint32_t TMEM_GROUP = USED <= 256 ? 256 : 512;
+    static constexpr uint32_t TMEM_COLS = TMEM_GROUP * GROUPS;
+    static constexpr int CTAS_PER_SM = 1;
+    static_assert(TMEM_COLS <= 512, "tensor memory of one SM");
+    static_assert(BYTES <= 227 * 1024, "shared memory of one CTA");
 };
 
-// Converts one fp32 weight matrix [rows x cols] (row-major, from the parameter blob) into an
-// interleaved fp16 tile; rows beyond `rows` up to `pad_rows` are zero.
-__device__ __forceinline__ void stage_weight(unsigned char* tile, const float* W, int rows, int pad_rows, int cols) {
+// This thread's row of its group's tile, and the TMEM lane base of its warp within the group.
+__device__ __forceinline__ int trow() { return (int)(threadIdx.x & 127u); }
+__device__ __forceinline__ uint32_t tlane() { return (threadIdx.x & 96u) << 16; }
+
+// Converts one fp32 weight matrix [rows x cols] (row-major, from the parameter blob) into the
+// interleaved fp16 pair (hi tile, lo tile); rows beyond `rows` up to `pad_rows` are zero.
+__device__ __forceinline__ void stage_weight(unsigned char* hi, unsigned char* lo, const float* W, int rows, int pad_rows,
+                                             int cols) {
     for (int e = threadIdx.x; e < pad_rows * (cols / 8); e += blockDim.x) {
         const int r = e / (cols / 8), c0 = (e - r * (cols / 8)) * 8;
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = r < rows ? W[r * cols + c0 + i] : 0.0f;
-        tc::st_chunk8(tile, r, c0, cols, v);
+        tc::st_chunk8_hilo(hi, lo, r, c0, cols, v);
     }
 }
 
@@ -100,10 +130,19 @@ __device__ __forceinline__ void gemm(uint32_t d, uint32_t a, int a_cols, bool a_
     }
 }
 
+// Forward layer with compensated operands: ACC = Ah*Wh^T + Ah*Wl^T + Al*Wh^T (both K-major; one
+// thread).  The large term first, then the two corrections into the same fp32 accumulator.
+__device__ __forceinline__ void gemm_fwd3(uint32_t d, uint32_t a_hi, uint32_t a_lo, int a_cols, uint32_t w_hi,
+                                         uint32_t w_lo, int N, int K) {
+    gemm(d, a_hi, a_cols, false, w_hi, a_cols, false, 128, N, K, 0);
+    gemm(d, a_hi, a_cols, false, w_lo, a_cols, false, 128, N, K, 1);
+    gemm(d, a_lo, a_cols, false, w_hi, a_cols, false, 128, N, K, 1);
+}
+
 // One row (this thread's sample) of an ACC region into registers.
 template <int N>
 __device__ __forceinline__ void acc_row(uint32_t tmem, uint32_t col, float (&v)[N]) {
-    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+    const uint32_t lane = tlane();
 #pragma unroll
     for (int j = 0; j < N; j += 16) {
         float t[16];
@@ -117,19 +156,21 @@ __device__ __forceinline__ void acc_row(uint32_t tmem, uint32_t col, float (&v)[
 template <int N>
 __device__ __forceinline__ void store_row(unsigned char* tile, int cols, const float (&v)[N]) {
 #pragma unroll
-    for (int c = 0; c < N; c += 8) tc::st_chunk8(tile, threadIdx.x, c, cols, v + c);
+    for (int c = 0; c < N; c += 8) tc::st_chunk8(tile, trow(), c, cols, v + c);
 }
 template <int N>
-__device__ __forceinline__ void load_row_h(const unsigned char* tile, int cols, float (&v)[N]) {
+__device__ __forceinline__ void store_row_hilo(unsigned char* hi, unsigned char* lo, int cols, const float (&v)[N]) {
 #pragma unroll
-    for (int c = 0; c < N; c += 8) tc::ld_chunk8(tile, threadIdx.x, c, cols, v + c);
+    for (int c = 0; c < N; c += 8) tc::st_chunk8_hilo(hi, lo, trow(), c, cols, v + c);
 }
 
 // Epilogue of a forward layer: row = relu(ACC * in_scale + bias) for N columns, 32 at a time (two
-// TMEM loads per wait; one copy of the loop body, to keep the kernel's code small).
+// TMEM loads per wait; one copy of the loop body, to keep the kernel's code small), stored as the
+// (hi, lo) pair that the next forward layer multiplies.
 __device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N, const float* bias, unsigned char* tile,
-                                              int cols, float in_scale = 1.0f) {
-    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+                                              unsigned char* lo_tile, int cols, float in_scale = 1.0f) {
+    const uint32_t lane = tlane();
+    const int r = trow();
 #pragma unroll 1
     for (int j = 0; j < N; j += 32) {
         float v[32];
@@ -139,35 +180,38 @@ __device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = fmaxf(fmaf(v[i], in_scale, bias[j + i]), 0.0f);
 #pragma unroll
-        for (int q = 0; q < 32; q += 8) tc::st_chunk8(tile, threadIdx.x, j + q, cols, v + q);
+        for (int q = 0; q < 32; q += 8) tc::st_chunk8_hilo(tile, lo_tile, r, j + q, cols, v + q);
     }
 }
 
 // Epilogue of a backward layer: row = ACC masked by (activation in `tile` > 0), written in place,
-// 32 columns at a time.
+// 32 columns at a time.  The mask reads the hi copy of the activation, which is > 0 whenever the
+// activation is, except below fp16's smallest subnormal (2^-24), where the delta's share is negligible.
 __device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N, unsigned char* tile, int cols) {
-    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+    const uint32_t lane = tlane();
+    const int r = trow();
 #pragma unroll 1
     for (int j = 0; j < N; j += 32) {
         float v[32], act[32];
         tc::tmem_ld16(tmem + lane + col + j, *reinterpret_cast<float(*)[16]>(v));
         tc::tmem_ld16(tmem + lane + col + j + 16, *reinterpret_cast<float(*)[16]>(v + 16));
 #pragma unroll
-        for (int q = 0; q < 32; q += 8) tc::ld_chunk8(tile, threadIdx.x, j + q, cols, act + q);
+        for (int q = 0; q < 32; q += 8) tc::ld_chunk8(tile, r, j + q, cols, act + q);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = act[i] > 0.0f ? v[i] : 0.0f;
 #pragma unroll
-        for (int q = 0; q < 32; q += 8) tc::st_chunk8(tile, threadIdx.x, j + q, cols, v + q);
+        for (int q = 0; q < 32; q += 8) tc::st_chunk8(tile, r, j + q, cols, v + q);
     }
 }
 
-// Hash encoding of this thread's sample straight into its fp16 row of the X0 tile, one 8-feature
-// chunk (8/F levels, 64/F independent gathers) at a time.
+// Hash encoding of this thread's sample straight into its row of the X0 tile pair (hi, lo), one
+// 8-feature chunk (8/F levels, 64/F independent gathers) at a time.
 template <int F>
 __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __restrict__ table, V3 p, bool hit,
-                                            unsigned char* tile) {
+                                            unsigned char* tile, unsigned char* lo_tile) {
     constexpr int LPOS = L * F, LV = 8 / F;
+    const int r = trow();
 #pragma unroll 1
     for (int q = 0; q < LPOS / 8; ++q) {
         float v[8];
@@ -197,9 +241,10 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] *= INPUT_SCALE;
-        tc::st_chunk8(tile, threadIdx.x, q * 8, LPOS, v);
+        tc::st_chunk8_hilo(tile, lo_tile, r, q * 8, LPOS, v);
     }
 }
+
 
 // Scatter of one level's hash-grid gradient (ffnerf_OG.cl:2090-2173): the thread's F raw feature
 // gradients `gl` become (coef_l * g) * w_c at the 8 trilinear corners, added with vector atomics.
@@ -214,7 +259,7 @@ template <int F>
 __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restrict__ grad, V3 p, int lvl,
                                               const float* gl, const float* coef, float* scratch) {
     const int lid = threadIdx.x & 31;
-    float* row = scratch + threadIdx.x * (8 * F);
+    float* row = scratch + trow() * (8 * F);
     float gf[F];
     bool any = false;
 #pragma unroll
@@ -285,7 +330,7 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
         while (rest) {
             const int m = __ffs(rest) - 1;
             rest &= rest - 1u;
-            const float* r = scratch + ((threadIdx.x & ~31u) + m) * (8 * F);
+            const float* r = scratch + ((trow() & ~31) + m) * (8 * F);
 #pragma unroll
             for (int q = 0; q < 8 * F; q += 4) {
                 const float4 t = *reinterpret_cast<const float4*>(r + q);
@@ -312,7 +357,7 @@ template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
                                                   V3 p, float unscale, const float* coef, float* scratch, float* gbuf) {
     constexpr int LPOS = L * F;
-    const uint32_t lane = (threadIdx.x & ~31u) << 16;
+    const uint32_t lane = tlane();
     if constexpr (F != 2) {
         // F = 4: the parked rows would not fit the free C2 tile; levels straight from the TMEM loads
 #pragma unroll 1
@@ -330,7 +375,7 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
         }
         return;
     }
-    const int row = threadIdx.x, sw = row & 7;
+    const int row = trow(), sw = row & 7;
     float4* grow = reinterpret_cast<float4*>(gbuf + row * LPOS);
 #pragma unroll
     for (int j = 0; j < LPOS; j += 16) {
@@ -400,73 +445,87 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // encodings; every sample is live, the view direction is fixed at (0.36, 0.48, 0.8), and the
 // compositing is replaced by the loss sum_k 0.5 (rgb_k - 0.5)^2 per sample (no density term), so
 // the step is the two MLPs forward and backward with their weight gradients; no table scatter.
+//
+// Work split: tile g of the CTA's groups takes tiles blockIdx.x * GROUPS + g, advancing by
+// gridDim.x * GROUPS; each group writes its own row of weight-gradient partials
+// (a.partials[(blockIdx.x * GROUPS + g) * P]).
 template <int F, int ND, bool STAGED = false, bool MLPB = false>
-__global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kernel(const StepArgs a) {
     static_assert(!MLPB || STAGED, "the MLP microbenchmark runs the staged form");
     using PL = TcPlan<F, ND>;
     constexpr int LPOS = PL::LPOS;
     extern __shared__ __align__(1024) unsigned char smem_tc[];
-    unsigned char* smem = smem_tc;
+    const int grp = PL::GROUPS == 1 ? 0 : (int)(threadIdx.x >> 7);
+    unsigned char* gsm = smem_tc + PL::SHARED_BYTES + grp * PL::GROUP_BYTES;   // this group's tiles
     const DevConfig& c = a.c;
     const ParamLayout& lo = a.lo;
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    unsigned char* tX0 = smem + PL::X0;
-    unsigned char* tXC = smem + PL::XC;
-    unsigned char* tC1 = smem + PL::C1;
-    unsigned char* tC2 = smem + PL::C2;
-    unsigned char* tDC = smem + PL::DC;
-    float* bias = reinterpret_cast<float*>(smem + PL::BIAS);
-    float* bgrad = reinterpret_cast<float*>(smem + PL::BGRAD);
-    float* rayb = reinterpret_cast<float*>(smem + PL::RAY);
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + PL::MISC);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PL::MISC + 8);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + PL::MISC + 12);
-    const uint32_t sbase = tc::smem_u32(smem);
-    auto S = [&](int off) { return sbase + (uint32_t)off; };
-    auto tH = [&](int l) { return smem + PL::HD + l * 128 * 64 * 2; };
+    const int tid = trow();            // this thread's row of the group's tile
+    const int warp = tid >> 5;         // warp within the group
+    unsigned char* tX0 = gsm + PL::X0;
+    unsigned char* tLO = gsm + PL::LO;
+    unsigned char* tXC = gsm + PL::XC;
+    unsigned char* tC1 = gsm + PL::C1;
+    unsigned char* tC2 = gsm + PL::C2;
+    unsigned char* tDC = gsm + PL::DC;
+    const float* bias = reinterpret_cast<const float*>(smem_tc + PL::BIAS);
+    float* bgrad = reinterpret_cast<float*>(gsm + PL::BGRAD);
+    float* rayb = reinterpret_cast<float*>(gsm + PL::RAY);
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(gsm + PL::MISC);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_tc + PL::SHARED_BYTES + PL::MISC + 8);   // group 0's slot
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gsm + PL::MISC + 12);
+    const uint32_t sbase = tc::smem_u32(smem_tc);
+    const uint32_t gbase = tc::smem_u32(gsm);
+    auto S = [&](int off) { return sbase + (uint32_t)off; };        // shared region (weights, one-hot)
+    auto G = [&](int off) { return gbase + (uint32_t)off; };        // this group's tiles
+    auto tH = [&](int l) { return gsm + PL::HD + l * 128 * 64 * 2; };
 
     const bool train = a.do_train != 0;
     const bool probe = a.probe != 0;
     const bool backward = train && !probe;
 
-    // ---- one-time set-up: barrier, tensor memory, fp16 weights, biases, one-hot tile
+    // ---- one-time set-up: barriers, tensor memory, fp16 weight pairs, biases, one-hot tile
     if (tid == 0) {
         tc::mbar_init(mbar, 1);
         *abort_flag = 0;
     }
-    if (warp == 0) tc::tmem_alloc(tmem_slot, PL::TMEM_COLS);
+    if (threadIdx.x < 32) tc::tmem_alloc(tmem_slot, PL::TMEM_COLS);
     const float* P = a.params;
-    stage_weight(smem + PL::W_DIN, P + lo.off[P_WD_IN], 64, 64, LPOS);
-    if (ND >= 2) stage_weight(smem + PL::W_D01, P + lo.off[P_WD_01], 64, 64, 64);
-    stage_weight(smem + PL::W_DOUT, P + lo.off[P_WD_OUT], 16, 16, 64);
-    stage_weight(smem + PL::W_CIN, P + lo.off[P_WC_IN], 64, 64, 32);
-    stage_weight(smem + PL::W_C01, P + lo.off[P_WC_01], 64, 64, 64);
-    stage_weight(smem + PL::W_COUT, P + lo.off[P_WC_OUT], 3, 16, 64);
-    for (int i = tid; i < 64; i += 128) {
-        bias[i] = P[lo.off[P_BD_0] + i];
-        bias[64 + i] = ND >= 2 ? P[lo.off[P_BD_1] + i] : 0.0f;
-        bias[144 + i] = P[lo.off[P_BC_0] + i];
-        bias[208 + i] = P[lo.off[P_BC_1] + i];
-    }
-    if (tid < 16) {
-        bias[128 + tid] = P[lo.off[P_BD_OUT] + tid];
-        bias[272 + tid] = tid < 3 ? P[lo.off[P_BC_OUT] + tid] : 0.0f;
+    unsigned char* wh = smem_tc + PL::W_HI;
+    unsigned char* wl = smem_tc + PL::W_LO;
+    stage_weight(wh + PL::W_DIN, wl + PL::W_DIN, P + lo.off[P_WD_IN], 64, 64, LPOS);
+    if (ND >= 2) stage_weight(wh + PL::W_D01, wl + PL::W_D01, P + lo.off[P_WD_01], 64, 64, 64);
+    stage_weight(wh + PL::W_DOUT, wl + PL::W_DOUT, P + lo.off[P_WD_OUT], 16, 16, 64);
+    stage_weight(wh + PL::W_CIN, wl + PL::W_CIN, P + lo.off[P_WC_IN], 64, 64, 32);
+    stage_weight(wh + PL::W_C01, wl + PL::W_C01, P + lo.off[P_WC_01], 64, 64, 64);
+    stage_weight(wh + PL::W_COUT, wl + PL::W_COUT, P + lo.off[P_WC_OUT], 3, 16, 64);
+    {
+        float* sb = reinterpret_cast<float*>(smem_tc + PL::BIAS);
+        for (int i = threadIdx.x; i < 64; i += blockDim.x) {
+            sb[i] = P[lo.off[P_BD_0] + i];
+            sb[64 + i] = ND >= 2 ? P[lo.off[P_BD_1] + i] : 0.0f;
+            sb[144 + i] = P[lo.off[P_BC_0] + i];
+            sb[208 + i] = P[lo.off[P_BC_1] + i];
+        }
+        if (threadIdx.x < 16) {
+            sb[128 + threadIdx.x] = P[lo.off[P_BD_OUT] + threadIdx.x];
+            sb[272 + threadIdx.x] = threadIdx.x < 3 ? P[lo.off[P_BC_OUT] + threadIdx.x] : 0.0f;
+        }
     }
     if (tid < 32) bgrad[tid] = 0.0f;
-    {
+    if (threadIdx.x < 128) {
         float v[8] = {1.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        tc::st_chunk8(smem + PL::ONES, tid, 0, 8, v);
+        tc::st_chunk8(smem_tc + PL::ONES, threadIdx.x, 0, 8, v);
     }
     tc::fence_proxy_async();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tmem = tmem_base + (uint32_t)grp * PL::TMEM_GROUP;   // this group's columns
     uint32_t phase = 0;
     bool dw_started = false;
 
-    // Commit the MMAs issued so far and wait for them (all threads).
+    // Commit the MMAs this group issued so far and wait for them (the group's threads).
     auto sync_mma = [&]() {
         if (tid == 0) tc::commit(mbar);
         if (!*abort_flag) {
@@ -478,11 +537,11 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         phase ^= 1u;
         tc::fence_after_sync();
     };
-    // All threads have finished reading TMEM and writing shared operands: MMAs may be issued.
+    // The group's threads have finished reading TMEM and writing shared operands: MMAs may be issued.
     auto handoff = [&]() {
         tc::fence_proxy_async();
         tc::fence_before_sync();
-        __syncthreads();
+        tile_sync();
         tc::fence_after_sync();
     };
 
@@ -506,13 +565,16 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
     uint32_t* sChg = reinterpret_cast<uint32_t*>(sAffE + 128);
     float* sRay = reinterpret_cast<float*>(sChg + 16);
 
-    // Staged form: while a tile runs, the next tile's X0 is copied into the other X0 buffer
-    // (cp.async) and its per-sample inputs are loaded into registers.
-    int xb = 0;
+    const int first_tile = (int)blockIdx.x * PL::GROUPS + grp;
+    const int tile_step = (int)gridDim.x * PL::GROUPS;
+
+    // Staged form: the next tile's X0 pair is copied (cp.async) into X0 / LO as soon as the current
+    // tile's last MMA that reads them has completed -- before the table scatter, which it overlaps
+    // -- and its per-sample inputs are loaded into registers.
     float2 nx_tdt = make_float2(0.f, 0.f);
     uint4 nx_rst = make_uint4(0u, 0u, 0u, 0u);
     float4 nx_ro = make_float4(0.f, 0.f, 0.f, 0.f), nx_rd = make_float4(0.f, 0.f, 1.f, 0.f);
-    auto prefetch = [&](int t, int buf) {
+    auto prefetch = [&](int t) {
         const uint32_t ri = (uint32_t)t * rays_per_tile + rl;
         nx_tdt = make_float2(0.f, 0.f);
         nx_rst = make_uint4(0u, 0u, 0u, 0u);
@@ -524,21 +586,24 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             nx_ro = a.rays[2 * ri];
             nx_rd = a.rays[2 * ri + 1];
         }
-        const unsigned char* src = a.x0_stage + (size_t)t * (128 * LPOS * 2);
-        const uint32_t dst = S(buf ? PL::X0B : PL::X0);
+        constexpr int HALF = 128 * LPOS * 2;   // bytes of the hi (and of the lo) tile
+        const unsigned char* src = a.x0_stage + (size_t)t * PL::X0_STAGE_BYTES;
 #pragma unroll
-        for (int k = tid; k < 128 * LPOS * 2 / 16; k += 128) cp_async16(dst + 16u * (uint32_t)k, src + 16 * k);
+        for (int k = tid; k < HALF / 16; k += 128) {
+            cp_async16(G(PL::X0) + 16u * (uint32_t)k, src + 16 * k);
+            cp_async16(G(PL::LO) + 16u * (uint32_t)k, src + HALF + 16 * k);
+        }
         cp_async_commit();
     };
     if constexpr (STAGED) {
-        if ((int)blockIdx.x < n_tiles) prefetch(blockIdx.x, 0);
+        if (first_tile < n_tiles) prefetch(first_tile);
     }
 
-    for (int tile = blockIdx.x; tile < n_tiles && !*abort_flag; tile += gridDim.x) {
+    for (int tile = first_tile; tile < n_tiles && !*abort_flag; tile += tile_step) {
         const uint32_t ray_idx = (uint32_t)tile * rays_per_tile + rl;
         const bool valid = ray_idx < a.n_rays;
         const uint32_t ray_id = a.ray_offset + ray_idx;
-        const int x0_off = STAGED && xb ? PL::X0B : PL::X0;   // this tile's X0 buffer
+        const bool more = tile + tile_step < n_tiles;
         float4 ro = make_float4(0.f, 0.f, 0.f, 0.f), rd = make_float4(0.f, 0.f, 1.f, 0.f);
         if constexpr (MLPB) {
             rd = make_float4(0.36f, 0.48f, 0.8f, 0.f);
@@ -563,40 +628,45 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             if (lid == 0) { sChg[rl * 2] = rst.x; sChg[rl * 2 + 1] = rst.y; }
             hit = MLPB || rst.z != 0u;
             cp_async_wait_all();
-            __syncthreads();
-            // the other buffer was last read by the previous tile's MMAs, which have completed
-            if (tile + (int)gridDim.x < n_tiles) prefetch(tile + (int)gridDim.x, xb ^ 1);
-            xb ^= 1;
+            tile_sync();
         } else {
             ray_sampler(a, R, hit, idx_sel);
         }
+        bool prefetched = false;
+        auto prefetch_next = [&]() {
+            if constexpr (STAGED) {
+                if (more && !prefetched) prefetch(tile + tile_step);
+            }
+            prefetched = true;
+        };
         const float* rs = sRay + rl * 16;
         const float t_s = sTs[tid];
         const float dt_s = sDTs[tid];
         const V3 xs = ray_point(o, d, t_s);
         const V3 pn = normalize_pos(c, xs);
 
-        // ---------------- forward MLP on the tensor cores
+        // ---------------- forward MLP on the tensor cores (compensated operand pairs)
         float sigma = 0.0f, rgb[3] = {0.f, 0.f, 0.f}, dout0 = 0.0f;
         if (probe && a.bypass) {
             float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
             if (valid) b = a.bypass[(size_t)ray_idx * spr + lid];
             sigma = b.x; rgb[0] = b.y; rgb[1] = b.z; rgb[2] = b.w;
         } else {
-            if constexpr (!STAGED) encode_rows<F>(c, a.table, pn, hit, tX0);
+            if constexpr (!STAGED) encode_rows<F>(c, a.table, pn, hit, tX0, tLO);
             handoff();
-            if (tid == 0) gemm(tmem + PL::ACC, S(x0_off), LPOS, false, S(PL::W_DIN), LPOS, false, 128, 64, LPOS, 0);
+            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::X0), G(PL::LO), LPOS, S(PL::W_HI + PL::W_DIN), S(PL::W_LO + PL::W_DIN), 64, LPOS);
             sync_mma();
-            epi_bias_relu(tmem, PL::ACC, 64, bias, tH(0), 64, 1.0f / INPUT_SCALE);
+            epi_bias_relu(tmem, PL::ACC, 64, bias, tH(0), tLO, 64, 1.0f / INPUT_SCALE);
             if (ND >= 2) {
                 handoff();
-                if (tid == 0) gemm(tmem + PL::ACC, S(PL::HD), 64, false, S(PL::W_D01), 64, false, 128, 64, 64, 0);
+                if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::HD), G(PL::LO), 64, S(PL::W_HI + PL::W_D01), S(PL::W_LO + PL::W_D01), 64, 64);
                 sync_mma();
-                epi_bias_relu(tmem, PL::ACC, 64, bias + 64, tH(ND - 1), 64);
+                epi_bias_relu(tmem, PL::ACC, 64, bias + 64, tH(ND - 1), tLO, 64);
             }
             handoff();
             if (tid == 0)
-                gemm(tmem + PL::ACC, S(PL::HD + (ND - 1) * 128 * 64 * 2), 64, false, S(PL::W_DOUT), 64, false, 128, 16, 64, 0);
+                gemm_fwd3(tmem + PL::ACC, G(PL::HD + (ND - 1) * 128 * 64 * 2), G(PL::LO), 64, S(PL::W_HI + PL::W_DOUT),
+                          S(PL::W_LO + PL::W_DOUT), 16, 64);
             sync_mma();
             {
                 float v[32];
@@ -610,18 +680,18 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
                 sh16(d.x, d.y, d.z, sh);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[16 + j] = sh[j] * a.sh_mult;
-                store_row<32>(tXC, 32, v);
+                store_row_hilo<32>(tXC, tLO, 32, v);
             }
             handoff();
-            if (tid == 0) gemm(tmem + PL::ACC, S(PL::XC), 32, false, S(PL::W_CIN), 32, false, 128, 64, 32, 0);
+            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_CIN), S(PL::W_LO + PL::W_CIN), 64, 32);
             sync_mma();
-            epi_bias_relu(tmem, PL::ACC, 64, bias + 144, tC1, 64);
+            epi_bias_relu(tmem, PL::ACC, 64, bias + 144, tC1, tLO, 64);
             handoff();
-            if (tid == 0) gemm(tmem + PL::ACC, S(PL::C1), 64, false, S(PL::W_C01), 64, false, 128, 64, 64, 0);
+            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::C1), G(PL::LO), 64, S(PL::W_HI + PL::W_C01), S(PL::W_LO + PL::W_C01), 64, 64);
             sync_mma();
-            epi_bias_relu(tmem, PL::ACC, 64, bias + 208, tC2, 64);
+            epi_bias_relu(tmem, PL::ACC, 64, bias + 208, tC2, tLO, 64);
             handoff();
-            if (tid == 0) gemm(tmem + PL::ACC, S(PL::C2), 64, false, S(PL::W_COUT), 64, false, 128, 16, 64, 0);
+            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_COUT), S(PL::W_LO + PL::W_COUT), 16, 64);
             sync_mma();
             {
                 float v[16];
@@ -659,7 +729,8 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         }
         if (!backward) {
             tc::fence_before_sync();
-            __syncthreads();
+            tile_sync();          // every thread is past its reads of X0 / LO / the ray arrays
+            prefetch_next();
             continue;
         }
 
@@ -682,6 +753,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
             ddout0 = 1.0f * d_sigma * softplus_prime(fclamp(dout0, -18.0f, 18.0f));
         }
         {
+            // the forward's last MMA (which read the lo tile) has completed: DC takes its place
             float v[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;
@@ -698,8 +770,8 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         const uint32_t acc0 = dw_started ? 1u : 0u;
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_COUT_T, S(PL::C2), 64, true, S(PL::DC), 16, true, 64, 16, 128, acc0);  // dWc_out^T
-            gemm(tmem + PL::ACC, S(PL::DC), 16, false, S(PL::W_COUT), 64, true, 128, 64, 16, 0);     // dC2
+            gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC), 16, true, 64, 16, 128, acc0);            // dWc_out^T
+            gemm(tmem + PL::ACC, G(PL::DC), 16, false, S(PL::W_HI + PL::W_COUT), 64, true, 128, 64, 16, 0);      // dC2
         }
         sync_mma();
         {
@@ -707,9 +779,9 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         }
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_C01, S(PL::C2), 64, true, S(PL::C1), 64, true, 64, 64, 128, acc0);    // dWc_01
-            gemm(tmem + PL::B_C1, S(PL::C2), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);     // dbc_1
-            gemm(tmem + PL::ACC, S(PL::C2), 64, false, S(PL::W_C01), 64, true, 128, 64, 64, 0);      // dC1
+            gemm(tmem + PL::DW_C01, G(PL::C2), 64, true, G(PL::C1), 64, true, 64, 64, 128, acc0);               // dWc_01
+            gemm(tmem + PL::B_C1, G(PL::C2), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbc_1
+            gemm(tmem + PL::ACC, G(PL::C2), 64, false, S(PL::W_HI + PL::W_C01), 64, true, 128, 64, 64, 0);       // dC1
         }
         sync_mma();
         {
@@ -717,9 +789,9 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         }
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_CIN, S(PL::C1), 64, true, S(PL::XC), 32, true, 64, 32, 128, acc0);    // dWc_in
-            gemm(tmem + PL::B_C0, S(PL::C1), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);     // dbc_0
-            gemm(tmem + PL::ACC, S(PL::C1), 64, false, S(PL::W_CIN), 32, true, 128, 16, 64, 0);      // dDout
+            gemm(tmem + PL::DW_CIN, G(PL::C1), 64, true, G(PL::XC), 32, true, 64, 32, 128, acc0);               // dWc_in
+            gemm(tmem + PL::B_C0, G(PL::C1), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbc_0
+            gemm(tmem + PL::ACC, G(PL::C1), 64, false, S(PL::W_HI + PL::W_CIN), 32, true, 128, 16, 64, 0);       // dDout
         }
         sync_mma();
         {
@@ -734,11 +806,11 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
                 if ((tid & 1) == 0) atomicAdd(bgrad + ((tid >> 1) & 15), sum);
             }
         }
-        const uint32_t hlast = S(PL::HD + (ND - 1) * 128 * 64 * 2);
+        const uint32_t hlast = G(PL::HD + (ND - 1) * 128 * 64 * 2);
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, S(PL::XC), 32, true, 64, 16, 128, acc0);     // dWd_out^T
-            gemm(tmem + PL::ACC, S(PL::XC), 32, false, S(PL::W_DOUT), 64, true, 128, 64, 16, 0);     // dH_last
+            gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::XC), 32, true, 64, 16, 128, acc0);               // dWd_out^T
+            gemm(tmem + PL::ACC, G(PL::XC), 32, false, S(PL::W_HI + PL::W_DOUT), 64, true, 128, 64, 16, 0);     // dH_last
         }
         sync_mma();
         {
@@ -747,34 +819,36 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         if (ND >= 2) {
             handoff();
             if (tid == 0) {
-                gemm(tmem + PL::DW_D01, hlast, 64, true, S(PL::HD), 64, true, 64, 64, 128, acc0);    // dWd_01
-                gemm(tmem + PL::B_D1, hlast, 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);     // dbd_1
-                gemm(tmem + PL::ACC, hlast, 64, false, S(PL::W_D01), 64, true, 128, 64, 64, 0);      // dH_0
+                gemm(tmem + PL::DW_D01, hlast, 64, true, G(PL::HD), 64, true, 64, 64, 128, acc0);               // dWd_01
+                gemm(tmem + PL::B_D1, hlast, 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbd_1
+                gemm(tmem + PL::ACC, hlast, 64, false, S(PL::W_HI + PL::W_D01), 64, true, 128, 64, 64, 0);       // dH_0
             }
             sync_mma();
             epi_relu_mask(tmem, PL::ACC, 64, tH(0), 64);
         }
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_DIN, S(PL::HD), 64, true, S(x0_off), LPOS, true, 64, LPOS, 128, acc0);  // dWd_in
-            gemm(tmem + PL::B_D0, S(PL::HD), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);       // dbd_0
-            gemm(tmem + PL::ACC, S(PL::HD), 64, false, S(PL::W_DIN), LPOS, true, 128, LPOS, 64, 0);    // hash grads
+            gemm(tmem + PL::DW_DIN, G(PL::HD), 64, true, G(PL::X0), LPOS, true, 64, LPOS, 128, acc0);           // dWd_in
+            gemm(tmem + PL::B_D0, G(PL::HD), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbd_0
+            gemm(tmem + PL::ACC, G(PL::HD), 64, false, S(PL::W_HI + PL::W_DIN), LPOS, true, 128, LPOS, 64, 0);   // hash grads
         }
         sync_mma();
         dw_started = true;
+        // X0 and LO are dead: the next tile's pair lands while this tile scatters
+        prefetch_next();
         // the activation tiles are dead once the last MMAs completed: C1 holds the scatter's exchange
         // rows, C2 the parked gradients
         if (!MLPB && hit && valid)
             scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef,
                                  reinterpret_cast<float*>(tC1), reinterpret_cast<float*>(tC2));
         tc::fence_before_sync();
-        __syncthreads();
+        tile_sync();
     }
 
     if constexpr (STAGED) cp_async_wait_all();      // a prefetch left by an early exit
-    // ---- weight-gradient partials of this CTA: TMEM (M = 64 layout) -> global, unscaled
+    // ---- weight-gradient partials of this group: TMEM (M = 64 layout) -> global, unscaled
     if (backward && a.partials) {
-        float* part = a.partials + (size_t)blockIdx.x * lo.total;
+        float* part = a.partials + ((size_t)blockIdx.x * PL::GROUPS + grp) * lo.total;
         const int lane = tid & 31;
         const int row = warp * 16 + lane;              // M = 64: rows 16w..16w+15 live in lanes 32w..32w+15
         const bool live = dw_started && !*abort_flag;
@@ -782,7 +856,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
                         float extra = 1.0f) {
             for (int j = 0; j < ncols; j += 16) {
                 float v[16];
-                tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + col + j, v);
+                tc::tmem_ld16(tmem + tlane() + col + j, v);
                 tc::tmem_wait_ld();
                 if (lane < 16) {
 #pragma unroll
@@ -803,7 +877,7 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
         dump(PL::DW_COUT_T, 16, lo.off[P_WC_OUT], true, 3, 64);
         auto dump_bias = [&](uint32_t col, int dst_off) {
             float v[16];
-            tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + col, v);
+            tc::tmem_ld16(tmem + tlane() + col, v);
             tc::tmem_wait_ld();
             if (lane < 16) part[dst_off + row] = live ? v[0] * (1.0f / DELTA_SCALE) : 0.0f;
         };
@@ -817,8 +891,10 @@ __global__ void __launch_bounds__(128, 1) fused_step_tc_kernel(const StepArgs a)
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tmem, PL::TMEM_COLS);
+    if (threadIdx.x < 32) tc::tmem_dealloc(tmem_base, PL::TMEM_COLS);
 }
+
+
 
 
 // ---------------------------------------------------------------- split step: stage kernels
@@ -881,7 +957,8 @@ __global__ void __launch_bounds__(128) sample_stage_kernel(const StepArgs a, flo
     }
 }
 
-// Hash encoding into the X0 operand tiles (x INPUT_SCALE, fp16), the same accumulation order as
+// Hash encoding into the staged X0 operand tiles (x INPUT_SCALE, as the compensated fp16 pair: the
+// hi tile, then the lo tile, TcPlan::X0_STAGE_BYTES per 128-row tile), the same accumulation order as
 // encode_rows.  Work is level-major: block-sized chunks of 256 consecutive samples for one level,
 // all chunks of level 0 first, so the whole grid gathers from one level's table at a time (an L2
 // working set of one level), and the 32 lanes of a warp -- consecutive samples of one ray -- read
@@ -893,6 +970,7 @@ __global__ void __launch_bounds__(256) encode_stage_kernel(const DevConfig c, co
                                                            const float4* __restrict__ pn_in, int64_t n_valid,
                                                            int64_t n_rows, unsigned char* __restrict__ x0_out) {
     constexpr int LPOS = L * F;
+    constexpr int HALF = 128 * LPOS * 2;   // bytes of one fp16 tile
     const int n_chunks = (int)((n_rows + 255) / 256);
     const int items = n_chunks * L;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
@@ -923,26 +1001,34 @@ __global__ void __launch_bounds__(256) encode_stage_kernel(const DevConfig c, co
                 }
             }
         }
-        unsigned char* tile = x0_out + (i >> 7) * (int64_t)(128 * LPOS * 2);
+        unsigned char* tile = x0_out + (i >> 7) * (int64_t)(2 * HALF);
         const int r = (int)(i & 127);
-        __half2 h0 = __halves2half2(tc::to_half_sat(v[0] * INPUT_SCALE), tc::to_half_sat(v[1] * INPUT_SCALE));
+        __half hi[F], lo[F];
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+            const float x = v[f] * INPUT_SCALE;
+            hi[f] = tc::to_half_sat(x);
+            lo[f] = tc::to_half_sat(x - __half2float(hi[f]));
+        }
+        const uint32_t off = tc::tile_off(r, lvl * F, LPOS);
         if constexpr (F == 2) {
-            *reinterpret_cast<__half2*>(tile + tc::tile_off(r, lvl * 2, LPOS)) = h0;
+            *reinterpret_cast<__half2*>(tile + off) = __halves2half2(hi[0], hi[1]);
+            *reinterpret_cast<__half2*>(tile + HALF + off) = __halves2half2(lo[0], lo[1]);
         } else {
-            __half2 h1 = __halves2half2(tc::to_half_sat(v[2] * INPUT_SCALE), tc::to_half_sat(v[3] * INPUT_SCALE));
-            uint2 u;
-            u.x = *reinterpret_cast<uint32_t*>(&h0);
-            u.y = *reinterpret_cast<uint32_t*>(&h1);
-            *reinterpret_cast<uint2*>(tile + tc::tile_off(r, lvl * 4, LPOS)) = u;
+            __half2 h[2] = {__halves2half2(hi[0], hi[1]), __halves2half2(hi[2], hi[3])};
+            __half2 l[2] = {__halves2half2(lo[0], lo[1]), __halves2half2(lo[2], lo[3])};
+            *reinterpret_cast<uint2*>(tile + off) = *reinterpret_cast<uint2*>(h);
+            *reinterpret_cast<uint2*>(tile + HALF + off) = *reinterpret_cast<uint2*>(l);
         }
     }
 }
 
-// Packs row-major fp16 rows [n][16F] into the 128-row operand tiles of the MLP kernels (x INPUT_SCALE,
-// the encoder's convention); one thread per (row, 8-column chunk).
+// Packs row-major fp16 rows [n][16F] into the staged operand tiles of the MLP kernels (x INPUT_SCALE,
+// the encoder's convention; a power-of-two scale of an fp16 value is exact, so every lo tile is
+// zero); one thread per (row, 8-column chunk).
 template <int F>
 __global__ void pack_x0_kernel(const __half* __restrict__ x, int64_t n, unsigned char* __restrict__ tiles) {
-    constexpr int LPOS = L * F, CH = LPOS / 8;
+    constexpr int LPOS = L * F, CH = LPOS / 8, HALF = 128 * LPOS * 2;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n * CH) return;
     const int64_t row = i / CH;
@@ -956,7 +1042,8 @@ __global__ void pack_x0_kernel(const __half* __restrict__ x, int64_t n, unsigned
         v[2 * k] = f.x * INPUT_SCALE;
         v[2 * k + 1] = f.y * INPUT_SCALE;
     }
-    tc::st_chunk8(tiles + (row / 128) * (128 * LPOS * 2), (int)(row % 128), c0, LPOS, v);
+    unsigned char* tile = tiles + (row / 128) * (2 * HALF);
+    tc::st_chunk8_hilo(tile, tile + HALF, (int)(row % 128), c0, LPOS, v);
 }
 
 }  // namespace ffn

@@ -124,6 +124,25 @@ __device__ __forceinline__ void st_chunk8(unsigned char* tile, int r, int c0, in
     for (int i = 0; i < 4; ++i) h[i] = __halves2half2(to_half_sat(v[2 * i]), to_half_sat(v[2 * i + 1]));
     *reinterpret_cast<uint4*>(tile + tile_off(r, c0, cols)) = *reinterpret_cast<uint4*>(h);
 }
+// Stores 8 values as a compensated pair of fp16 chunks: hi = fp16(x) into `hi_tile`, lo = fp16(x - hi)
+// into `lo_tile` (same position), so that hi + lo carries about 22 significant bits.  A product
+// with an operand pair is formed as hi*hi' + hi*lo' + lo*hi' (the split-fp16 scheme of Markidis et
+// al., "NVIDIA Tensor Core Programmability, Performance & Precision", IPDPSW 2018, and Ootomo &
+// Yokota, "Recovering single-precision accuracy from Tensor Cores while surpassing the FP32
+// theoretical peak", IJHPCA 2022); the lo*lo' term is below fp32 rounding and is left out.
+__device__ __forceinline__ void st_chunk8_hilo(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
+                                               const float* v) {
+    __half2 h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half a = to_half_sat(v[2 * i]), b = to_half_sat(v[2 * i + 1]);
+        h[i] = __halves2half2(a, b);
+        l[i] = __halves2half2(to_half_sat(v[2 * i] - __half2float(a)), to_half_sat(v[2 * i + 1] - __half2float(b)));
+    }
+    const uint32_t off = tile_off(r, c0, cols);
+    *reinterpret_cast<uint4*>(hi_tile + off) = *reinterpret_cast<uint4*>(h);
+    *reinterpret_cast<uint4*>(lo_tile + off) = *reinterpret_cast<uint4*>(l);
+}
 __device__ __forceinline__ void ld_chunk8(const unsigned char* tile, int r, int c0, int cols, float* v) {
     uint4 u = *reinterpret_cast<const uint4*>(tile + tile_off(r, c0, cols));
     const __half2* h = reinterpret_cast<const __half2*>(&u);

@@ -4,8 +4,8 @@ same step read it (ffnerf_OG.cl:2155-2168) -- against the CPU oracle in sequenti
 (rays in order, each update applied at once: one legal schedule of the same race).
 
 Contracts:
-  * one step: the table change matches the oracle's within rel-L2 1e-3 (fp32 MLP) / 5e-2 (fp16
-    tensor-core MLP), the gradient buffer's table part stays zero;
+  * one step: the table change matches the oracle's within rel-L2 1e-3 (fp32 MLP) / 1e-2 (fp16
+    tensor-core MLP, the contract's gradient tolerance), the gradient buffer's table part stays zero;
   * an Adam table refuses immediate updates.
 (100-step training runs in this mode are in test_gpu_train100.py.)
 """
@@ -21,8 +21,8 @@ from oracle import OrcStep, make_orc_config
 import ffn_native as fn
 
 GEOM = dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0)
-TOL = {"fp32": (1e-3,), "fp16": (5e-2,)}
-MLP_GRAD_TOL = {"fp32": 1e-3, "fp16": 5e-2}
+TOL = {"fp32": (1e-3,), "fp16": (1e-2,)}
+MLP_GRAD_TOL = {"fp32": 1e-3, "fp16": 1e-2}
 
 
 def _cuda(a):

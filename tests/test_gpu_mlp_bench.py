@@ -1,8 +1,9 @@
 """The MLP microbenchmark (ffn_pack_x0 + ffn_mlp_bench) against a plain PyTorch fp32 reference of the
 same computation: density MLP 32 -> 64 -> 16 and colour MLP [16 density outputs, SH16(d)] -> 64 -> 64 ->
 3 with sigmoid_soft, d = (0.36, 0.48, 0.8), loss sum 0.5 (rgb - 0.5)^2, gradients summed over the
-samples.  The device runs fp16 operands and activations with fp32 accumulation, so each parameter's
-gradient is held to rel-L2 5e-2 of the fp32 reference.
+samples.  The device runs the forward on compensated fp16 operand pairs and the backward on fp16
+operands, with fp32 accumulation; each parameter's gradient is held to rel-L2 1e-2 of the fp32
+reference (the contract's gradient tolerance).
 """
 import numpy as np
 import pytest
@@ -55,7 +56,7 @@ def test_mlp_bench_matches_torch_fp32():
     table_before = ctx.tensor(fn.BUF_TABLE).clone()
     n = 1 << 14
     x = torch.randn((n, 32), generator=torch.Generator().manual_seed(5)).half()
-    tiles = torch.empty(n * 32 * 2, dtype=torch.uint8, device="cuda")
+    tiles = torch.empty(ctx.x0_tile_bytes(n), dtype=torch.uint8, device="cuda")
     ctx.pack_x0(x.cuda(), tiles, n)
     ctx.mlp_bench(tiles, n)
     torch.cuda.synchronize()
@@ -81,14 +82,14 @@ def test_mlp_bench_matches_torch_fp32():
         o, s = lay[k]
         ref = t.grad.detach().numpy().reshape(-1)
         assert np.isfinite(g_dev[o:o + s]).all(), k
-        assert rel_l2(g_dev[o:o + s], ref) < 5e-2, (k, rel_l2(g_dev[o:o + s], ref))
+        assert rel_l2(g_dev[o:o + s], ref) < 1e-2, (k, rel_l2(g_dev[o:o + s], ref))
     assert ctx.status() == 0
 
 
 def test_mlp_bench_rejects_bad_sizes():
     g = make_geometry(F=2, ND=1, NC=2, spr=64, G=16, log2_entries=12, rmax=512.0)
     ctx = fn.Context(g, mlp_precision="fp16")
-    tiles = torch.empty(200 * 64, dtype=torch.uint8, device="cuda")
+    tiles = torch.empty(ctx.x0_tile_bytes(200), dtype=torch.uint8, device="cuda")
     with pytest.raises(Exception):
         ctx.mlp_bench(tiles, 200)            # not a multiple of the 128-row tile
     ctx32 = fn.Context(g, mlp_precision="fp32")

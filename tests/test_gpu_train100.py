@@ -3,12 +3,13 @@ step-start table; table gradients summed, then applied), for both table-update m
 device (deferred; immediate = the reference's Hogwild update inside the fused kernel) and both
 MLP precisions.
 
-Contracts (fp32 MLP / fp16 tensor-core MLP):
-  * per-step loss within 1e-3 / 2e-3 relative of the oracle's, every step;
-  * parameters and table within rel-L2 1e-2 / 3e-2 and 1e-2 of the oracle's after 100 steps;
+Contracts (fp32 MLP / fp16 tensor-core MLP; the north-star tolerances for both):
+  * per-step loss within 1e-3 relative of the oracle's, every step;
+  * parameters and table within rel-L2 1e-2 of the oracle's after 100 steps;
   * gradients after 100 steps, evaluated on the device's own state (so that the comparison
     measures the kernels, not the divergence of two trajectories): MLP gradients within rel-L2
-    1e-4 / 5e-2; table gradients (deferred) within the same, or the step's table change
+    1e-4 (fp32) / 1e-2 (fp16, measured ~1e-4: the backward's fp16 operand rounding); table
+    gradients (deferred) within the same, or the step's table change
     (immediate) within 5e-2 of the deferred change: in immediate mode a ray's gather sees the
     updates of rays that scattered before it, which on this trained state moves the step's table
     change by about 2e-2 (rel-L2) from the deferred schedule's.
@@ -32,7 +33,7 @@ import ffn_native as fn
 GEOM = dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0)
 TOL = {  # loss rel, params, table, gradients on the device state, immediate table change
     "fp32": (1e-3, 1e-2, 1e-2, 1e-4, 5e-2),
-    "fp16": (2e-3, 3e-2, 1e-2, 5e-2, 5e-2),
+    "fp16": (1e-3, 1e-2, 1e-2, 1e-2, 5e-2),
 }
 
 
