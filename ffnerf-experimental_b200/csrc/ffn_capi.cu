@@ -32,10 +32,12 @@ struct ffn_ctx {
     uint32_t* occ_in = nullptr;
     uint32_t* occ_st = nullptr;
     float* grads = nullptr;      // [table_floats + Pw]
-    float* partials = nullptr;   // [max_grid * Pw]
+    float* partials = nullptr;   // [max_grid * groups * Pw]
     int* status = nullptr;       // device status word
     int max_grid = 0;
-    int rows = 0;
+    int rows = 0;                // samples per tile
+    int threads = 0;             // threads per block of the fused kernel (tiles side by side x rows)
+    int groups = 1;              // tiles side by side per block (one weight-gradient partial row each)
     int ctas_per_sm = 1;
     size_t smem = 0;
     void (*kernel)(StepArgs) = nullptr;
@@ -90,6 +92,8 @@ void bind_kernel(ffn_ctx* c) {
         c->kernel_staged = fused_step_tc_kernel<F, ND, true>;
         c->encoder = encode_stage_kernel<F>;
         c->rows = PL::ROWS;
+        c->threads = PL::THREADS;
+        c->groups = PL::GROUPS;
         c->smem = PL::BYTES;
         c->ctas_per_sm = PL::CTAS_PER_SM;
         return;
@@ -98,6 +102,8 @@ void bind_kernel(ffn_ctx* c) {
     c->kernel_staged = fused_step_kernel<F, ND, NC, ROWS, true>;
     c->encoder = encode_stage_f32_kernel<F>;
     c->rows = ROWS;
+    c->threads = ROWS;
+    c->groups = 1;
     c->smem = (size_t)Smem<F, ND, NC, ROWS>::floats(c->Pw) * sizeof(float);
     c->ctas_per_sm = 1;
 }
@@ -124,6 +130,14 @@ int check_config(const ffn_config* g, std::string* why) {
     if (g->G < 1 || g->G > 1024) { *why = "occupancy grid side must be 1..1024"; return FFN_E_CONFIG; }
     if (g->background < 0 || g->background > 2) { *why = "background must be 0 (black), 1 (white) or 2 (random)"; return FFN_E_CONFIG; }
     if (g->mlp_precision != 0 && g->mlp_precision != 1) { *why = "mlp_precision must be 0 (fp32) or 1 (fp16 tensor cores)"; return FFN_E_CONFIG; }
+    if (g->transfer_fmt != 0 && g->transfer_fmt != 32 && g->transfer_fmt != 16 && g->transfer_fmt != 8) {
+        *why = "transfer_fmt must be 32 (fp32), 16 (fp16) or 8 (fp8)";
+        return FFN_E_CONFIG;
+    }
+    if (g->mlp_precision == 1 && g->transfer_fmt != 0 && g->transfer_fmt != 32) {
+        *why = "the fp16 / fp8 transfer formats are reproduced by the fp32 MLP (mlp_precision 0) only";
+        return FFN_E_CONFIG;
+    }
     uint64_t expect = 0;
     for (int l = 0; l < FFN_N_LEVELS; ++l) {
         if (g->level_log2[l] < 1 || g->level_log2[l] > 24) { *why = "per-level table size must be 2^1..2^24"; return FFN_E_CONFIG; }
@@ -150,6 +164,7 @@ void fill_dev_config(ffn_ctx* c) {
     for (int i = 0; i < 3; ++i) { d.bmin[i] = g.box_min[i]; d.bmax[i] = g.box_max[i]; }
     d.rho_min = g.rho_min; d.rho_max = g.rho_max; d.dt_min = g.dt_min; d.dt_max = g.dt_max;
     d.t_near = g.t_near; d.t_far = g.t_far;
+    d.transfer = g.transfer_fmt ? g.transfer_fmt : 32;
 }
 
 StepArgs base_args(ffn_ctx* c, const void* rays, const void* targets, void* out, uint32_t n,
@@ -181,13 +196,20 @@ StepArgs base_args(ffn_ctx* c, const void* rays, const void* targets, void* out,
     return a;
 }
 
-int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* grid_out) {
+// Blocks for n_tiles tiles at c->groups tiles per block, at most max_grid.
+int fused_grid(const ffn_ctx* c, int n_tiles) {
+    const int blocks = (n_tiles + c->groups - 1) / c->groups;
+    return blocks < c->max_grid ? blocks : c->max_grid;
+}
+
+// Launches the fused kernel; *parts_out = weight-gradient partial rows it writes (blocks x groups).
+int launch_fused(ffn_ctx* c, const StepArgs& a, cudaStream_t st, int* parts_out) {
     const int rpt = c->rows / a.c.spr;
     const int n_tiles = (int)((a.n_rays + (uint32_t)rpt - 1) / (uint32_t)rpt);
-    const int grid = n_tiles < c->max_grid ? n_tiles : c->max_grid;
-    if (grid_out) *grid_out = grid;
+    const int grid = fused_grid(c, n_tiles);
+    if (parts_out) *parts_out = grid * c->groups;
     if (grid == 0) return FFN_OK;
-    c->kernel<<<grid, c->rows, c->smem, st>>>(a);
+    c->kernel<<<grid, c->threads, c->smem, st>>>(a);
     ++c->launches;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "fused step launch");
@@ -241,11 +263,11 @@ int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, v
         a.tdt_stage = c->tdt_stage;
         a.ray_stage = c->ray_stage;
         const int mtiles = (int)((m + (uint32_t)(c->rows / spr) - 1) / (uint32_t)(c->rows / spr));   // MLP-kernel tiles
-        const int grid = mtiles < c->max_grid ? mtiles : c->max_grid;
-        c->kernel_staged<<<grid, c->rows, c->smem, st>>>(a);
+        const int grid = fused_grid(c, mtiles);
+        c->kernel_staged<<<grid, c->threads, c->smem, st>>>(a);
         ++c->launches;
-        reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats,
-                                                            c->status);
+        reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid * c->groups, c->Pw,
+                                                            c->grads + c->table_floats, c->status);
         ++c->launches;
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(c, e, "split step launch");
@@ -316,7 +338,7 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
     struct { void** p; size_t n; } allocs[] = {
         {(void**)&c->params, Pb}, {(void**)&c->adam_m, Pb}, {(void**)&c->adam_v, Pb},
         {(void**)&c->table, Tb}, {(void**)&c->occ_in, Gb}, {(void**)&c->occ_st, Gb},
-        {(void**)&c->grads, Tb + Pb}, {(void**)&c->partials, (size_t)c->max_grid * Pb},
+        {(void**)&c->grads, Tb + Pb}, {(void**)&c->partials, (size_t)c->max_grid * c->groups * Pb},
         {(void**)&c->status, sizeof(int)}};
     for (auto& al : allocs) {
         if ((e = cudaMalloc(al.p, al.n)) != cudaSuccess) { ffn_destroy(c); return cuda_fail(nullptr, e, "device allocation"); }
@@ -324,7 +346,8 @@ int ffn_create(const ffn_config* cfg, int device, ffn_ctx** out) {
     }
     if (c->kernel_staged) {
         struct { void** p; size_t n; } st_allocs[] = {
-            {(void**)&c->x0_stage, (size_t)STAGE_SAMPLES * 16 * cfg->F * (cfg->mlp_precision == 1 ? 2 : 4)},
+            // fp32 rows (fp32 MLP) or the hi and lo fp16 operand tiles (tensor-core MLP): 4 B per feature
+            {(void**)&c->x0_stage, (size_t)STAGE_SAMPLES * 16 * cfg->F * 4},
             {(void**)&c->tdt_stage, (size_t)STAGE_SAMPLES * sizeof(float2)},
             {(void**)&c->pn_stage, (size_t)STAGE_SAMPLES * sizeof(float4)},
             {(void**)&c->ray_stage, (size_t)(STAGE_SAMPLES / 16) * sizeof(uint4)}};
@@ -419,9 +442,9 @@ int ffn_forward_backward(ffn_ctx* c, const void* rays, const void* targets, void
     if (c->kernel_staged) return forward_backward_staged(c, rays, targets, out, n, s, st);
     StepArgs a = base_args(c, rays, targets, out, n, s);
     a.do_train = 1;
-    int grid = 0;
-    if ((rc = launch_fused(c, a, st, &grid)) != FFN_OK) return rc;
-    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats,
+    int parts = 0;
+    if ((rc = launch_fused(c, a, st, &parts)) != FFN_OK) return rc;
+    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, parts, c->Pw, c->grads + c->table_floats,
                                                             c->status);
     ++c->launches;
     cudaError_t e = cudaGetLastError();
@@ -623,12 +646,11 @@ int ffn_mlp_bench(ffn_ctx* c, const void* tiles, int64_t n, void* stream) {
     StepArgs a = base_args(c, nullptr, nullptr, nullptr, (uint32_t)(n / c->cfg.spr), &s);
     a.do_train = 1;
     a.x0_stage = static_cast<const unsigned char*>(tiles);
-    const int64_t n_tiles = n / 128;
-    const int grid = (int)(n_tiles < c->max_grid ? n_tiles : c->max_grid);
-    kfn<<<grid, 128, PL::BYTES, st>>>(a);
+    const int grid = fused_grid(c, (int)(n / 128));
+    kfn<<<grid, PL::THREADS, PL::BYTES, st>>>(a);
     ++c->launches;
-    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid, c->Pw, c->grads + c->table_floats,
-                                                        c->status);
+    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid * PL::GROUPS, c->Pw,
+                                                        c->grads + c->table_floats, c->status);
     ++c->launches;
     e = cudaGetLastError();
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "MLP microbenchmark launch");
@@ -816,16 +838,24 @@ int ffn_dp_reduce_apply(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
     if (c->dp->mc_grads)
         ffn::dp_reduce_apply_nvls_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, c->dp->mc_grads, c->dp->mc_table,
                                                                   c->table, table4, total4, lc, epoch, c->status,
-                                                                  c->dp->done_counter);
+                                                                  c->dp->done_counter, c->dp->wait_limit);
     else
         ffn::dp_reduce_apply_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, table4, total4, lc, epoch, c->status,
-                                                             c->dp->done_counter);
+                                                             c->dp->done_counter, c->dp->wait_limit);
     ++c->launches;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "exchange launch");
     // every rank has read this rank's table gradients: clear them for the next step
     if ((e = cudaMemsetAsync(c->grads, 0, c->table_floats * sizeof(float), st)) != cudaSuccess)
         return cuda_fail(c, e, "gradient clear");
+    return FFN_OK;
+}
+
+int ffn_dp_set_wait_limit(ffn_ctx* c, uint32_t polls) {
+    if (!c) return FFN_E_CONFIG;
+    if (!c->dp) return fail(c, FFN_E_STATE, "ffn_dp_ipc_handles must be called first");
+    if (polls == 0) return fail(c, FFN_E_CONFIG, "the wait limit must be at least one poll");
+    c->dp->wait_limit = polls;
     return FFN_OK;
 }
 

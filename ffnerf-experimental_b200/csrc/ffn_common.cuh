@@ -9,6 +9,7 @@
 // fp32 code and are compared within tolerance.
 #pragma once
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "../../include/ffnerf.h"
@@ -60,7 +61,41 @@ struct DevConfig {
     float hash_lr_scale[L];
     float bmin[3], bmax[3];
     float rho_min, rho_max, dt_min, dt_max, t_near, t_far;
+    int transfer;   // format of the weight-gradient operands: 32 fp32, 16 fp16, 8 the reference's fp8
 };
+
+// The reference's transfer formats (ffnerf_OG.cl:85-156): the weight update reads the staged
+// activations and deltas as stored in the format.  fp16: saturate to +-65504 (non-finite to
+// +-65504), round to nearest even.  fp8 (e4m3-like minifloat): saturate to +-15.5 (non-finite to
+// +-15.5), flush |x| < 1e-8 and exponents below the bias to zero, 3 mantissa bits rounded to
+// nearest even (a carry bumps the exponent), exponents above 14 stored as 2^3 * 1.875.
+__device__ __forceinline__ float transfer_fp16(float x) {
+    if (!isfinite(x)) x = copysignf(65504.0f, x);
+    return __half2float(__float2half_rn(fminf(fmaxf(x, -65504.0f), 65504.0f)));
+}
+__device__ __forceinline__ float transfer_fp8(float x) {
+    x = isfinite(x) ? fminf(fmaxf(x, -15.5f), 15.5f) : copysignf(15.5f, x);
+    const bool neg = x < 0.0f;
+    const float ax = fabsf(x);
+    if (ax < 1.0e-8f) return neg ? -0.0f : 0.0f;
+    int e = 0;
+    const float m = frexpf(ax, &e);
+    int ef = e - 1 + 7;
+    if (ef <= 0) return neg ? -0.0f : 0.0f;
+    int mant;
+    if (ef > 14) {
+        ef = 10; mant = 7;
+    } else {
+        mant = (int)rintf(__fmul_rn(__fsub_rn(__fmul_rn(m, 2.0f), 1.0f), 8.0f));
+        if (mant >= 8) { mant = 0; ef += 1; }
+        if (ef > 14) { ef = 10; mant = 7; }
+    }
+    const float v = ldexpf(1.0f + (float)mant * 0.125f, ef - 7);
+    return neg ? -v : v;
+}
+__device__ __forceinline__ float transfer_q(float x, int fmt) {
+    return fmt == 16 ? transfer_fp16(x) : (fmt == 8 ? transfer_fp8(x) : x);
+}
 
 // ------------------------------------------------------------------------- integer RNG
 // hash_u32 / rand01 (ffnerf_OG.cl:293-311)
@@ -78,6 +113,15 @@ __device__ __forceinline__ float rand01(uint32_t* s) {
 // ------------------------------------------------------------------------- exact fp32 ops
 __device__ __forceinline__ float fm(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fa(float a, float b) { return __fadd_rn(a, b); }
+
+// Barrier over the threads of one 128-sample tile.  Kernels of at most 128 threads hold one tile:
+// the whole block.  The tensor-core kernel runs two tiles side by side in a 256-thread block, one
+// per 128-thread group, and each group synchronises on its own named barrier (1 + group), so the
+// groups never wait for each other.
+__device__ __forceinline__ void tile_sync() {
+    if (blockDim.x <= 128) __syncthreads();
+    else asm volatile("bar.sync %0, 128;" :: "r"(1 + (threadIdx.x >> 7)) : "memory");
+}
 __device__ __forceinline__ float fs(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float fd(float a, float b) { return __fdiv_rn(a, b); }
 __device__ __forceinline__ float fclamp(float x, float lo, float hi) { return fminf(fmaxf(x, lo), hi); }

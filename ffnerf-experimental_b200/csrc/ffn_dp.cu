@@ -19,14 +19,16 @@
 //   exit:  the last block of rank r to finish stores epoch into slot r of every rank's exit flags,
 //          then waits until all W exit slots reach epoch, so that no rank's next step reads a
 //          table or writes a gradient buffer that a peer is still reading or writing.
-// Every wait is bounded (DP_WAIT_LIMIT polls with a back-off); a wait that runs out sets status
-// bit 8 and the kernel skips its work, so no rank can hang the others.
+// Every wait is bounded (wait_limit polls of about 1 us each, DP_WAIT_LIMIT_DEFAULT unless the
+// caller set another with ffn_dp_set_wait_limit); a wait that runs out sets status bit 8 and the
+// kernel skips its work, so no rank can hang the others.  After a timeout the ranks' epochs no
+// longer agree: the exchange is not used again until the ranks re-attach.
 #include <cuda_runtime.h>
 
 namespace ffn {
 
 constexpr int DP_MAX_RANKS = 8;
-constexpr uint32_t DP_WAIT_LIMIT = 1u << 24;   // polls of ~1 us each (~16 s) before giving up
+constexpr uint32_t DP_WAIT_LIMIT_DEFAULT = 1u << 24;   // polls of ~1 us each (~16 s) before giving up
 
 struct DpPeers {
     float* grads[DP_MAX_RANKS];      // every rank's gradient buffer (this rank's included)
@@ -45,8 +47,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Waits until flags[first .. first + n) all reach epoch (wrap-safe compare).
-__device__ __forceinline__ bool dp_wait(const uint32_t* flags, int first, int n, uint32_t epoch) {
-    for (uint32_t it = 0; it < DP_WAIT_LIMIT; ++it) {
+__device__ __forceinline__ bool dp_wait(const uint32_t* flags, int first, int n, uint32_t epoch, uint32_t limit) {
+    for (uint32_t it = 0; it < limit; ++it) {
         bool all = true;
         for (int k = 0; k < n; ++k) all &= (int32_t)(ld_acquire_sys(flags + first + k) - epoch) >= 0;
         if (all) return true;
@@ -57,7 +59,7 @@ __device__ __forceinline__ bool dp_wait(const uint32_t* flags, int first, int n,
 
 __global__ void __launch_bounds__(256) dp_reduce_apply_kernel(const DpPeers P, uint32_t table4, uint32_t total4,
                                                               const LevelCoef lc, uint32_t epoch, int* status,
-                                                              unsigned int* done_counter) {
+                                                              unsigned int* done_counter, uint32_t wait_limit) {
     __shared__ int ok;
     const int W = P.world, r = P.rank;
     if (threadIdx.x == 0) {
@@ -65,7 +67,7 @@ __global__ void __launch_bounds__(256) dp_reduce_apply_kernel(const DpPeers P, u
             __threadfence_system();
             for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + r, epoch);
         }
-        ok = dp_wait(P.flags[r], 0, W, epoch) ? 1 : 0;
+        ok = dp_wait(P.flags[r], 0, W, epoch, wait_limit) ? 1 : 0;
         if (!ok) atomicOr(status, ST_DP_TIMEOUT);
     }
     __syncthreads();
@@ -106,7 +108,7 @@ __global__ void __launch_bounds__(256) dp_reduce_apply_kernel(const DpPeers P, u
             *done_counter = 0u;
             __threadfence_system();
             for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + W + r, epoch);
-            if (!dp_wait(P.flags[r], W, W, epoch)) atomicOr(status, ST_DP_TIMEOUT);
+            if (!dp_wait(P.flags[r], W, W, epoch, wait_limit)) atomicOr(status, ST_DP_TIMEOUT);
         }
     }
 }
@@ -129,7 +131,8 @@ __device__ __forceinline__ void mc_st(float* mc, float4 v) {
 __global__ void __launch_bounds__(256) dp_reduce_apply_nvls_kernel(const DpPeers P, float* mc_grads, float* mc_table,
                                                                    const float* __restrict__ table, uint32_t table4,
                                                                    uint32_t total4, const LevelCoef lc, uint32_t epoch,
-                                                                   int* status, unsigned int* done_counter) {
+                                                                   int* status, unsigned int* done_counter,
+                                                                   uint32_t wait_limit) {
     __shared__ int ok;
     const int W = P.world, r = P.rank;
     if (threadIdx.x == 0) {
@@ -137,7 +140,7 @@ __global__ void __launch_bounds__(256) dp_reduce_apply_nvls_kernel(const DpPeers
             __threadfence_system();
             for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + r, epoch);
         }
-        ok = dp_wait(P.flags[r], 0, W, epoch) ? 1 : 0;
+        ok = dp_wait(P.flags[r], 0, W, epoch, wait_limit) ? 1 : 0;
         if (!ok) atomicOr(status, ST_DP_TIMEOUT);
     }
     __syncthreads();
@@ -166,7 +169,7 @@ __global__ void __launch_bounds__(256) dp_reduce_apply_nvls_kernel(const DpPeers
             *done_counter = 0u;
             __threadfence_system();
             for (int p = 0; p < W; ++p) st_release_sys(P.flags[p] + W + r, epoch);
-            if (!dp_wait(P.flags[r], W, W, epoch)) atomicOr(status, ST_DP_TIMEOUT);
+            if (!dp_wait(P.flags[r], W, W, epoch, wait_limit)) atomicOr(status, ST_DP_TIMEOUT);
         }
     }
 }
@@ -183,6 +186,7 @@ struct DpState {
     unsigned int* done_counter = nullptr;
     bool opened[ffn::DP_MAX_RANKS] = {};    // which peer mappings this rank opened (and closes)
     uint32_t epoch = 0;
+    uint32_t wait_limit = ffn::DP_WAIT_LIMIT_DEFAULT;   // polls per cross-rank wait (ffn_dp_set_wait_limit)
 };
 
 }  // namespace

@@ -9,9 +9,9 @@
 // device in the middle of the caller's frame).  Such callers hold the model's buffers themselves
 // and pass them in; ffn_create, which allocates, is not for them.
 //
-// The one piece of memory the step needs beyond its inputs and outputs is the per-CTA weight-
-// gradient partial sums (one row of Pw floats per CTA of the fused kernel, summed in a fixed
-// order by reduce_partials).  Here it lives in a file-scope __device__ array of
+// The one piece of memory the step needs beyond its inputs and outputs is the weight-gradient
+// partial sums (one row of Pw floats per tile group of the fused kernel, summed in a fixed order
+// by reduce_partials).  Here it lives in a file-scope __device__ array of
 // FFN_NOALLOC_SCRATCH_BYTES (24 MiB) that every GPU which loads this library holds until the
 // process exits.  Its first 256 bytes hold a status word for callers that pass no status output.
 #include <mutex>
@@ -28,17 +28,18 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH
 
 struct NoallocKernel {
     void (*fn)(StepArgs) = nullptr;
-    int rows = 0;
+    int rows = 0;          // samples per tile
+    int threads = 0;       // threads per block
+    int groups = 1;        // tiles side by side per block (one partial row each)
     int ctas_per_sm = 1;
     size_t smem = 0;
 };
 
 struct NoallocDevice {
-    bool ready = false;
-    int rc = FFN_OK;
-    char err[160] = {0};
+    bool ready = false;                 // set-up succeeded; a failed set-up is retried by the next call
     unsigned char* scratch = nullptr;   // device address of g_noalloc_scratch on this device
     int sms = 0;
+    int max_smem = 0;                   // opt-in dynamic shared memory per block
 };
 
 std::mutex g_noalloc_mu;
@@ -51,11 +52,14 @@ NoallocKernel noalloc_kernel_for(int mlp_precision, int Pw) {
         using PL = TcPlan<F, ND>;
         k.fn = fused_step_tc_kernel<F, ND>;
         k.rows = PL::ROWS;
+        k.threads = PL::THREADS;
+        k.groups = PL::GROUPS;
         k.smem = PL::BYTES;
         k.ctas_per_sm = PL::CTAS_PER_SM;
     } else {
         k.fn = fused_step_kernel<F, ND, NC, ROWS>;
         k.rows = ROWS;
+        k.threads = ROWS;
         k.smem = (size_t)Smem<F, ND, NC, ROWS>::floats(Pw) * sizeof(float);
         k.ctas_per_sm = 1;
     }
@@ -73,43 +77,46 @@ bool noalloc_pick(int F, int ND, int NC, int mlp_precision, NoallocKernel* k) {
     return false;
 }
 
-int noalloc_setup_fail(NoallocDevice& d, int code, const char* what, cudaError_t e) {
-    d.rc = code;
-    snprintf(d.err, sizeof(d.err), "%s%s%s", what, e != cudaSuccess ? ": " : "", e != cudaSuccess ? cudaGetErrorString(e) : "");
-    d.ready = true;
+// A failed set-up is not remembered: the device stays "not ready" and the next call tries again
+// (a transient error, such as a context that was still being created, does not disable the entry
+// point for the rest of the process).
+int noalloc_setup_fail(char* err, size_t err_size, int code, const char* what, cudaError_t e) {
+    snprintf(err, err_size, "%s%s%s", what, e != cudaSuccess ? ": " : "", e != cudaSuccess ? cudaGetErrorString(e) : "");
     return code;
 }
 
 // Once per device, with that device current: resolve the scratch array's device address and
-// raise the dynamic shared-memory limit of every compiled fused kernel.  Runs inside the first
-// call on each device.
-int noalloc_setup(int dev, NoallocDevice** out) {
+// raise the dynamic shared-memory limit of every compiled fused kernel that fits the device.  Runs
+// inside the first successful call on each device.
+int noalloc_setup(int dev, NoallocDevice** out, char* err, size_t err_size) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     NoallocDevice& d = g_noalloc_dev[dev];
     *out = &d;
-    if (d.ready) return d.rc;
+    if (d.ready) return FFN_OK;
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return noalloc_setup_fail(d, FFN_E_CUDA, "scratch symbol address", e);
-    if ((reinterpret_cast<uintptr_t>(p) & 255u) != 0) return noalloc_setup_fail(d, FFN_E_CUDA, "scratch not 256-byte aligned", cudaSuccess);
-    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-        return noalloc_setup_fail(d, FFN_E_CUDA, "device query", e);
-    int max_smem = 0;
+    if (e != cudaSuccess) return noalloc_setup_fail(err, err_size, FFN_E_CUDA, "scratch symbol address", e);
+    if ((reinterpret_cast<uintptr_t>(p) & 255u) != 0)
+        return noalloc_setup_fail(err, err_size, FFN_E_CUDA, "scratch not 256-byte aligned", cudaSuccess);
+    int sms = 0, max_smem = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return noalloc_setup_fail(err, err_size, FFN_E_CUDA, "device query", e);
     if ((e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
-        return noalloc_setup_fail(d, FFN_E_CUDA, "device query", e);
+        return noalloc_setup_fail(err, err_size, FFN_E_CUDA, "device query", e);
     const int combos[4][2] = {{2, 1}, {4, 1}, {2, 2}, {4, 2}};
     for (const auto& fd : combos) {
         for (int prec = 0; prec < 2; ++prec) {
             NoallocKernel k;
             noalloc_pick(fd[0], fd[1], 2, prec, &k);
-            if ((int)k.smem > max_smem) continue;   // rejected per call
+            if ((int)k.smem > max_smem) continue;   // such a kernel is refused per call (FFN_E_CONFIG)
             if ((e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)k.smem)) != cudaSuccess)
-                return noalloc_setup_fail(d, FFN_E_CUDA, "shared-memory attribute", e);
+                return noalloc_setup_fail(err, err_size, FFN_E_CUDA, "shared-memory attribute", e);
         }
     }
     d.scratch = static_cast<unsigned char*>(p);
+    d.sms = sms;
+    d.max_smem = max_smem;
     d.ready = true;
-    d.rc = FFN_OK;
     return FFN_OK;
 }
 
@@ -142,19 +149,29 @@ extern "C" int ffn_forward_backward_noalloc(const ffn_config* cfg, const float* 
     if (e != cudaSuccess) return cuda_fail(nullptr, e, "current device");
     if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(nullptr, FFN_E_CONFIG, "device index beyond 63");
     NoallocDevice* d = nullptr;
-    if (noalloc_setup(dev, &d) != FFN_OK) return fail(nullptr, d->rc, d->err);
+    char setup_err[160] = {0};
+    const int setup_rc = noalloc_setup(dev, &d, setup_err, sizeof(setup_err));
+    if (setup_rc != FFN_OK) return fail(nullptr, setup_rc, setup_err);
+    if (k.smem > (size_t)d->max_smem) {
+        char msg[160];
+        snprintf(msg, sizeof(msg), "the fused kernel for this configuration needs %zu bytes of shared memory per block; "
+                 "this device allows %d", k.smem, d->max_smem);
+        return fail(nullptr, FFN_E_CONFIG, msg);
+    }
 
     const ParamLayout lo = make_param_layout(cfg->F, cfg->ND, cfg->NC);
     const int spr = s->spr ? (int)s->spr : cfg->spr;
     const int rpt = k.rows / spr;
     const int n_tiles = (int)((n + (uint32_t)rpt - 1) / (uint32_t)rpt);
     const int max_grid = d->sms * k.ctas_per_sm;
-    const int grid = n_tiles < max_grid ? n_tiles : max_grid;
-    const size_t need = NOALLOC_HEADER_BYTES + (size_t)grid * lo.total * sizeof(float);
+    const int blocks = (n_tiles + k.groups - 1) / k.groups;
+    const int grid = blocks < max_grid ? blocks : max_grid;
+    const int parts = grid * k.groups;
+    const size_t need = NOALLOC_HEADER_BYTES + (size_t)parts * lo.total * sizeof(float);
     if (need > NOALLOC_SCRATCH_BYTES) {
         char msg[200];
-        snprintf(msg, sizeof(msg), "this call needs %zu bytes of weight-gradient scratch (%d CTAs x %d floats); "
-                 "the static scratch holds %zu", need, grid, lo.total, NOALLOC_SCRATCH_BYTES);
+        snprintf(msg, sizeof(msg), "this call needs %zu bytes of weight-gradient scratch (%d partial rows x %d floats); "
+                 "the static scratch holds %zu", need, parts, lo.total, NOALLOC_SCRATCH_BYTES);
         return fail(nullptr, FFN_E_CAPACITY, msg);
     }
     uint64_t entries = 0;
@@ -173,6 +190,7 @@ extern "C" int ffn_forward_backward_noalloc(const ffn_config* cfg, const float* 
     for (int i = 0; i < 3; ++i) { dc.bmin[i] = cfg->box_min[i]; dc.bmax[i] = cfg->box_max[i]; }
     dc.rho_min = cfg->rho_min; dc.rho_max = cfg->rho_max; dc.dt_min = cfg->dt_min; dc.dt_max = cfg->dt_max;
     dc.t_near = cfg->t_near; dc.t_far = cfg->t_far;
+    dc.transfer = cfg->transfer_fmt ? cfg->transfer_fmt : 32;
     a.lo = lo;
     a.params = params;
     a.table = table;
@@ -203,9 +221,9 @@ extern "C" int ffn_forward_backward_noalloc(const ffn_config* cfg, const float* 
     if ((e = cudaMemsetAsync(grads, 0, (table_floats + (size_t)lo.total) * sizeof(float), st)) != cudaSuccess)
         return cuda_fail(nullptr, e, "gradient clear");
     if ((e = cudaMemsetAsync(a.status, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail(nullptr, e, "status clear");
-    k.fn<<<grid, k.rows, k.smem, st>>>(a);
+    k.fn<<<grid, k.threads, k.smem, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "fused step launch");
-    reduce_partials<<<(lo.total + 255) / 256, 256, 0, st>>>(partials, grid, lo.total, grads + table_floats);
+    reduce_partials<<<(lo.total + 255) / 256, 256, 0, st>>>(partials, parts, lo.total, grads + table_floats, a.status);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(nullptr, e, "gradient reduction launch");
     return FFN_OK;
 }

@@ -83,11 +83,12 @@ __device__ __forceinline__ void dense_bwd(const float (&d)[OUT], const float* W,
 }
 
 // Weight gradient of one layer over the tile: gW[o][i] += sum_r D[r][o] * A[r][i] and
-// gb[o] += sum_r D[r][o]  (update_layer_tile_adam_i32's reduction, weight_update.cl:260-314).
-// D may have a zero pad column (OUT = 3 is read as 4).
+// gb[o] += sum_r D[r][o]  (update_layer_tile_adam_i32's reduction, weight_update.cl:260-314), with
+// D and A read in the transfer format `tq` (32: as they are; 16 / 8: quantised as the reference's
+// weight update reads its staged buffers).  D may have a zero pad column (OUT = 3 is read as 4).
 template <int ROWS>
 __device__ __forceinline__ void coop_wgrad(const float* D, int ldd, int OUT, const float* A, int lda,
-                                           int IN, float* gW, float* gb) {
+                                           int IN, float* gW, float* gb, int tq) {
     const int nib = IN >> 2, nob = (OUT + 3) >> 2;
     for (int b = threadIdx.x; b < nib * nob; b += ROWS) {
         const int ob = b / nib, ib = b - ob * nib;
@@ -100,8 +101,12 @@ __device__ __forceinline__ void coop_wgrad(const float* D, int ldd, int OUT, con
         for (int r = 0; r < ROWS; ++r) {
             const float4 dv = *reinterpret_cast<const float4*>(D + r * ldd + ob * 4);
             const float4 av = *reinterpret_cast<const float4*>(A + r * lda + ib * 4);
-            const float dd[4] = {dv.x, dv.y, dv.z, dv.w};
-            const float aa[4] = {av.x, av.y, av.z, av.w};
+            float dd[4] = {dv.x, dv.y, dv.z, dv.w};
+            float aa[4] = {av.x, av.y, av.z, av.w};
+            if (tq != 32) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) { dd[i] = transfer_q(dd[i], tq); aa[i] = transfer_q(aa[i], tq); }
+            }
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -120,7 +125,7 @@ __device__ __forceinline__ void coop_wgrad(const float* D, int ldd, int OUT, con
     }
     for (int o = threadIdx.x; o < OUT; o += ROWS) {
         float s = 0.f;
-        for (int r = 0; r < ROWS; ++r) s += D[r * ldd + o];
+        for (int r = 0; r < ROWS; ++r) s += transfer_q(D[r * ldd + o], tq);
         gb[o] += s;
     }
 }
@@ -351,7 +356,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
         float* gpart = part;
         const ParamLayout& lo = a.lo;
         // color head
-        coop_wgrad<ROWS>(sDC, 4, C_OUT, sHc + (NC - 1) * ROWS * LDH, LDH, M, gpart + lo.off[P_WC_OUT], gpart + lo.off[P_BC_OUT]);
+        coop_wgrad<ROWS>(sDC, 4, C_OUT, sHc + (NC - 1) * ROWS * LDH, LDH, M, gpart + lo.off[P_WC_OUT], gpart + lo.off[P_BC_OUT], a.c.transfer);
         __syncthreads();
         {
             float dv[C_OUT] = {dcout[0], dcout[1], dcout[2]};
@@ -362,7 +367,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
         for (int l = NC - 1; l >= 1; --l) {
             __syncthreads();
             coop_wgrad<ROWS>(sHc + l * ROWS * LDH, LDH, M, sHc + (l - 1) * ROWS * LDH, LDH, M,
-                             gpart + lo.off[P_WC_IN + l], gpart + lo.off[P_BC_0 + l]);
+                             gpart + lo.off[P_WC_IN + l], gpart + lo.off[P_BC_0 + l], a.c.transfer);
             __syncthreads();
             float dv[M];
             load_row<M>(dv, sHc + l * ROWS * LDH + tid * LDH);
@@ -370,7 +375,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
             dense_bwd<M, M, true>(dv, sW + lo.off[P_WC_IN + l], row, row);
         }
         __syncthreads();
-        coop_wgrad<ROWS>(sHc, LDH, M, sAc, LDC, C_IN, gpart + lo.off[P_WC_IN], gpart + lo.off[P_BC_0]);
+        coop_wgrad<ROWS>(sHc, LDH, M, sAc, LDC, C_IN, gpart + lo.off[P_WC_IN], gpart + lo.off[P_BC_0], a.c.transfer);
         __syncthreads();
         {
             // delta at the density output: color contribution through Wc_in[:, :16] (:2016-2020)
@@ -390,7 +395,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
             }
         }
         __syncthreads();
-        coop_wgrad<ROWS>(sAc, LDC, D_OUT, sHd + (ND - 1) * ROWS * LDH, LDH, M, gpart + lo.off[P_WD_OUT], gpart + lo.off[P_BD_OUT]);
+        coop_wgrad<ROWS>(sAc, LDC, D_OUT, sHd + (ND - 1) * ROWS * LDH, LDH, M, gpart + lo.off[P_WD_OUT], gpart + lo.off[P_BD_OUT], a.c.transfer);
         __syncthreads();
         {
             float dv[D_OUT];
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
         for (int l = ND - 1; l >= 1; --l) {
             __syncthreads();
             coop_wgrad<ROWS>(sHd + l * ROWS * LDH, LDH, M, sHd + (l - 1) * ROWS * LDH, LDH, M,
-                             gpart + lo.off[P_WD_IN + l], gpart + lo.off[P_BD_0 + l]);
+                             gpart + lo.off[P_WD_IN + l], gpart + lo.off[P_BD_0 + l], a.c.transfer);
             __syncthreads();
             float dv[M];
             load_row<M>(dv, sHd + l * ROWS * LDH + tid * LDH);
@@ -410,7 +415,7 @@ __global__ void __launch_bounds__(ROWS, 1) fused_step_kernel(const StepArgs a) {
             dense_bwd<M, M, true>(dv, sW + lo.off[P_WD_IN + l], row, row);
         }
         __syncthreads();
-        coop_wgrad<ROWS>(sHd, LDH, M, sA0, LDA0, LPOS, gpart + lo.off[P_WD_IN], gpart + lo.off[P_BD_0]);
+        coop_wgrad<ROWS>(sHd, LDH, M, sA0, LDA0, LPOS, gpart + lo.off[P_WD_IN], gpart + lo.off[P_BD_0], a.c.transfer);
         __syncthreads();
         // ------------------------------------------------ hash-grid gradient (:2090-2173)
         {

@@ -34,7 +34,7 @@ class FfnConfig(C.Structure):
                 ("rho_min", C.c_float), ("rho_max", C.c_float), ("dt_min", C.c_float),
                 ("dt_max", C.c_float), ("t_near", C.c_float), ("t_far", C.c_float),
                 ("adam_beta1", C.c_float), ("adam_beta2", C.c_float), ("adam_eps", C.c_float),
-                ("table_adam_eps", C.c_float), ("mlp_precision", C.c_int32)]
+                ("table_adam_eps", C.c_float), ("mlp_precision", C.c_int32), ("transfer_fmt", C.c_int32)]
 
 
 class FfnStep(C.Structure):
@@ -47,7 +47,7 @@ STEP_TABLE_IMMEDIATE = 1
 STEP_TABLE_APPLIED = 2
 STATUS_NONFINITE, STATUS_TC_TIMEOUT, STATUS_DP_TIMEOUT = 1, 4, 8   # ffn_status bits
 STAGE_SAMPLES = 1 << 20   # samples per group of the split tensor-core step (ffn_capi.cu)
-ABI_VERSION = 4          # include/ffnerf.h FFN_ABI_VERSION
+ABI_VERSION = 5          # include/ffnerf.h FFN_ABI_VERSION
 
 
 _VP = C.c_void_p
@@ -78,6 +78,7 @@ _SIGS = {
     "ffn_dp_ipc_handles": (C.c_int, [_VP, _VP]),
     "ffn_dp_attach": (C.c_int, [_VP, C.c_int, C.c_int, _VP]),
     "ffn_dp_reduce_apply": (C.c_int, [_VP, C.POINTER(FfnStep), _VP]),
+    "ffn_dp_set_wait_limit": (C.c_int, [_VP, C.c_uint32]),
     "ffn_bind_external": (C.c_int, [_VP, C.c_int, _VP, C.c_size_t]),
     "ffn_dp_attach_multicast": (C.c_int, [_VP, _VP, _VP]),
     "ffn_kernel_launches": (C.c_uint64, [_VP]),
@@ -118,10 +119,12 @@ def load_library(path: Path | None = None):
 
 
 MLP_PRECISIONS = {"fp32": 0, "fp16": 1}
+TRANSFER_FORMATS = {"fp32": 32, "fp16": 16, "fp8": 8}   # ffn_config.transfer_fmt
 
 
 def make_ffn_config(geom: dict, table_optimizer: int = 0, max_rays: int = 0, adam_beta1=0.9,
-                    adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15, mlp_precision: str = "fp32") -> FfnConfig:
+                    adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15, mlp_precision: str = "fp32",
+                    transfer_fmt: str = "fp32") -> FfnConfig:
     c = FfnConfig()
     for k in ("F", "ND", "NC", "spr", "G", "background"):
         setattr(c, k, int(geom[k]))
@@ -138,6 +141,7 @@ def make_ffn_config(geom: dict, table_optimizer: int = 0, max_rays: int = 0, ada
         setattr(c, k, float(geom[k]))
     c.adam_beta1, c.adam_beta2, c.adam_eps, c.table_adam_eps = adam_beta1, adam_beta2, adam_eps, table_adam_eps
     c.mlp_precision = MLP_PRECISIONS[mlp_precision]
+    c.transfer_fmt = TRANSFER_FORMATS[transfer_fmt]
     return c
 
 
@@ -171,13 +175,14 @@ class Context:
     """One native context (parameters, optimizer state, table, occupancy grids, gradients)."""
 
     def __init__(self, geom: dict, device: int = 0, table_optimizer: int = 0, max_rays: int = 0,
-                 adam_beta1=0.9, adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15, mlp_precision: str = "fp32"):
+                 adam_beta1=0.9, adam_beta2=0.999, adam_eps=1e-6, table_adam_eps=1e-15, mlp_precision: str = "fp32",
+                 transfer_fmt: str = "fp32"):
         self.lib = load_library()
         self.geom = dict(geom)
         self.device = int(device)
         self.mlp_precision = mlp_precision
         self.cfg = make_ffn_config(geom, table_optimizer, max_rays, adam_beta1, adam_beta2, adam_eps, table_adam_eps,
-                                   mlp_precision)
+                                   mlp_precision, transfer_fmt)
         h = _VP()
         rc = self.lib.ffn_create(C.byref(self.cfg), self.device, C.byref(h))
         if rc != FFN_OK:
@@ -282,6 +287,10 @@ class Context:
     def dp_reduce_apply(self, step: FfnStep, stream=None):
         self._check(self.lib.ffn_dp_reduce_apply(self.h, C.byref(step), self._stream(stream)), "ffn_dp_reduce_apply")
 
+    def dp_set_wait_limit(self, polls: int):
+        """Polls (~1 us each) per cross-rank wait of the exchange before it sets STATUS_DP_TIMEOUT."""
+        self._check(self.lib.ffn_dp_set_wait_limit(self.h, int(polls)), "ffn_dp_set_wait_limit")
+
     def render(self, rays, out, n_rays: int, step: FfnStep, stream=None):
         self._check(self.lib.ffn_render(self.h, _ptr(rays), _ptr(out), int(n_rays), C.byref(step),
                                         self._stream(stream)), "ffn_render")
@@ -309,13 +318,29 @@ class Context:
         self._check(self.lib.ffn_hash_encode_f16(self.h, _ptr(table16), _ptr(pts), _ptr(enc16), int(n),
                                                  self._stream(stream)), "ffn_hash_encode_f16")
 
+    def x0_tile_bytes(self, n: int) -> int:
+        """Bytes of the packed operand tiles for n rows: an fp16 hi tile and an fp16 lo tile per
+        128 rows of 16F features (n * 16F * 4)."""
+        return int(n) * 16 * int(self.cfg.F) * 4
+
+    def _check_tiles(self, x16, tiles, n: int):
+        need = self.x0_tile_bytes(n)
+        have = tiles.numel() * tiles.element_size()
+        if have < need:
+            raise ValueError(f"tiles holds {have} bytes; {n} rows need {need} (hi and lo fp16 tiles)")
+        if x16 is not None and x16.numel() * x16.element_size() < int(n) * 16 * int(self.cfg.F) * 2:
+            raise ValueError(f"x16 holds fewer than {n} rows of 16F fp16 features")
+
     def pack_x0(self, x16, tiles, n: int, stream=None):
-        """Packs fp16 rows x16 [n, 16F] (n a multiple of 128) into the MLP kernels' operand tiles."""
+        """Packs fp16 rows x16 [n, 16F] (n a multiple of 128) into the MLP kernels' operand tiles
+        (x0_tile_bytes(n) bytes)."""
+        self._check_tiles(x16, tiles, n)
         self._check(self.lib.ffn_pack_x0(self.h, _ptr(x16), _ptr(tiles), int(n), self._stream(stream)), "ffn_pack_x0")
 
     def mlp_bench(self, tiles, n: int, stream=None):
         """The MLP microbenchmark over packed inputs: gradients of sum 0.5 (rgb - 0.5)^2 added to the
         MLP part of BUF_GRADS (view direction (0.36, 0.48, 0.8), sh multiplier 1)."""
+        self._check_tiles(None, tiles, n)
         self._check(self.lib.ffn_mlp_bench(self.h, _ptr(tiles), int(n), self._stream(stream)), "ffn_mlp_bench")
 
     def hash_encode_bwd_f16(self, grad16, pts, denc, n: int, stream=None):

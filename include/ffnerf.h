@@ -38,8 +38,9 @@ extern "C" {
 #endif
 
 #define FFN_N_LEVELS 16
-#define FFN_ABI_VERSION 4   /* 2: ffn_step_scalars.flags; 3: batch/exchange entry points;
-                                   4: fp16-table hash and MLP microbenchmark entry points */
+#define FFN_ABI_VERSION 5   /* 2: ffn_step_scalars.flags; 3: batch/exchange entry points;
+                                   4: fp16-table hash and MLP microbenchmark entry points;
+                                   5: ffn_dp_set_wait_limit, ffn_config.transfer_fmt */
 
 enum {
     FFN_OK = 0,
@@ -82,6 +83,11 @@ typedef struct ffn_config {
     float table_adam_eps;
     int32_t mlp_precision;   /* 0: fp32 on the CUDA cores (reference-exact arithmetic),
                                 1: fp16 operands / fp32 accumulation on the tensor cores (tcgen05) */
+    int32_t transfer_fmt;    /* the reference's TRANSFER_FMT (ffnerf_OG.cl:85-156): the format in which
+                                the weight update reads the step's activations and deltas --
+                                32 (or 0) fp32, 16 fp16 (saturating, round to nearest even), 8 the
+                                reference's e4m3-like fp8 (saturating at +-15.5).  16 and 8 need
+                                mlp_precision 0 (the tensor-core MLP keeps its own operand formats). */
 } ffn_config;
 
 typedef struct ffn_step_scalars {
@@ -168,7 +174,8 @@ int ffn_hash_encode_bwd_f16(ffn_ctx* ctx, void* grad16, const float* pts, const 
                             void* stream);
 /* The MLP microbenchmark (no reference counterpart; the MLP half of the "fused MLP + Adam"
  * microbenchmark).  ffn_pack_x0 packs row-major fp16 inputs x16 [n][16*F] into the tensor-core
- * operand tiles (tiles: n*16*F*2 bytes, n a multiple of 128).  ffn_mlp_bench runs the density and
+ * operand tiles (tiles: n*16*F*4 bytes -- per 128 rows an fp16 hi tile and an fp16 lo tile -- n a
+ * multiple of 128).  ffn_mlp_bench runs the density and
  * colour MLPs forward and backward over those inputs on the tensor cores (tensor-core MLP, F=2,
  * ND=1 contexts), with the view direction fixed at (0.36, 0.48, 0.8), sh multiplier 1 and the loss
  * sum_k 0.5 (rgb_k - 0.5)^2 per sample, and adds the summed MLP weight and bias gradients to the MLP
@@ -196,6 +203,11 @@ int ffn_status(ffn_ctx* ctx, uint32_t* status);
 int ffn_dp_ipc_handles(ffn_ctx* ctx, void* handles_out);
 int ffn_dp_attach(ffn_ctx* ctx, int rank, int world, const void* handles);
 int ffn_dp_reduce_apply(ffn_ctx* ctx, const ffn_step_scalars* s, void* stream);
+/* Polls (about 1 us each) that each cross-rank wait of ffn_dp_reduce_apply makes before it gives up
+ * and sets status bit 8; default 2^24 (about 16 s).  Call after ffn_dp_ipc_handles.  No reference
+ * counterpart (the reference has no multi-device path); it lets a caller bound how long a rank
+ * waits for a peer that stopped calling the exchange. */
+int ffn_dp_set_wait_limit(ffn_ctx* ctx, uint32_t polls);
 /* NVSwitch (NVLS) variant of the exchange.  ffn_bind_external moves the context's table or
  * gradient buffer (FFN_BUF_TABLE / FFN_BUF_GRADS) into caller-owned device memory of at least the
  * same size -- here, memory bound to a multicast object on every rank -- copying the contents; the

@@ -147,3 +147,79 @@ def test_fused_exchange_matches_nccl(mode):
         assert st == "ok", res
         assert res["table"] < 1e-4 and res["params"] < 1e-4, res
         assert res["grads_clear"] and res["same_table"] and res["status"] == (0, 0), res
+
+
+def _timeout_worker(rank, world, port, q):
+    """Both ranks stay alive; in the second exchange rank 1 withholds its call, so rank 0's waits
+    for rank 1's flags run out (short limit), the kernel sets STATUS_DP_TIMEOUT and returns."""
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"   # no NVLink multicast anywhere in this test
+        for p in (ROOT / "ffnerf-experimental_b200", ROOT / "tests"):
+            sys.path.insert(0, str(p))
+        import datetime
+        import time
+        import torch.distributed as dist
+        import ffn_native as fn
+        from ffn_config import make_geometry
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        g = make_geometry(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0)
+        ctx = fn.Context(g, device=rank, mlp_precision="fp32")
+        handles = ctx.dp_ipc_handles()
+        allh = [None] * world
+        dist.all_gather_object(allh, handles)
+        ctx.dp_attach(rank, world, allh)
+        ctx.dp_set_wait_limit(200_000)          # ~0.2 s per wait instead of ~16 s
+        step = fn.make_step(lr_f=1e-2, lr_t=1e-3, rng_u32=1)
+        ctx.dp_reduce_apply(step)               # every rank calls: completes
+        torch.cuda.synchronize()
+        st1 = ctx.status()
+        dist.barrier()
+        t0 = time.time()
+        if rank == 0:
+            ctx.dp_reduce_apply(step)           # rank 1 does not call this one
+            torch.cuda.synchronize()
+        elapsed = time.time() - t0
+        st2 = ctx.status()
+        dist.barrier()                          # rank 1 waits on the host until rank 0 is back
+        ctx.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok", dict(st1=st1, st2=st2, elapsed=elapsed)))
+    except Exception as exc:
+        import traceback
+        q.put((rank, "err", f"{exc}\n{traceback.format_exc()}"))
+
+
+def test_exchange_wait_runs_out():
+    """The exchange's cross-rank waits are bounded: with a short limit, a rank whose peer withholds
+    its call gets STATUS_DP_TIMEOUT within a second and both ranks tear down cleanly (peer form,
+    NVLS off: no rank's memory is bound to a multicast object)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import ffn_native as fn
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_timeout_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, st, res = q.get(timeout=180)
+            results[rank] = (st, res)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank, (st, res) in results.items():
+        assert st == "ok", res
+        assert res["st1"] == 0, res
+    assert results[0][1]["st2"] & fn.STATUS_DP_TIMEOUT, results[0]
+    assert results[0][1]["elapsed"] < 5.0, results[0]
+    assert results[1][1]["st2"] == 0, results[1]
+    assert all(p.exitcode == 0 for p in procs)
