@@ -9,12 +9,15 @@ streams/events.  Checkpoints use the reference's NPZ layout byte for byte (float
 as int32 bit patterns), plus a few extra keys the reference loader ignores.
 
 Differences from the reference behaviour (each deliberate):
-  * the hash-table SGD update is applied after the whole batch (every sample reads the table as
-    it was at the start of the step) instead of racing in-kernel adds;
+  * the hash-table SGD update races in-kernel like the reference's (``table_update="immediate"``,
+    the default on one GPU) but in one legal order of that race: in the split tensor-core step every
+    gather of a step precedes its scatter; ``table_update="deferred"`` (data-parallel runs, the Adam
+    table) applies it after the whole batch;
   * ``setup_buffers`` keeps the device state when the batch shape changes (the reference
     re-uploads its last host snapshot then, ffnerf_tools.py:1380-1385);
-  * ``transfer_fmt`` is recorded in checkpoints but activations never leave the chip, so it does
-    not change the numerics.
+  * activations never leave the chip; ``transfer_fmt`` ("fp32", "fp16", "fp8") still selects the
+    format in which the weight update reads them, quantised as the reference's staging buffers are
+    (fp32 MLP; the tensor-core MLP runs with "fp32" only).
 """
 from __future__ import annotations
 
@@ -574,6 +577,8 @@ class Nerf:
         self.ND = int(nd if nd is not None else ND)
         self.NC = int(nc if nc is not None else NC)
         self._set_transfer(transfer_fmt)
+        if not load_id:
+            self._check_transfer()
         self.table_size_entries = int(table_size_entries)
         self.f_per_level = int(f_per_level)
         self.level_log2 = _level_log2_for(self.table_size_entries, level_log2)
@@ -624,6 +629,13 @@ class Nerf:
         return cls(ctx, queue, lib, lib, lib, lib, ffnerf_kernel_name, decay_kernel_name, wu_kernel_name,
                    training_dir, model_id, layers, edges, transfer_fmt, table_size_entries, f_per_level, occ,
                    load_id, rng_seed, background=background, **kw)
+
+    def _check_transfer(self):
+        """The fp16 / fp8 transfer formats quantise the weight-update operands the reference's way
+        (ffnerf_OG.cl:85-156) in the fp32 MLP; the tensor-core MLP has its own operand formats."""
+        if self.mlp_precision == "fp16" and self.transfer_fmt != "fp32":
+            raise ValueError(f"transfer_fmt={self.transfer_fmt!r} needs mlp_precision='fp32' (the tensor-core MLP "
+                             "runs with transfer_fmt='fp32' only)")
 
     def _set_transfer(self, transfer_fmt: str):
         if transfer_fmt not in ("fp32", "fp16", "fp8"):
@@ -769,11 +781,12 @@ class Nerf:
         self.batch_rays = self.num_rays
         self.B = self.num_rays * self.samples_per_ray if self.do_train else None
         if self.native is None:
+            self._check_transfer()
             opt = {"sgd": 0, "adam": 1}[self.table_optimizer]
             self.native = ffn_native.Context(self.geometry(self.samples_per_ray), device=self.ctx.device.index,
                                              table_optimizer=opt, adam_beta1=float(self.ADAM_BETA1),
                                              adam_beta2=float(self.ADAM_BETA2), adam_eps=float(self.ADAM_EPS),
-                                             mlp_precision=self.mlp_precision)
+                                             mlp_precision=self.mlp_precision, transfer_fmt=self.transfer_fmt)
             self._push_params_to_device()
         self.buf = {"native": self.native}
 

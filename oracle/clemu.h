@@ -23,6 +23,9 @@ namespace clemu {
 typedef unsigned int uint;
 typedef unsigned long ulong;
 typedef unsigned char uchar;
+typedef _Float16 half;     // cl_khr_fp16 storage type (the fp16 transfer format)
+inline half convert_half_rte(float x) { return (half)x; }   // IEEE round to nearest even
+inline float convert_float(half h) { return (float)h; }
 
 // ----------------------------------------------------------------- vector types
 struct float3 { float x, y, z, w_; };

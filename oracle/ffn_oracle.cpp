@@ -391,6 +391,43 @@ struct Stage {
     float dc_out[C_OUT];
 };
 
+// Transfer formats of the staged activations and deltas (ffnerf_OG.cl:85-156, read back by
+// weight_update.cl's tload): the weight update sees each staged value as stored in the format.
+// fp16: saturate to +-65504 (non-finite -> +-65504), round to nearest even.
+inline float transfer_fp16(float x) {
+    if (!std::isfinite(x)) x = std::copysign(65504.0f, x);
+    x = fclampf(x, -65504.0f, 65504.0f);
+    return (float)(_Float16)x;
+}
+// fp8: the reference's e4m3-like minifloat -- saturate to +-15.5 (non-finite -> +-15.5), flush
+// |x| < 1e-8 and exponents below the bias to zero, 3 mantissa bits rounded to nearest even (a
+// carry bumps the exponent), exponents above 14 stored as 2^3 * 1.875.
+inline float transfer_fp8(float x) {
+    x = std::isfinite(x) ? fclampf(x, -15.5f, 15.5f) : std::copysign(15.5f, x);
+    const bool neg = x < 0.0f;
+    const float ax = std::fabs(x);
+    if (ax < 1.0e-8f) return neg ? -0.0f : 0.0f;
+    int e = 0;
+    const float m = std::frexp(ax, &e);
+    int ef = e - 1 + 7;
+    if (ef <= 0) return neg ? -0.0f : 0.0f;
+    int mant;
+    if (ef > 14) {
+        ef = 10; mant = 7;
+    } else {
+        mant = (int)std::rint((m * 2.0f - 1.0f) * 8.0f);
+        if (mant >= 8) { mant = 0; ef += 1; }
+        if (ef > 14) { ef = 10; mant = 7; }
+    }
+    const float v = std::ldexp(1.0f + (float)mant * (1.0f / 8.0f), ef - 7);
+    return neg ? -v : v;
+}
+void quantize_stage(Stage& s, int fmt) {
+    if (fmt != 16 && fmt != 8) return;
+    float* f = reinterpret_cast<float*>(&s);
+    for (size_t i = 0; i < sizeof(Stage) / sizeof(float); ++i) f[i] = fmt == 16 ? transfer_fp16(f[i]) : transfer_fp8(f[i]);
+}
+
 }  // namespace
 
 // ============================================================================ public API
@@ -850,7 +887,10 @@ extern "C" int32_t orc_forward_backward(const orc_config* c, const orc_step* st,
             }
         }
         if (!stage.empty())
-            for (int lid = 0; lid < WG; ++lid) stage[(size_t)r * WG + lid] = lane_st[lid];
+            for (int lid = 0; lid < WG; ++lid) {
+                stage[(size_t)r * WG + lid] = lane_st[lid];
+                quantize_stage(stage[(size_t)r * WG + lid], c->transfer_fmt);
+            }
     }
 
     // ---------------------------------------------------- weight gradients (weight_update.cl:210-314)
@@ -931,6 +971,20 @@ extern "C" void orc_mlp_adam(const orc_config* c, float* params, const float* gr
         bool color = (i >= P_WC_IN && i <= P_WC_OUT) || (i >= P_BC_0 && i <= P_BC_OUT);
         int o = lo.off[i];
         orc_adam(params + o, grad + o, m + o, v + o, lo.size[i], color ? lr_c : lr_t, b1, b2, eps);
+    }
+}
+
+// Opt-in Adam for the hash table (no reference counterpart: the reference trains the table with
+// the in-kernel SGD step, ffnerf_OG.cl:2155-2168).  The reference's Adam update
+// (weight_update.cl:177-201, orc_adam above) per level, with step size lr_t * 2^(-0.1 l) -- the
+// reference's per-level SGD roll-off (ffnerf_OG.cl:2110-2111) applied to Adam's step.
+extern "C" void orc_table_adam(const orc_config* c, float* table, const float* tg, float* m, float* v,
+                               float lr_t, float b1, float b2, float eps) {
+    for (int lvl = 0; lvl < L; ++lvl) {
+        const float lr = lr_t * c->hash_lr_scale[lvl];
+        const int64_t b = (int64_t)c->level_offset[lvl] * c->F;
+        const int64_t n = ((int64_t)1 << c->level_log2[lvl]) * c->F;
+        orc_adam(table + b, tg + b, m + b, v + b, n, lr, b1, b2, eps);
     }
 }
 

@@ -36,7 +36,8 @@ typedef struct {
                              1: sequential (one legal Hogwild schedule: rays in order,
                                 updates applied immediately)                        */
     int32_t tilek;        /* weight-update K chunk (reference TILEK)                */
-    int32_t pad0;
+    int32_t transfer_fmt; /* staged activations / deltas read by the weight update:
+                             32 fp32, 16 fp16, 8 the reference's e4m3-like fp8     */
     uint32_t level_log2[ORC_N_LEVELS];   /* log2 entries per level                 */
     uint32_t level_offset[ORC_N_LEVELS]; /* first entry of each level              */
     int32_t  level_res[ORC_N_LEVELS];    /* grid resolution per level              */
@@ -85,6 +86,9 @@ void orc_adam(float* p, const float* g, float* m, float* v, int64_t n,
 void orc_mlp_adam(const orc_config* cfg, float* params, const float* grad, float* m, float* v,
                   float lr_t, float color_rel_lr, float b1, float b2, float eps);
 void orc_table_apply(const orc_config* cfg, float* table, const float* table_grad, float lr_f);
+/* Opt-in table Adam: orc_adam per level with step lr_t * 2^(-0.1 l). */
+void orc_table_adam(const orc_config* cfg, float* table, const float* table_grad, float* m, float* v,
+                    float lr_t, float b1, float b2, float eps);
 void orc_decay(uint32_t* occ_in, uint32_t* occ_st, uint32_t n_words, uint32_t decay_q24,
                uint32_t seed);
 

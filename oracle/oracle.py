@@ -35,7 +35,7 @@ def build_oracle(cxx: str = "g++") -> Path:
 class OrcConfig(C.Structure):
     _fields_ = [("F", C.c_int32), ("ND", C.c_int32), ("NC", C.c_int32), ("spr", C.c_int32),
                 ("G", C.c_int32), ("background", C.c_int32), ("math_mode", C.c_int32),
-                ("table_mode", C.c_int32), ("tilek", C.c_int32), ("pad0", C.c_int32),
+                ("table_mode", C.c_int32), ("tilek", C.c_int32), ("transfer_fmt", C.c_int32),
                 ("level_log2", C.c_uint32 * N_LEVELS), ("level_offset", C.c_uint32 * N_LEVELS),
                 ("level_res", C.c_int32 * N_LEVELS), ("hash_lr_scale", C.c_float * N_LEVELS),
                 ("box_min", C.c_float * 4), ("box_max", C.c_float * 4),
@@ -59,14 +59,15 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
 
 
-def make_orc_config(geom: dict, math_mode: int = 0, table_mode: int = 0, tilek: int = 236) -> OrcConfig:
+def make_orc_config(geom: dict, math_mode: int = 0, table_mode: int = 0, tilek: int = 236,
+                    transfer_fmt: int = 32) -> OrcConfig:
     """Builds the C config from a geometry dict (keys as produced by the product's config helper:
     F, ND, NC, spr, G, background, level_log2, level_offset, level_res, hash_lr_scale, box_min,
     box_max, rho_min, rho_max, dt_min, dt_max, t_near, t_far)."""
     c = OrcConfig()
     for k in ("F", "ND", "NC", "spr", "G", "background"):
         setattr(c, k, int(geom[k]))
-    c.math_mode, c.table_mode, c.tilek = math_mode, table_mode, tilek
+    c.math_mode, c.table_mode, c.tilek, c.transfer_fmt = math_mode, table_mode, tilek, transfer_fmt
     for i in range(N_LEVELS):
         c.level_log2[i] = int(geom["level_log2"][i])
         c.level_offset[i] = int(geom["level_offset"][i])
@@ -91,6 +92,7 @@ class Oracle:
         L.orc_adam.argtypes = [C.c_void_p] * 4 + [C.c_int64] + [C.c_float] * 4
         L.orc_mlp_adam.argtypes = [C.POINTER(OrcConfig)] + [C.c_void_p] * 4 + [C.c_float] * 5
         L.orc_table_apply.argtypes = [C.POINTER(OrcConfig), C.c_void_p, C.c_void_p, C.c_float]
+        L.orc_table_adam.argtypes = [C.POINTER(OrcConfig)] + [C.c_void_p] * 4 + [C.c_float] * 4
         L.orc_decay.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32]
         L.orc_hash_fwd.argtypes = [C.POINTER(OrcConfig), C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
         L.orc_hash_bwd.argtypes = [C.POINTER(OrcConfig), C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
@@ -129,6 +131,9 @@ class Oracle:
 
     def table_apply(self, cfg, table, table_grad, lr_f):
         self.lib.orc_table_apply(C.byref(cfg), _p(table), _p(table_grad), lr_f)
+
+    def table_adam(self, cfg, table, table_grad, m, v, lr_t, b1, b2, eps):
+        self.lib.orc_table_adam(C.byref(cfg), _p(table), _p(table_grad), _p(m), _p(v), lr_t, b1, b2, eps)
 
     def decay(self, occ_in, occ_st, decay_q24, seed):
         self.lib.orc_decay(_p(occ_in), _p(occ_st), occ_in.size, decay_q24, seed)

@@ -38,6 +38,9 @@ VARIANTS = {
     "default": dict(F=4, ND=2, NC=2, log2T=None, rmax=None),
     "cfg1": dict(F=2, ND=1, NC=2, log2T=14, rmax=512.0),
     "cfg3": dict(F=2, ND=1, NC=2, log2T=19, rmax=2048.0),
+    # the reference's fp16 and fp8 transfer formats of the staged activations / deltas
+    "cfg1_t16": dict(F=2, ND=1, NC=2, log2T=14, rmax=512.0, transfer=16),
+    "cfg1_t8": dict(F=2, ND=1, NC=2, log2T=14, rmax=512.0, transfer=8),
 }
 
 
@@ -132,6 +135,7 @@ TRAIN_LAUNCHER = r"""
 extern "C" void ffnref_train(const ffnref_train_args* a) {
     using namespace clemu;
     using namespace clemu::k_train;
+    auto T = [](float* p) { return reinterpret_cast<TRANSFER_T*>(p); };   // scratch in the transfer format
     const float3 bmin = f3_make(a->box_min[0], a->box_min[1], a->box_min[2]);
     const float3 bmax = f3_make(a->box_max[0], a->box_max[1], a->box_max[2]);
     const Ray* rays = (const Ray*)a->rays;
@@ -146,10 +150,10 @@ extern "C" void ffnref_train(const ffnref_train_args* a) {
                               a->W[4], a->W[5], a->W[6], a->W[7], a->W[8],
                               a->b[4], a->b[5], a->b[6], a->b[7], a->b[8],
                               a->table, rays, tg,
-                              a->deltas[0], a->deltas[1], a->deltas[2], a->deltas[3], a->deltas[4],
-                              a->deltas[5], a->deltas[6], a->deltas[7], a->deltas[8],
-                              a->acts[0], a->acts[1], a->acts[2], a->acts[3], a->acts[4],
-                              a->acts[5], a->acts[6], a->acts[7], a->acts[8],
+                              T(a->deltas[0]), T(a->deltas[1]), T(a->deltas[2]), T(a->deltas[3]), T(a->deltas[4]),
+                              T(a->deltas[5]), T(a->deltas[6]), T(a->deltas[7]), T(a->deltas[8]),
+                              T(a->acts[0]), T(a->acts[1]), T(a->acts[2]), T(a->acts[3]), T(a->acts[4]),
+                              T(a->acts[5]), T(a->acts[6]), T(a->acts[7]), T(a->acts[8]),
                               out, a->lr, a->num_rays, a->spr, a->do_train, a->sh_mult,
                               a->occ_in, a->occ_st, bmin, bmax, a->G, a->rho_min, a->rho_max,
                               a->dt_min, a->dt_max, a->t_near, a->t_far, a->seed, a->occ_strength);
@@ -167,6 +171,7 @@ WU_LAUNCHER = r"""
 extern "C" void ffnref_weight_update(const ffnref_wu_args* a) {
     using namespace clemu;
     using namespace clemu::k_wu;
+    auto T = [](float* p) { return reinterpret_cast<TRANSFER_T*>(p); };   // scratch in the transfer format
     const int max_in = a->M > 32 ? (a->M > a->L ? a->M : a->L) : (32 > a->L ? 32 : a->L);
     const int ngx = (max_in + INT - 1) / INT;
     const int ngy = (a->M + OUTT - 1) / OUTT;
@@ -181,10 +186,10 @@ extern "C" void ffnref_weight_update(const ffnref_wu_args* a) {
                                     a->vW[0], a->vW[1], a->vW[2], a->vW[3], a->vW[4], a->vW[5], a->vW[6], a->vW[7], a->vW[8],
                                     a->mb[0], a->mb[1], a->mb[2], a->mb[3], a->mb[4], a->mb[5], a->mb[6], a->mb[7], a->mb[8],
                                     a->vb[0], a->vb[1], a->vb[2], a->vb[3], a->vb[4], a->vb[5], a->vb[6], a->vb[7], a->vb[8],
-                                    a->deltas[0], a->deltas[1], a->deltas[2], a->deltas[3], a->deltas[4],
-                                    a->deltas[5], a->deltas[6], a->deltas[7], a->deltas[8],
-                                    a->acts[0], a->acts[1], a->acts[2], a->acts[3], a->acts[4],
-                                    a->acts[5], a->acts[6], a->acts[7], a->acts[8],
+                                    T(a->deltas[0]), T(a->deltas[1]), T(a->deltas[2]), T(a->deltas[3]), T(a->deltas[4]),
+                                    T(a->deltas[5]), T(a->deltas[6]), T(a->deltas[7]), T(a->deltas[8]),
+                                    T(a->acts[0]), T(a->acts[1]), T(a->acts[2]), T(a->acts[3]), T(a->acts[4]),
+                                    T(a->acts[5]), T(a->acts[6]), T(a->acts[7]), T(a->acts[8]),
                                     a->B, a->L, a->M, a->lr_t, a->color_rel_lr, a->beta1, a->beta2, a->eps);
             });
 }
@@ -221,8 +226,9 @@ def build_variant(ref_dir: Path, name: str, cxx: str = "g++", quiet: bool = True
     for fn, text in units.items():
         (out_dir / fn).write_text(text, encoding="utf-8")
     # Same -D options the reference host passes (ffnerf_tools.py:618-637), BACKGROUND_COLOR=2 as
-    # selected by the trainer for SfM scenes (run_ffnerf_OG.py:1082), fp32 transfer.
-    defs = [f"-DND={v['ND']}", f"-DNC={v['NC']}", "-DNDMAX=3", "-DNCMAX=4", "-DTRANSFER_FMT=32",
+    # selected by the trainer for SfM scenes (run_ffnerf_OG.py:1082), fp32 transfer unless the
+    # variant names another.
+    defs = [f"-DND={v['ND']}", f"-DNC={v['NC']}", "-DNDMAX=3", "-DNCMAX=4", f"-DTRANSFER_FMT={v.get('transfer', 32)}",
             "-DWG_X=16", "-DWG_Y=16", "-DREG_X=1", "-DREG_Y=1", "-DTILEK=236",
             "-DBACKGROUND_COLOR=2", f"-DF_PER_LEVEL={v['F']}"]
     so = OUT_ROOT / f"libffnref_{name}.so"

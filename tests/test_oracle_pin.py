@@ -5,7 +5,9 @@ occ_nibble_decay_write_both_q24 unmodified on CPU fibers (oracle/ref_build.py). 
 library's exp/pow (math mode 1), one OS thread (work-groups in ray order) and the oracle's
 sequential table mode (the Hogwild schedule that order produces), every output is bit-identical:
 ray colours, the table after the in-kernel SGD adds, occupancy proposals, and all MLP parameters
-and Adam moments after the weight update.  Skipped where the reference library was not built."""
+and Adam moments after the weight update -- also with the reference's fp16 and fp8 transfer
+formats, where the weight update reads the staged activations and deltas quantised.  Skipped where
+the reference library was not built."""
 import numpy as np
 import pytest
 
@@ -18,7 +20,11 @@ VARIANTS = {
     "default": dict(F=4, ND=2, NC=2, spr=64, G=32, log2_entries=list(REFERENCE_LEVEL_LOG2), rmax=1024.0,
                     box_min=(-3, -3, -3), box_max=(3, 3, 3)),
     "cfg3": dict(F=2, ND=1, NC=2, spr=64, G=128, log2_entries=19, rmax=2048.0),
+    # the reference's fp16 / fp8 transfer formats of the activations and deltas the weight update reads
+    "cfg1_t16": dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0),
+    "cfg1_t8": dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0),
 }
+TRANSFER = {"cfg1_t16": 16, "cfg1_t8": 8}
 
 
 def _split(blob, geom):
@@ -57,7 +63,7 @@ def test_oracle_matches_compiled_reference(oracle, variant, occ_strength, sh_mul
     v_ = {k: np.zeros(v.size, np.float32) for k, v in params.items()}
     ref.weight_update(params, m, v_, scr, n * g["spr"], 1e-3, 0.15, 0.9, 0.999, 1e-6)
     # oracle: libm math, sequential table updates
-    cfg = make_orc_config(g, math_mode=1, table_mode=1)
+    cfg = make_orc_config(g, math_mode=1, table_mode=1, transfer_fmt=TRANSFER.get(variant, 32))
     tab_o = table0.copy()
     out_o = np.zeros((n, 4), np.float32)
     occ_st_o = occ0.copy()
