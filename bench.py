@@ -10,8 +10,12 @@ occupied, proposals on, maintenance every 32 steps), on the seeded 56-camera 450
 blob scene (synthetic data: rays through random pixels, targets rendered analytically and
 quantised to 8 bits).  Every step is the full training step: forward, backward, MLP Adam and the
 hash-table SGD update -- on one GPU applied inside the fused kernel as the reference does
-(Hogwild), on N GPUs as a gradient all-reduce (NCCL) followed by the SGD pass.  L2 is flushed
-between timed steps; ``l2_warm`` repeats the steps back to back without the flush.
+(Hogwild), on N GPUs by the fused exchange kernel (cross-rank gradient sum, table SGD of each
+rank's shard and broadcast of the new table over NVLink peer memory, or NVSwitch multicast from 4
+ranks up).  The MLPs run on the tensor cores (--mlp fp16, the default): fp16 operand pairs with
+fp32 accumulation (a compensated hi/lo forward, fp16 backward operands); the table is fp32.
+--mlp fp32 runs the CUDA-core fp32 MLP instead.  L2 is flushed between timed steps; ``l2_warm``
+repeats the steps back to back without the flush.
 
 For N > 1 run under torchrun (one process per GPU, NCCL).  Rank 0 prints one JSON line:
   value       -- samples/s of the whole job, inputs resident on the device, CUDA events, max
@@ -21,8 +25,9 @@ For N > 1 run under torchrun (one process per GPU, NCCL).  Rank 0 prints one JSO
   roofline    -- the fused forward/backward kernel: algorithmic bytes per launch / its average
                  duration (CUDA events on its stream) against the measured HBM copy bandwidth;
   cpu_baseline-- the reference kernels compiled for the CPU (oracle/_ref) on the host cores.
-``--impl reference`` times the reference's own CPU implementation of the step instead (rank 0
-only) and prints the same metric.
+``--impl reference`` times the reference's own kernels compiled for the CPU (oracle/_ref) on the
+same workload -- the same batches, occupancy grid, initial parameters and schedules -- on all host
+cores (rank 0 only) and prints the same metric.
 """
 from __future__ import annotations
 
@@ -45,7 +50,7 @@ METRIC = "train samples/s (fwd+bwd+Adam)"
 WORKLOADS = {
     "cfg3": dict(rays=16384, spr=64, F=2, ND=1, NC=2, log2T=19, rmax=2048.0, G=128, n_cams=56, W=800, H=450,
                  maint=32, desc="cfg3: 16384 rays x 64 samples (2^20 samples/step) split by ray across GPUs; "
-                                "hash L=16 F=2 T=2^19 fp32 replicated, Rmax 2048; MLP 32-64-16 / 32-64-64-3 fp32; "
+                                "hash L=16 F=2 T=2^19 fp32 replicated, Rmax 2048; MLP 32-64-16 / 32-64-64-3; "
                                 "occupancy 128^3 ~5% occupied; 56-camera 450x800 synthetic blob scene"),
     "cfg2": dict(rays=512, spr=64, F=2, ND=1, NC=2, log2T=19, rmax=2048.0, G=128, n_cams=56, W=800, H=450,
                  maint=16, desc="cfg2: 512 rays x 64 samples; hash L=16 F=2 T=2^19, Rmax 2048; occupancy 128^3, "
@@ -107,7 +112,7 @@ def run_mlp_micro(args, wl, dev, st, gen, timed) -> dict:
     ctx.tensor(fn.BUF_PARAMS).copy_(torch.from_numpy(blob))
     n = wl["n"]
     x16 = torch.randn((n, 32), device=dev, generator=gen).half()
-    tiles = torch.empty(n * 32 * 2, dtype=torch.uint8, device=dev)
+    tiles = torch.empty(ctx.x0_tile_bytes(n), dtype=torch.uint8, device=dev)
     ctx.pack_x0(x16, tiles, n, stream=st)
     step = lambda: ctx.mlp_bench(tiles, n, stream=st)           # noqa: E731
     for _ in range(args.warmup):
@@ -385,34 +390,100 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+# ------------------------------------------------------------------------------ shared inputs
+BATCH_POOL = 4          # global batches drawn once and cycled through the steps
+BASE_LR = 5e-5 * 8      # base learning rate of the timed steps (schedules.lr_schedule)
+START_STEP = 3000       # steps_trained before the first step: the schedules' steady state
+
+
+def build_inputs(wl: dict, n_glob: int, rank: int, world: int, device):
+    """The workload's synthetic batches and occupancy grid, the same on both arms: BATCH_POOL global
+    batches of n_glob rays through random pixels of the seeded scene's cameras (targets rendered by
+    quadrature, quantised to 8 bits), this rank's contiguous slice of each; the scene's occupancy
+    grid with ~5% of sub-cells occupied."""
+    import torch
+    from synthetic_scene import BlobScene, cameras_ring, cameras_sphere, intrinsics, pixel_rays
+    scene = BlobScene(0)
+    cams = cameras_ring(wl["n_cams"], 2.5, 0) if wl["n_cams"] > 8 else cameras_sphere(wl["n_cams"], 2.0, 0)
+    K = intrinsics(wl["W"], wl["H"], 50.0)
+    n_loc = n_glob // world
+    rng = np.random.default_rng(1234)
+    pool_rays, pool_tg = [], []
+    for _ in range(BATCH_POOL):
+        ci = rng.integers(0, cams.shape[0], n_glob)
+        u = rng.integers(0, wl["W"], n_glob)
+        v = rng.integers(0, wl["H"], n_glob)
+        rays = np.zeros((n_glob, 8), np.float32)
+        for c in np.unique(ci):
+            sel = ci == c
+            rays[sel] = pixel_rays(cams[c], K, u[sel], v[sel])
+        rays_t = torch.from_numpy(rays).to(device)
+        rgb = scene.render_torch(rays_t, n_quad=192)
+        tg = torch.zeros((n_glob, 4), device=device)
+        tg[:, :3] = torch.round(rgb * 255.0) / 255.0
+        sl = slice(rank * n_loc, (rank + 1) * n_loc)
+        pool_rays.append(rays_t[sl].contiguous())
+        pool_tg.append(tg[sl].contiguous())
+    return pool_rays, pool_tg, scene.occupancy_grid_torch(wl["G"], device)
+
+
+def reference_init(g: dict, seed: int = 777):
+    """Fresh parameters with the reference's draws in the reference's order (Nerf._init_fresh,
+    ffnerf_tools.py:836-898), as the public host class makes them for our arm: table U(-1e-4, 1e-4),
+    weights N(0, 0.01) for heads of <= 16 outputs else He N(0, sqrt(2/fan_in)), biases 0 except
+    bd_out[0] = -2.  Returns (param blob, table, the generator -- it draws the per-step seeds next)."""
+    from ffn_config import param_layout, param_shapes
+    rng = np.random.default_rng(seed)
+    lay, total = param_layout(g["F"], g["ND"], g["NC"])
+    shapes = param_shapes(g["F"], g["ND"], g["NC"])
+    table = rng.uniform(-1e-4, 1e-4, size=g["table_entries"] * g["F"]).astype(np.float32)
+    blob = np.zeros(total, np.float32)
+    for name in ("Wd_in", "Wd_01", "Wd_12", "Wd_out", "Wc_in", "Wc_01", "Wc_12", "Wc_23", "Wc_out"):
+        if name not in shapes:
+            continue
+        sh = shapes[name]
+        std = 0.01 if sh[0] <= 16 else np.sqrt(2.0 / int(sh[1]))
+        off, size = lay[name]
+        blob[off:off + size] = rng.normal(0.0, std, size=sh).astype(np.float32).reshape(-1)
+    blob[lay["bd_out"][0]] = -2.0
+    return blob, table, rng
+
+
 # ------------------------------------------------------------------------------ reference arm
-def run_reference_arm(args, wl) -> dict:
+def run_reference_arm(args, wl, n_rays: int | None = None, steps: int | None = None, warmup: int | None = None) -> dict:
     """The reference's own kernels, compiled for the CPU from their sources (oracle/_ref), timed on
-    all host cores; the oracle port stands in when that build is absent."""
+    all host cores on the same workload as our arm: the same batches (n_rays of each, default the
+    whole global batch), occupancy grid, initial parameters, per-step seeds and schedules, and the
+    reference's step order (fused kernel, occupancy decay every 32nd step, weight update + Adam).
+    The oracle port stands in when the compiled reference is absent."""
+    import torch
     sys.path.insert(0, str(ROOT / "oracle"))
-    sys.path.insert(0, str(ROOT / "tests"))
     import oracle as orc
+    import schedules as sch
     from ffn_config import make_geometry, param_layout, param_shapes
     g = make_geometry(F=wl["F"], ND=wl["ND"], NC=wl["NC"], spr=wl["spr"], G=wl["G"], log2_entries=wl["log2T"],
-                      rmax=wl["rmax"])
+                      rmax=wl["rmax"], dt_min=2.0 / 8192, dt_max=12.8 / wl["spr"] / 6 * 2.0)
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     cores = os.cpu_count() or 1
-    n_rays = min(1024, wl["rays"])            # bounded sample of the batch per step
-    rng = np.random.default_rng(0)
-    from synthetic_scene import BlobScene, cameras_ring, intrinsics, random_batch
-    scene = BlobScene(0)
-    cams = cameras_ring(wl["n_cams"], 2.5, 0)
-    K = intrinsics(wl["W"], wl["H"], 50.0)
-    rays, tg = random_batch(scene, cams, K, wl["W"], wl["H"], n_rays, 1, n_quad=96)
+    torch.set_num_threads(cores)
+    n_glob, spr = wl["rays"], wl["spr"]
+    n_rays = n_glob if n_rays is None else min(n_rays, n_glob)
+    pool_rays, pool_tg, occ_grid = build_inputs(wl, n_glob, 0, 1, "cpu")
+    rays_pool = [r[:n_rays].numpy().copy() for r in pool_rays]
+    tg_pool = [t[:n_rays].numpy().copy() for t in pool_tg]
+    blob, table, rng = reference_init(g)
+    occ_in, occ_st = occ_grid.copy(), occ_grid.copy()
     lay, total = param_layout(g["F"], g["ND"], g["NC"])
-    blob = (rng.normal(0, 0.1, total)).astype(np.float32)
-    table = rng.uniform(-1e-4, 1e-4, g["table_entries"] * g["F"]).astype(np.float32)
-    occ = np.full(g["G"] ** 3, 0xEEEEEEEE, np.uint32)
     variant = {"cfg3": "cfg3", "cfg2": "cfg3", "cfg1": "cfg1"}[args.workload]
     kind = "reference"
     try:
         ref = orc.RefKernels(variant)
     except (FileNotFoundError, OSError):
         ref, kind = None, "port"
+    lmbda = sch.lr_lambda(1e-4, n_glob, spr)
+    b1, b2 = np.float32(0.9), np.float32(0.999)
+    state = {"t": START_STEP}
     out = np.zeros((n_rays, 4), np.float32)
     if ref is not None:
         shapes = param_shapes(g["F"], g["ND"], g["NC"])
@@ -420,11 +491,21 @@ def run_reference_arm(args, wl) -> dict:
                   for n, (o, s) in lay.items()}
         m = {k: np.zeros(v.size, np.float32) for k, v in params.items()}
         v = {k: np.zeros(v.size, np.float32) for k, v in params.items()}
-        scr = ref.alloc_scratch(n_rays * g["spr"])
+        scr = ref.alloc_scratch(n_rays * spr)
+        table_i = table.view(np.int32)
 
         def step(i):
-            ref.train(params, table.view(np.int32), rays, tg, out, scr, occ, occ.copy(), g, 1e-3, 1.0, 1.0, i, True, cores)
-            ref.weight_update(params, m, v, scr, n_rays * g["spr"], 1e-3, 1.0, 0.9, 0.999, 1e-6, cores)
+            lr_f = sch.lr_schedule(state["t"], BASE_LR, lmbda, n_glob, spr)
+            seed = int(np.uint32(rng.integers(0, 2**32, dtype=np.uint32)))
+            state["t"] += 1
+            t = np.float32(state["t"])
+            lr_t = float(np.float32(lr_f) * np.sqrt(1.0 - b2 ** t) / (1.0 - b1 ** t))
+            b = i % BATCH_POOL
+            ref.train(params, table_i, rays_pool[b], tg_pool[b], out, scr, occ_in, occ_st, g, float(lr_f), 1.0, 1.0,
+                      seed, True, cores)
+            if state["t"] % 32 == 0:
+                ref.decay(occ_in, occ_st, 15099494, seed)
+            ref.weight_update(params, m, v, scr, n_rays * spr, lr_t, 1.0, 0.9, 0.999, 1e-6, cores)
     else:
         o_ = orc.Oracle()
         cfg = orc.make_orc_config(g)
@@ -433,35 +514,49 @@ def run_reference_arm(args, wl) -> dict:
         cores = 1
 
         def step(i):
+            lr_f = sch.lr_schedule(state["t"], BASE_LR, lmbda, n_glob, spr)
+            seed = int(np.uint32(rng.integers(0, 2**32, dtype=np.uint32)))
+            state["t"] += 1
+            t = np.float32(state["t"])
+            lr_t = np.float32(np.float32(lr_f) * np.sqrt(1.0 - b2 ** t) / (1.0 - b1 ** t))
+            b = i % BATCH_POOL
             tgr[:] = 0
-            o_.forward_backward(cfg, orc.OrcStep(1e-3, 1.0, 1.0, i, 1, 0), blob, table, occ, occ.copy(), rays, tg, out, tgr, mg)
-            o_.mlp_adam(cfg, blob, mg, m, v, 1e-3, 1.0, 0.9, 0.999, 1e-6)
-            o_.table_apply(cfg, table, tgr, 1e-3)
-    for i in range(args.warmup):
+            o_.forward_backward(cfg, orc.OrcStep(lr_f, 1.0, 1.0, seed, 1, 0), blob, table, occ_in, occ_st,
+                                rays_pool[b], tg_pool[b], out, tgr, mg)
+            if state["t"] % 32 == 0:
+                o_.decay(occ_in, occ_st, 15099494, seed)
+            o_.mlp_adam(cfg, blob, mg, m, v, lr_t, 1.0, b1, b2, np.float32(1e-6))
+            o_.table_apply(cfg, table, tgr, lr_f)
+    for i in range(warmup):
         step(i)
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        step(args.warmup + i)
+    for i in range(steps):
+        step(warmup + i)
     dt = time.perf_counter() - t0
-    samples = n_rays * g["spr"] * args.steps
+    samples = n_rays * spr * steps
     val = samples / dt
-    sample_desc = (f"{n_rays} rays x {g['spr']} samples per step ({n_rays * g['spr']} of the workload's "
-                   f"{wl['rays'] * wl['spr']}), fused step + weight update + Adam")
-    return {"metric": METRIC, "value": val, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+    same = n_rays == n_glob
+    sample_desc = (f"{'the whole global batch' if same else 'a bounded sample'}: {n_rays} rays x {spr} samples per "
+                   f"step ({n_rays * spr} of the workload's {n_glob * spr}), {steps} timed steps after {warmup}; "
+                   f"fused step + occupancy decay + weight update + Adam on the workload's batches, occupancy "
+                   f"grid, initial parameters and schedules")
+    return {"metric": METRIC, "value": val, "unit": "samples/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warmup, "ms_per_step": dt / steps * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference", "config": {"workload": wl["desc"], "global_batch_rays": wl["rays"]},
+            "impl": "reference", "config": {"workload": wl["desc"], "global_batch_rays": n_glob, "samples_per_ray": spr,
+                                            "samples_per_step": n_glob * spr, "rays_timed_per_step": n_rays},
             "cpu_baseline": {"value": val, "unit": "samples/s", "cores": cores, "kind": kind, "sample": sample_desc},
             "e2e": {"value": val, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def cpu_baseline_sample(wl) -> dict:
-    """A bounded run (~10-20 s) of the reference kernels compiled for the CPU."""
+def cpu_baseline_sample(args, wl) -> dict:
+    """A bounded run (~10-20 s) of the reference kernels compiled for the CPU: the whole global
+    batch, 3 timed steps after 1."""
     class A:
-        steps, warmup, gpus, workload = 6, 1, 1, None
+        pass
     a = A()
-    a.workload = next(k for k, v in WORKLOADS.items() if v["desc"] in wl["desc"])
-    r = run_reference_arm(a, WORKLOADS[a.workload])
+    a.gpus, a.workload = 1, args.workload
+    r = run_reference_arm(a, WORKLOADS[args.workload], steps=3, warmup=1)
     return r["cpu_baseline"]
 
 
@@ -507,7 +602,6 @@ def main():
 
     import torch
     import ffnerf_tools as ft
-    from synthetic_scene import BlobScene, cameras_ring, cameras_sphere, intrinsics, pixel_rays
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
@@ -516,31 +610,11 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
-    # ---- synthetic data: scene, cameras, a pool of global batches (same on every rank)
-    scene = BlobScene(0)
-    cams = cameras_ring(wl["n_cams"], 2.5, 0) if wl["n_cams"] > 8 else cameras_sphere(wl["n_cams"], 2.0, 0)
-    K = intrinsics(wl["W"], wl["H"], 50.0)
+    # ---- synthetic data: a pool of global batches (same on every rank) and the occupancy grid
     n_glob, spr = wl["rays"], wl["spr"]
     n_loc = n_glob // world
-    pool = 4
-    rng = np.random.default_rng(1234)
-    pool_rays, pool_tg = [], []
-    for b in range(pool):
-        ci = rng.integers(0, cams.shape[0], n_glob)
-        u = rng.integers(0, wl["W"], n_glob)
-        v = rng.integers(0, wl["H"], n_glob)
-        rays = np.zeros((n_glob, 8), np.float32)
-        for c in np.unique(ci):
-            sel = ci == c
-            rays[sel] = pixel_rays(cams[c], K, u[sel], v[sel])
-        rays_t = torch.from_numpy(rays).to(dev)
-        rgb = scene.render_torch(rays_t, n_quad=192)
-        tg = torch.zeros((n_glob, 4), device=dev)
-        tg[:, :3] = torch.round(rgb * 255.0) / 255.0
-        sl = slice(rank * n_loc, (rank + 1) * n_loc)
-        pool_rays.append(rays_t[sl].contiguous())
-        pool_tg.append(tg[sl].contiguous())
-    occ_grid = scene.occupancy_grid_torch(wl["G"], dev)
+    pool = BATCH_POOL
+    pool_rays, pool_tg, occ_grid = build_inputs(wl, n_glob, rank, world, dev)
 
     # ---- the model through the public host API
     ctx = ft.Context([ft.Device(local)])
@@ -550,31 +624,37 @@ def main():
                        dt_max=np.float32(12.8 / spr / 6 * 2.0), t_near_clip=np.float32(0.3),
                        t_far_clip=np.float32(1e9), occ_update_strength0=np.float32(1.0)).finalize()
     tmp = tempfile.mkdtemp(prefix="ffn_bench_")
-    nerf = ft.Nerf(ctx, queue, training_dir=tmp, model_id="bench", transfer_fmt="fp32",
-                   table_size_entries=16 << wl["log2T"], f_per_level=wl["F"], occ=occ, rng_seed=777,
-                   background="random", finest_resolution=wl["rmax"], nd=wl["ND"], nc=wl["NC"],
-                   mlp_precision=args.mlp, verbose=False)
-    nerf.state_i32["occ_grid_in_u32"] = occ_grid.view(np.int32).copy()
-    nerf.state_i32["occ_grid_st_u32"] = occ_grid.view(np.int32).copy()
-    nerf.steps_trained = 3000                  # steady-state schedules (past the warm-up phases)
-    if world > 1:
-        nerf.enable_data_parallel(ray_offset=rank * n_loc)
+
+    def make_nerf(mlp_precision: str):
+        m = ft.Nerf(ctx, queue, training_dir=tmp, model_id="bench", transfer_fmt="fp32",
+                    table_size_entries=16 << wl["log2T"], f_per_level=wl["F"], occ=occ, rng_seed=777,
+                    background="random", finest_resolution=wl["rmax"], nd=wl["ND"], nc=wl["NC"],
+                    mlp_precision=mlp_precision, verbose=False)
+        m.state_i32["occ_grid_in_u32"] = occ_grid.view(np.int32).copy()
+        m.state_i32["occ_grid_st_u32"] = occ_grid.view(np.int32).copy()
+        m.steps_trained = START_STEP           # steady-state schedules (past the warm-up phases)
+        if world > 1:
+            m.enable_data_parallel(ray_offset=rank * n_loc)
+        m.setup_buffers(n_loc, spr)
+        return m
+
+    nerf = make_nerf(args.mlp)
     io = ft.RayBatch.init(ctx, queue, n_loc, spr)
-    nerf.setup_buffers(n_loc, spr)
     import schedules as sch
     lmbda = sch.lr_lambda(1e-4, n_glob, spr)
 
-    def one_step(i, host=False):
+    def one_step(i, host=False, model=None):
+        model = model or nerf
         b = i % pool
-        stp = nerf.steps_trained
-        lr_f = sch.lr_schedule(stp, 5e-5 * 8, lmbda, n_glob, spr)
+        stp = model.steps_trained
+        lr_f = sch.lr_schedule(stp, BASE_LR, lmbda, n_glob, spr)
         if host:
             io.upload_rays(host_rays[b])
             io.upload_targets(host_tg[b])
         else:
             io.rays_buf, io.targets_buf = pool_rays[b], pool_tg[b]
-        out = nerf.step(io, lr_f=float(lr_f), do_train=True, return_output=host, sh_multiplier=1.0,
-                        color_MLP_rel_lr=1.0, occ_update_strength=1.0)[0]
+        out = model.step(io, lr_f=float(lr_f), do_train=True, return_output=host, sh_multiplier=1.0,
+                         color_MLP_rel_lr=1.0, occ_update_strength=1.0)[0]
         return out
 
     def barrier():
@@ -595,7 +675,7 @@ def main():
 
     host_s = []
 
-    def timed_steps(n_steps: int, start: int, host: bool, flush: bool = True):
+    def timed_steps(n_steps: int, start: int, host: bool, flush: bool = True, model=None):
         pairs, outs = [], []
         for i in range(n_steps):
             if flush:
@@ -604,7 +684,7 @@ def main():
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(queue.stream)
             h0 = time.perf_counter()
-            out = one_step(start + i, host=host)
+            out = one_step(start + i, host=host, model=model)
             host_s.append(time.perf_counter() - h0)
             b.record(queue.stream)
             pairs.append((a, b))
@@ -650,6 +730,18 @@ def main():
             e2e_ms = max_over_ranks(e2e_sum)
             losses = [float(np.mean((o[:, :3] - host_tg[i % pool][:, :3]) ** 2)) for i, o in enumerate(outs)]
             io = io_dev
+        # (4) the same device-resident steps with the fp32 CUDA-core MLP (one GPU)
+        fp32_line = None
+        if world == 1 and args.mlp == "fp16" and not args.no_e2e:
+            nerf32 = make_nerf("fp32")
+            for i in range(args.warmup):
+                one_step(i, model=nerf32)
+            torch.cuda.synchronize()
+            ms32, _ = timed_steps(args.steps, args.warmup, host=False, model=nerf32)
+            fp32_line = {"value": n_glob * spr * args.steps / (ms32 * 1e-3), "unit": "samples/s",
+                         "ms_per_step": ms32 / args.steps,
+                         "note": "same steps with mlp_precision fp32 (fp32 MLP on the CUDA cores)"}
+            nerf32.native.close()
     clocks = clk.summary()
     if args.no_e2e:
         if rank == 0:
@@ -682,8 +774,13 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": ("f16 operands / f32 accumulation (MLP on tensor cores, compensated hi/lo f16 forward); "
+                      "f32 table" if args.mlp == "fp16" else "f32"),
+            "data": "synthetic",
             "config": {"workload": wl["desc"], "global_batch_rays": n_glob, "samples_per_ray": spr,
+                       "mlp": ("tensor cores: f16 hi/lo operand pairs in the forward, f16 backward operands, "
+                               "f32 accumulation" if args.mlp == "fp16" else "fp32 on the CUDA cores"),
                        "samples_per_step": samples_per_step, "parallelism": f"dp{world}",
                        "table_update": "immediate (Hogwild, in the fused kernel)" if nerf.table_immediate
                                        else ("deferred; fused exchange kernel over NVSwitch multicast (multimem "
@@ -698,6 +795,7 @@ def main():
             "e2e": {"value": e2e_val, "unit": "samples/s", "h2d_bytes_per_step": n_loc * (32 + 16) * world,
                     "d2h_bytes_per_step": n_loc * 16 * world, "final_mse": losses[-1]},
             "gpu_launches": launches,
+            "mlp_fp32": fp32_line,
             "host_ms_per_step": host_ms,
             "exchange_ms": ex_ms,
             "roofline": {"bound": "hbm", "kernel": ("forward/backward group: sample_stage_kernel + encode_stage_kernel + "
@@ -711,7 +809,7 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             try:
-                line["cpu_baseline"] = cpu_baseline_sample(wl)
+                line["cpu_baseline"] = cpu_baseline_sample(args, wl)
             except Exception as exc:   # the baseline is a side measurement; report why it is missing
                 line["cpu_baseline"] = {"value": None, "unit": "samples/s", "cores": os.cpu_count(),
                                         "kind": "reference", "sample": f"not run: {exc}"}
