@@ -8,6 +8,9 @@
 #include <cstdio>
 #include <vector>
 
+#include <omp.h>
+#include <sys/mman.h>
+
 #if !defined(__x86_64__)
 #include <ucontext.h>
 #endif
@@ -141,7 +144,67 @@ void run_work_group(size_t gx, size_t gy, size_t lx, size_t ly, const std::funct
             if (wg.fibers[i].done) --remaining;
         }
     }
+    wg.free_locals();
     tls_wg = saved;
+}
+
+void run_work_groups_lockstep(size_t n_groups, size_t lx, const std::function<void()>& body, int n_threads) {
+#if defined(__x86_64__)
+    const int nt = n_threads > 0 ? n_threads : 1;
+    std::vector<long> live((size_t)nt, 0);
+    #pragma omp parallel num_threads(nt)
+    {
+        const size_t t = (size_t)omp_get_thread_num(), T = (size_t)omp_get_num_threads();
+        std::vector<WorkGroup> wgs;
+        for (size_t g = t; g < n_groups; g += T) {
+            WorkGroup wg;
+            wg.n = (int)lx;
+            wg.group_id[0] = g;
+            wg.local_size[0] = lx;
+            wg.body = body;
+            wgs.push_back(wg);
+        }
+        const size_t n_fibers = wgs.size() * lx;
+        // one reservation for all stacks of this thread: pages are committed only when touched
+        char* stacks = n_fibers ? (char*)mmap(nullptr, n_fibers * kStackBytes, PROT_READ | PROT_WRITE,
+                                               MAP_PRIVATE | MAP_ANONYMOUS | MAP_NORESERVE, -1, 0) : nullptr;
+        if (n_fibers && stacks == (char*)MAP_FAILED) std::abort();
+        std::vector<Fiber> fibers(n_fibers);
+        for (size_t k = 0; k < wgs.size(); ++k) {
+            wgs[k].fibers = fibers.data() + k * lx;
+            for (size_t i = 0; i < lx; ++i) {
+                Fiber& f = wgs[k].fibers[i];
+                f.stack = stacks + (k * lx + i) * kStackBytes;
+                f.sp = init_stack(f.stack);
+                f.done = false;
+            }
+        }
+        long mine = (long)n_fibers;
+        for (;;) {
+            for (WorkGroup& wg : wgs) {        // one barrier interval of every group of this thread
+                tls_wg = &wg;
+                for (int i = 0; i < wg.n; ++i) {
+                    if (wg.fibers[i].done) continue;
+                    wg.cur = i;
+                    to_fiber(&wg, i);
+                    if (wg.fibers[i].done) --mine;
+                }
+            }
+            tls_wg = nullptr;
+            live[t] = mine;
+            #pragma omp barrier
+            long total = 0;
+            for (long x : live) total += x;
+            #pragma omp barrier
+            if (total == 0) break;
+        }
+        for (WorkGroup& wg : wgs) wg.free_locals();
+        if (stacks) munmap(stacks, n_fibers * kStackBytes);
+    }
+#else
+    (void)n_groups; (void)lx; (void)body; (void)n_threads;
+    std::abort();   // lockstep scheduling is implemented for x86-64 only
+#endif
 }
 
 }  // namespace clemu

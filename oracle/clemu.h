@@ -100,6 +100,8 @@ struct Fiber {
     bool done = false;
 };
 
+constexpr int kMaxLocals = 64;    // __local variables per kernel
+
 struct WorkGroup {
     int n = 0;
     size_t group_id[2] = {0, 0}, local_size[2] = {1, 1};
@@ -107,9 +109,22 @@ struct WorkGroup {
     void* sched_sp = nullptr;
     Fiber* fibers = nullptr;
     std::function<void()> body;
+    void* locals[kMaxLocals] = {};  // this group's __local memory, one block per declaration
+    void free_locals() {
+        for (void*& p : locals) { std::free(p); p = nullptr; }
+    }
 };
 
 extern thread_local WorkGroup* tls_wg;
+
+// The __local variable `id` of the running work-group: zeroed on the group's first use, then shared
+// by its work-items (ref_build.py rewrites each __local declaration into a reference to it).
+template <typename T>
+T& local_ref(int id) {
+    void*& p = tls_wg->locals[id];
+    if (!p) p = std::calloc(1, sizeof(T));
+    return *reinterpret_cast<T*>(p);
+}
 
 inline size_t get_group_id(int d) { return tls_wg->group_id[d]; }
 inline size_t get_local_size(int d) { return tls_wg->local_size[d]; }
@@ -121,5 +136,11 @@ void barrier(int flags);
 
 // Runs `body` once per work-item of a (lx * ly)-item work-group with ids (gx, gy).
 void run_work_group(size_t gx, size_t gy, size_t lx, size_t ly, const std::function<void()>& body);
+
+// Runs work-groups 0 .. n_groups-1 (lx work-items each) in lockstep: every work-item of every group
+// reaches barrier k before any passes it, as on a device that holds all the groups at once.  The
+// groups are spread over n_threads OS threads that meet at a thread barrier after every barrier
+// interval.
+void run_work_groups_lockstep(size_t n_groups, size_t lx, const std::function<void()>& body, int n_threads);
 
 }  // namespace clemu

@@ -155,7 +155,8 @@ class RefTrainArgs(C.Structure):
                 ("box_min", C.c_float * 3), ("box_max", C.c_float * 3), ("G", C.c_int32),
                 ("rho_min", C.c_float), ("rho_max", C.c_float), ("dt_min", C.c_float),
                 ("dt_max", C.c_float), ("t_near", C.c_float), ("t_far", C.c_float),
-                ("seed", C.c_uint32), ("occ_strength", C.c_float), ("n_threads", C.c_int32)]
+                ("seed", C.c_uint32), ("occ_strength", C.c_float), ("n_threads", C.c_int32),
+                ("lockstep", C.c_int32)]
 
 
 class RefWUArgs(C.Structure):
@@ -209,7 +210,11 @@ class RefKernels:
 
     def train(self, params: dict, table, rays, targets, out, scratch: dict, occ_in, occ_st, geom: dict,
               lr: float, sh_mult: float, occ_strength: float, seed: int, do_train: bool = True,
-              n_threads: int = 1) -> None:
+              n_threads: int = 1, lockstep: bool = False) -> None:
+        """One launch of ffnerf_train_step over the rays.  lockstep: every work-group advances barrier
+        interval by barrier interval with all the others (each table read of the step precedes each
+        in-kernel table update, the schedule of a device running the whole batch at once); else each
+        OS thread runs one work-group to completion at a time (n_threads = 1: rays in order)."""
         a = RefTrainArgs()
         keep = []
         for i, n in enumerate(REF_W):
@@ -232,6 +237,7 @@ class RefKernels:
                       ("dt_max", "dt_max"), ("t_near", "t_near"), ("t_far", "t_far")):
             setattr(a, k, float(geom[kk]))
         a.seed, a.occ_strength, a.n_threads = int(seed) & 0xFFFFFFFF, occ_strength, n_threads
+        a.lockstep = int(bool(lockstep))
         del keep
         self.lib.ffnref_train(C.byref(a))
 

@@ -31,6 +31,10 @@ typedef struct {
     uint32_t seed;
     float occ_strength;
     int32_t n_threads;    /* OS threads running work-groups (1 = sequential ray order) */
+    int32_t lockstep;     /* 1: all rays' work-groups advance barrier interval by barrier interval
+                             together (every table read of the step precedes every table update,
+                             as on a GPU that holds the whole batch); 0: one work-group at a time
+                             per OS thread */
 } ffnref_train_args;
 
 typedef struct {

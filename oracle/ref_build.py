@@ -10,8 +10,10 @@ Rewrites (syntax only):
   * ``(float3)(a,b,c)`` / ``(float4)(a,b,c,d)`` vector literals -> braced initialisers (which keep
     OpenCL's left-to-right evaluation of the components), ``(float3)(s)`` -> broadcast;
   * ``.xyz`` swizzle -> ``.xyz()``;
-  * ``__local`` variable declarations inside kernels -> ``static thread_local`` (shared by the
-    fibers of one work-group); every other ``__local`` / ``__global`` qualifier is dropped;
+  * ``__local`` variable declarations inside kernels -> references into the local memory of the
+    running work-group (``clemu::local_ref``, shared by its fibers, separate per work-group, so that
+    several work-groups can be in flight on one OS thread); every other ``__local`` / ``__global``
+    qualifier is dropped;
   * ``__constant`` -> ``static const``; OpenCL extension pragmas are removed.
 
 Patches (semantics), each asserted to apply exactly once:
@@ -101,13 +103,33 @@ def _sub_once(pattern: str, repl: str, src: str, flags=0) -> str:
     return out
 
 
+_LOCAL_ID = [0]
+
+
+def _local_decl(m: re.Match) -> str:
+    """``__local T a[N], b;`` -> one reference per name into the running work-group's local memory
+    (clemu::local_ref: allocated zeroed on first use by the group, shared by its work-items)."""
+    indent, typ, names = m.group(1), m.group(2), m.group(3)
+    out = []
+    for part in names.split(","):
+        part = part.strip()
+        nm = re.match(r"(\w+)\s*(\[[^\]]*\])?", part)
+        name, dim = nm.group(1), nm.group(2) or ""
+        if _LOCAL_ID[0] >= 64:
+            raise ValueError("more __local declarations than clemu::kMaxLocals")
+        out.append(f"auto& {name} = ::clemu::local_ref<{typ}{dim}>({_LOCAL_ID[0]});")
+        _LOCAL_ID[0] += 1
+    return indent + " ".join(out)
+
+
 def translate(src: str) -> str:
+    _LOCAL_ID[0] = 0        # __local ids are per translation unit (clemu::kMaxLocals of them)
     src = re.sub(r"^\s*#pragma\s+OPENCL.*$", "", src, flags=re.M)
     src = _rewrite_vector_literals(src)
     src = re.sub(r"\.xyz\b", ".xyz()", src)
     src = re.sub(
         r"^(\s*)__local\s+(\w+)\s+(\w+\s*(?:\[[^\]]*\])?(?:\s*,\s*\w+\s*(?:\[[^\]]*\])?)*)\s*;",
-        r"\1static thread_local \2 \3;", src, flags=re.M)
+        _local_decl, src, flags=re.M)
     src = src.replace("__local", "")
     src = re.sub(r"\b__kernel\b", "", src)
     src = re.sub(r"\b__global\b", "", src)
@@ -143,9 +165,7 @@ extern "C" void ffnref_train(const ffnref_train_args* a) {
     float4* out = (float4*)a->out;
     const long n = (long)a->num_rays;
     const int nt = a->n_threads > 0 ? a->n_threads : 1;
-    #pragma omp parallel for schedule(dynamic, 4) num_threads(nt)
-    for (long g = 0; g < n; ++g) {
-        run_work_group((size_t)g, 0, a->spr, 1, [&]() {
+    auto body = [&]() {
             ffnerf_train_step(a->W[0], a->W[1], a->W[2], a->W[3], a->b[0], a->b[1], a->b[2], a->b[3],
                               a->W[4], a->W[5], a->W[6], a->W[7], a->W[8],
                               a->b[4], a->b[5], a->b[6], a->b[7], a->b[8],
@@ -157,8 +177,13 @@ extern "C" void ffnref_train(const ffnref_train_args* a) {
                               out, a->lr, a->num_rays, a->spr, a->do_train, a->sh_mult,
                               a->occ_in, a->occ_st, bmin, bmax, a->G, a->rho_min, a->rho_max,
                               a->dt_min, a->dt_max, a->t_near, a->t_far, a->seed, a->occ_strength);
-        });
+    };
+    if (a->lockstep) {
+        run_work_groups_lockstep((size_t)n, a->spr, body, nt);
+        return;
     }
+    #pragma omp parallel for schedule(dynamic, 4) num_threads(nt)
+    for (long g = 0; g < n; ++g) run_work_group((size_t)g, 0, a->spr, 1, body);
 }
 
 extern "C" void ffnref_info(int32_t* f_, int32_t* nd_, int32_t* nc_, int32_t* log2T, float* rmax) {

@@ -101,3 +101,58 @@ def test_decay_matches_compiled_reference(oracle, variant):
         ref.decay(a1, b1, dq, seed)
         oracle.decay(a2, b2, dq, seed)
         assert np.array_equal(a1, a2) and np.array_equal(b1, b2)
+
+
+@pytest.mark.parametrize("variant", ["cfg1", "default"])
+def test_reference_lockstep_matches_deferred_oracle(oracle, variant):
+    """The reference kernels with every work-group of the step in lockstep (barrier interval by
+    barrier interval, on 4 OS threads: the schedule of a device that holds the whole batch, where
+    each ray's table reads precede every ray's in-kernel table update) against the oracle's deferred
+    table mode: ray colours, occupancy proposals and the weight update + Adam are bit-identical; the
+    tables after the step (the reference adds each -lr 2^(-0.1 l) 0.5 g w with a CAS loop, the oracle
+    sums g w per entry first) agree within float rounding of the table values.  The near-sequential schedule (one work-group at a
+    time, rays in order) gives other colours."""
+    if not ref_so(variant).exists():
+        pytest.skip("reference kernels not compiled here")
+    ref = RefKernels(variant)
+    g = make_geometry(**VARIANTS[variant])
+    n = 48
+    rays = rays_toward_box(n, 31, radius=6.0 if variant == "default" else 2.0, n_miss=3)
+    tg = targets(n, 31)
+    blob = init_blob(g, 31, sigma_bias=2.0)
+    table0 = init_table(g, 31)
+    occ0 = init_occ(g, 31, mask=0x33333333)
+    lr, seed = np.float32(5e-2), 77
+    runs = {}
+    for mode in ("lockstep", "sequential"):
+        params = {k: v.view(np.int32).copy() for k, v in _split(blob, g).items()}
+        tab, out, occ_st = table0.copy(), np.zeros((n, 4), np.float32), occ0.copy()
+        scr = ref.alloc_scratch(n * g["spr"])
+        ref.train(params, tab.view(np.int32), rays, tg, out, scr, occ0.copy(), occ_st, g, float(lr), 1.0, 1.0, seed,
+                  True, 4 if mode == "lockstep" else 1, lockstep=mode == "lockstep")
+        m = {k: np.zeros(v.size, np.float32) for k, v in params.items()}
+        v_ = {k: np.zeros(v.size, np.float32) for k, v in params.items()}
+        ref.weight_update(params, m, v_, scr, n * g["spr"], 1e-3, 0.15, 0.9, 0.999, 1e-6)
+        runs[mode] = (params, m, v_, tab, out, occ_st)
+    cfg = make_orc_config(g, math_mode=1, table_mode=0)
+    tab_o, out_o, occ_st_o = table0.copy(), np.zeros((n, 4), np.float32), occ0.copy()
+    tgr, mg = np.zeros_like(table0), np.zeros(blob.size, np.float32)
+    oracle.forward_backward(cfg, OrcStep(lr, 1.0, 1.0, seed, 1, 0), blob, tab_o, occ0.copy(), occ_st_o, rays, tg, out_o,
+                            tgr, mg)
+    oracle.table_apply(cfg, tab_o, tgr, lr)
+    p_o, m_o, v_o = blob.copy(), np.zeros_like(blob), np.zeros_like(blob)
+    oracle.mlp_adam(cfg, p_o, mg, m_o, v_o, np.float32(1e-3), np.float32(0.15), np.float32(0.9), np.float32(0.999),
+                    np.float32(1e-6))
+    params, m, v_, tab, out, occ_st = runs["lockstep"]
+    assert np.array_equal(out, out_o)
+    assert np.array_equal(occ_st, occ_st_o) and (occ_st != occ0).sum() > 0
+    lay, _ = param_layout(g["F"], g["ND"], g["NC"])
+    for name, (off, sz) in lay.items():
+        if sz:
+            assert np.array_equal(params[name].view(np.float32), p_o[off:off + sz]), name
+            assert np.array_equal(m[name], m_o[off:off + sz]) and np.array_equal(v_[name], v_o[off:off + sz]), name
+    # each of the reference's in-kernel adds rounds to the table value's ulp (~1e-8 here, about the size of
+    # one add), so the two tables agree to float rounding of the table, not of the change
+    assert (tab_o != table0).sum() > 1000
+    assert np.linalg.norm((tab - tab_o).astype(np.float64)) <= 1e-6 * np.linalg.norm(table0.astype(np.float64))
+    assert not np.array_equal(runs["sequential"][4], out)
