@@ -233,6 +233,7 @@ def run_micro(args, name: str) -> dict:
                 fwd(); bwd()
                 h_enc.copy_(enc, non_blocking=True)
             (t_e2e,) = timed([e2e])
+        ceil = random_access_ceiling(g["table_entries"] * wl["F"] * s_tab, 16 * 8 * n, dev, st)
         bf, bb = hash_bytes_per_point(wl["F"], s_tab)
         gbs_f = bf * n / (t_fwd / args.steps * 1e-3) / 1e9
         gbs_b = bb * n / (t_bwd / args.steps * 1e-3) / 1e9
@@ -275,6 +276,16 @@ def run_micro(args, name: str) -> dict:
                          else "hash_fwd_kernel + hash_bwd_kernel", "achieved": gbs, "peak": hbm,
                          "unit": "GB/s", "frac": gbs / hbm, "traffic": None, "peak_source": peak_kind,
                          "note": "peak = measured HBM copy bandwidth; random 8 B gathers move 32 B sectors"},
+            "achievable": {
+                "what": "fully random 8-byte accesses over a buffer of the table's size (ffn_probe_random_access: "
+                        "float2 loads on the read-only path / red.global.add.v2.f32), 8 in flight per thread",
+                "gather_ops_per_s": ceil["gather_ops_per_s"], "red_ops_per_s": ceil["red_ops_per_s"],
+                "fwd_gathers_per_s": 128 * n / (t_fwd / args.steps * 1e-3),
+                "fwd_frac": 128 * n / (t_fwd / args.steps * 1e-3) / ceil["gather_ops_per_s"],
+                "bwd_reds_per_s": 128 * n / (t_bwd / args.steps * 1e-3),
+                "bwd_frac": 128 * n / (t_bwd / args.steps * 1e-3) / ceil["red_ops_per_s"],
+                "note": "16 levels x 8 corners = 128 random accesses per point each way; coarse levels share "
+                        "cells between points, so a kernel can exceed the fully random rate"},
             "clocks": clk.summary(),
             "cpu_baseline": {"value": cpu_gbs, "unit": "GB/s", "cores": 1, "kind": "port",
                              "sample": f"{m} points fwd+bwd, oracle restatement (fp32 table; its GB/s counts "
@@ -337,6 +348,33 @@ def run_micro(args, name: str) -> dict:
 def fused_bytes_per_sample(F: int, spr: int) -> float:
     gather = 16 * 8 * F * 4
     return gather + 2 * gather + 64.0 / spr + 4
+
+
+def random_access_ceiling(table_bytes: int, n_ops: int, dev, st, reps: int = 5) -> dict:
+    """Achievable rates of fully random 8-byte loads and vector reductions over a buffer of
+    table_bytes (ffn_probe_random_access): median of reps launches of n_ops each, CUDA events on st."""
+    import torch
+    import ffn_native as fn
+    buf = torch.zeros(max(table_bytes // 4, 4), dtype=torch.float32, device=dev)
+    out = {}
+    for mode, name in ((fn.PROBE_GATHER, "gather"), (fn.PROBE_RED, "red")):
+        with torch.cuda.stream(st):
+            fn.probe_random_access(buf, mode, n_ops, seed=7, stream=st)
+        ms = []
+        for r in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            with torch.cuda.stream(st):
+                fn.probe_random_access(buf, mode, n_ops, seed=11 + r, stream=st)
+            b.record(st)
+            torch.cuda.synchronize()
+            ms.append(a.elapsed_time(b))
+        out[name + "_ops_per_s"] = n_ops / (statistics.median(ms) * 1e-3)
+        out[name + "_ms"] = statistics.median(ms)
+    out["table_bytes"] = int(table_bytes)
+    out["ops"] = int(n_ops)
+    del buf
+    return out
 
 
 def peaks():
@@ -742,6 +780,11 @@ def main():
                          "ms_per_step": ms32 / args.steps,
                          "note": "same steps with mlp_precision fp32 (fp32 MLP on the CUDA cores)"}
             nerf32.native.close()
+        # (5) the random-access ceiling at the step's table size: as many random gathers as the encoder
+        # makes and as many random reductions as the scatter would make without its coarse-level merging
+        ceil = None
+        if world == 1 and not args.no_e2e:
+            ceil = random_access_ceiling((16 << wl["log2T"]) * wl["F"] * 4, 16 * 8 * n_loc * spr, dev, queue.stream)
     clocks = clk.summary()
     if args.no_e2e:
         if rank == 0:
@@ -804,9 +847,18 @@ def main():
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": traffic, "peak_source": peak_kind,
                          "algorithmic_bytes_per_sample": fused_bytes_per_sample(wl["F"], spr),
-                         "launch_ms": fb_ms},
+                         "launch_ms": fb_ms,
+                         "binding": "random 32-byte sector requests (trilinear gathers in L1/L2, vector "
+                                    "reductions at L2; the table is L2-resident), not DRAM bandwidth: see achievable"},
             "clocks": clocks,
         }
+        if ceil is not None:
+            floor_ms = ceil["gather_ms"] + ceil["red_ms"]
+            line["roofline"]["achievable"] = {
+                "what": "the step's random accesses at the measured fully random rates over a buffer of the "
+                        "table's size: 128 gathers + 128 vector reductions per sample (ffn_probe_random_access)",
+                "gather_ops_per_s": ceil["gather_ops_per_s"], "red_ops_per_s": ceil["red_ops_per_s"],
+                "floor_ms": floor_ms, "frac": floor_ms / fb_ms}
         if world == 1 and not args.no_cpu_baseline:
             try:
                 line["cpu_baseline"] = cpu_baseline_sample(args, wl)

@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 SO = HERE / "libffnerf.so"
-SOURCES = [HERE / "csrc" / n for n in ("ffn_capi.cu", "ffn_step.cu", "ffn_common.cuh", "ffn_raymarch.cuh", "ffn_hashgrid.cuh", "ffn_tcgen05.cuh", "ffn_step_tc.cu", "ffn_noalloc.cu", "ffn_dp.cu", "ffn_batch.cu")] + [ROOT / "include" / "ffnerf.h"]
+SOURCES = [HERE / "csrc" / n for n in ("ffn_capi.cu", "ffn_step.cu", "ffn_common.cuh", "ffn_raymarch.cuh", "ffn_hashgrid.cuh", "ffn_tcgen05.cuh", "ffn_step_tc.cu", "ffn_noalloc.cu", "ffn_dp.cu", "ffn_batch.cu", "ffn_probe.cu")] + [ROOT / "include" / "ffnerf.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -873,3 +873,4 @@ int ffn_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_t
 }  // extern "C"
 
 #include "ffn_noalloc.cu"
+#include "ffn_probe.cu"

@@ -82,6 +82,7 @@ _SIGS = {
     "ffn_bind_external": (C.c_int, [_VP, C.c_int, _VP, C.c_size_t]),
     "ffn_dp_attach_multicast": (C.c_int, [_VP, _VP, _VP]),
     "ffn_kernel_launches": (C.c_uint64, [_VP]),
+    "ffn_probe_random_access": (C.c_int, [_VP, C.c_size_t, C.c_int, C.c_uint64, C.c_uint32, _VP]),
     "ffn_batch_generate": (C.c_int, [_VP, C.c_int, C.c_int, _VP, _VP, _VP, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_uint32, C.c_float, C.c_uint32, C.c_uint32, _VP, _VP, _VP, _VP, _VP, _VP]),
     "ffn_batch_errors": (C.c_int, [_VP, _VP, C.c_uint32, _VP, _VP, _VP]),
@@ -369,3 +370,16 @@ def adam(p, g, m, v, n: int, lr_t: float, beta1: float, beta2: float, eps: float
     rc = lib.ffn_adam(_ptr(p), _ptr(g), _ptr(m), _ptr(v), int(n), lr_t, beta1, beta2, eps, Context._stream(stream))
     if rc != FFN_OK:
         raise RuntimeError(f"ffn_adam failed ({rc})")
+
+
+PROBE_GATHER, PROBE_RED = 0, 1
+
+
+def probe_random_access(buf, mode: int, n_ops: int, seed: int = 1, stream=None):
+    """n_ops fully random 8-byte loads (PROBE_GATHER) or vector reductions (PROBE_RED) over the
+    device tensor ``buf`` (the ceiling probe of ffn_probe_random_access)."""
+    lib = load_library()
+    rc = lib.ffn_probe_random_access(_ptr(buf), buf.numel() * buf.element_size(), int(mode), int(n_ops),
+                                     int(seed) & 0xFFFFFFFF, Context._stream(stream))
+    if rc != FFN_OK:
+        raise RuntimeError(f"ffn_probe_random_access failed ({rc}): {lib.ffn_last_error(None).decode()}")

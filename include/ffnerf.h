@@ -182,6 +182,13 @@ int ffn_hash_encode_bwd_f16(ffn_ctx* ctx, void* grad16, const float* pts, const 
  * part of FFN_BUF_GRADS.  The table and its gradients are not touched. */
 int ffn_pack_x0(ffn_ctx* ctx, const void* x16, void* tiles, int64_t n, void* stream);
 int ffn_mlp_bench(ffn_ctx* ctx, const void* tiles, int64_t n, void* stream);
+/* Ceiling probe (no reference counterpart): n_ops fully random 8-byte accesses (mode 0: float2
+ * loads through the read-only path, as the hash encoders do; mode 1: red.global.add.v2.f32
+ * reductions, as the gradient scatter does; both adding a negligible value) over the largest
+ * power-of-two number of 8-byte entries in the caller's device buffer buf (bytes), eight
+ * independent accesses in flight per thread.  Timed by the caller, it gives the achievable
+ * random-access rate that bounds the encode and scatter kernels at that table size. */
+int ffn_probe_random_access(void* buf, size_t bytes, int mode, uint64_t n_ops, uint32_t seed, void* stream);
 /* Kernels this context has launched so far (all entry points; no reference counterpart). */
 uint64_t ffn_kernel_launches(const ffn_ctx* ctx);
 /* Reads and clears the context's device status word (waits for the device): 0 when every kernel
