@@ -16,7 +16,10 @@ their host-side results are captured:
   * golden_schedules.npz   -- run_ffnerf_OG's learning-rate, SH, occupancy and colour-lr
                               schedules over a step range;
   * golden_batch_feedback.npz -- run_ffnerf_OG's pixel-weight feedback (_update_weights_u8 with
-                              the make_fg_mask_from_rgb foreground) on small uint8 images.
+                              the make_fg_mask_from_rgb foreground) on small uint8 images;
+  * golden_ref_checkpoint.npz -- a checkpoint written by the reference's own Nerf.save (F=2, ND=1,
+                              after 70 recorded steps); the stub's device->host copy returns
+                              what was uploaded to each buffer, so it holds the initial draws.
 The tests compare this repository's host module against these arrays bit for bit.
 """
 from __future__ import annotations
@@ -74,9 +77,16 @@ def _enqueue_nd_range_kernel(queue=None, kernel=None, global_work_size=None, loc
     return _Event()
 
 
+COPY_FROM_HOSTBUF = [False]
+
+
 def _enqueue_copy(queue, dst, src, wait_for=None):
     if isinstance(dst, np.ndarray):
-        dst[...] = 0
+        hb = getattr(src, "kw", {}).get("hostbuf") if COPY_FROM_HOSTBUF[0] else None
+        if hb is not None and np.asarray(hb).nbytes == dst.nbytes:
+            dst.reshape(-1).view(np.uint8)[...] = np.ascontiguousarray(hb).reshape(-1).view(np.uint8)
+        else:
+            dst[...] = 0
     return _Event()
 
 
@@ -136,6 +146,13 @@ def host_init_and_steps(ft, tmp: Path):
                                wu_color=np.float32(sc[4]), wu_b1=np.float32(sc[5]), wu_b2=np.float32(sc[6]),
                                wu_eps=np.float32(sc[7]), wu_gws=gws, wu_lws=lws)
             steps.append(rec)
+        # the reference's own checkpoint writer, device buffers read back as uploaded
+        COPY_FROM_HOSTBUF[0] = True
+        try:
+            path = nerf.save(min_new_file_seconds=0)
+        finally:
+            COPY_FROM_HOSTBUF[0] = False
+        (OUT / "golden_ref_checkpoint.npz").write_bytes(Path(path).read_bytes())
     keys = sorted({k for r in steps for k in r})
     cols = {}
     for k in keys:

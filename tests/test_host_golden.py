@@ -102,3 +102,33 @@ def test_checkpoint_roundtrip_reference_layout(tmp_path):
     assert other.steps_trained == 17 and (other.ND, other.NC, other.f_per_level) == (1, 2, 2)
     for k, v in nerf.state_i32.items():
         assert np.array_equal(np.asarray(other.state_i32[k]).ravel(), np.asarray(v).ravel()), k
+
+
+def test_checkpoint_written_by_reference_loads(tmp_path):
+    """A checkpoint written by the reference's own Nerf.save (golden_ref_checkpoint.npz, from
+    make_golden.py) loads through load_latest with every array, the geometry, the occupancy
+    parameters and the step count; saving it again writes the same values under the same keys."""
+    import shutil
+    ref = np.load(G / "golden_ref_checkpoint.npz")
+    mid = str(ref["model_id"])
+    shutil.copy(G / "golden_ref_checkpoint.npz", tmp_path / f"{mid}_weights_20260101-000000.npz")
+    nerf = ft.Nerf(None, None, training_dir=tmp_path, model_id="again", load_id=mid, rng_seed=1)
+    assert nerf.steps_trained == int(ref["steps_trained"])
+    assert (nerf.ND, nerf.NC, nerf.f_per_level) == (int(ref["ND"]), int(ref["NC"]), int(ref["table_f_per_level"]))
+    assert nerf.transfer_fmt == str(ref["transfer_fmt"])
+    assert np.array_equal(nerf.state_i32["table"], ref["table_i"])
+    for name in ref["active_params"].tolist():
+        for pre in ("", "m", "v"):
+            assert np.array_equal(np.asarray(nerf.state_i32[pre + name]).ravel(), ref[pre + name + "_i"]), pre + name
+    assert np.array_equal(nerf.state_i32["occ_grid_in_u32"].view(np.uint32), ref["occ_grid_in_u32"])
+    assert np.array_equal(nerf.state_i32["occ_grid_st_u32"].view(np.uint32), ref["occ_grid_st_u32"])
+    for k in ("box_min", "box_max"):
+        assert np.array_equal(getattr(nerf.occ, k), ref[k])
+    for k in ("rho_min", "rho_max", "dt_min", "dt_max", "t_near_clip", "t_far_clip"):
+        assert np.float32(getattr(nerf.occ, k)) == ref[k], k
+    out = np.load(nerf.save(min_new_file_seconds=0))
+    for k in ref.files:
+        if k in ("timestamp", "model_id"):
+            continue
+        assert k in out.files, k
+        assert out[k].dtype == ref[k].dtype and np.array_equal(out[k], ref[k]), k
