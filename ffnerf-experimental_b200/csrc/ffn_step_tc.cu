@@ -67,7 +67,8 @@ struct TcPlan {
     static constexpr int LO = X0 + ROWS * LPOS * 2;           // the lo tile of the operand being multiplied
                                                               // (16 KB: any [128 x 64] or X0); the
                                                               // output-delta tile in the backward
-    static constexpr int DC = LO;                             // output delta [128 x 16]
+    static constexpr int DC = LO;                             // output delta [128 x 16], its lo at DC + DC_LO
+    static constexpr int DC_LO = ROWS * 16 * 2;
     static constexpr int HD = LO + ROWS * 64 * 2;             // ND density hidden tiles [128 x 64]
     static constexpr int XC = HD + ND * ROWS * 64 * 2;        // colour input [128 x 32]
     static constexpr int C1 = XC + ROWS * 32 * 2;             // colour hidden 1 [128 x 64]
@@ -139,6 +140,23 @@ __device__ __forceinline__ void gemm_fwd3(uint32_t d, uint32_t a_hi, uint32_t a_
     gemm(d, a_lo, a_cols, false, w_hi, a_cols, false, 128, N, K, 1);
 }
 
+// Backward-data layer with compensated operands: ACC = Dh*Wh + Dl*Wh + Dh*Wl, D [128 x K] K-major
+// (d_cols columns), W [K x N] read MN-major (w_cols columns).  One thread.
+__device__ __forceinline__ void gemm_bwd3(uint32_t d, uint32_t d_hi, uint32_t d_lo, int d_cols, uint32_t w_hi,
+                                         uint32_t w_lo, int w_cols, int N, int K) {
+    gemm(d, d_hi, d_cols, false, w_hi, w_cols, true, 128, N, K, 0);
+    gemm(d, d_lo, d_cols, false, w_hi, w_cols, true, 128, N, K, 1);
+    gemm(d, d_hi, d_cols, false, w_lo, w_cols, true, 128, N, K, 1);
+}
+
+// Weight (or bias, with the one-hot tile) gradient with a compensated delta: ACC (+)= Dh^T X + Dl^T X,
+// D [128 x 64] and X [128 x N] both read MN-major (the activation X stays a single fp16 tile).
+__device__ __forceinline__ void gemm_wgrad2(uint32_t d, uint32_t d_hi, uint32_t d_lo, uint32_t x, int x_cols, int N,
+                                           uint32_t accumulate) {
+    gemm(d, d_hi, 64, true, x, x_cols, true, 64, N, 128, accumulate);
+    gemm(d, d_lo, 64, true, x, x_cols, true, 64, N, 128, 1);
+}
+
 // One row (this thread's sample) of an ACC region into registers.
 template <int N>
 __device__ __forceinline__ void acc_row(uint32_t tmem, uint32_t col, float (&v)[N]) {
@@ -187,7 +205,8 @@ __device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N
 // Epilogue of a backward layer: row = ACC masked by (activation in `tile` > 0), written in place,
 // 32 columns at a time.  The mask reads the hi copy of the activation, which is > 0 whenever the
 // activation is, except below fp16's smallest subnormal (2^-24), where the delta's share is negligible.
-__device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N, unsigned char* tile, int cols) {
+__device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N, unsigned char* tile,
+                                              unsigned char* lo_tile, int cols) {
     const uint32_t lane = tlane();
     const int r = trow();
 #pragma unroll 1
@@ -201,7 +220,7 @@ __device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = act[i] > 0.0f ? v[i] : 0.0f;
 #pragma unroll
-        for (int q = 0; q < 32; q += 8) tc::st_chunk8(tile, r, j + q, cols, v + q);
+        for (int q = 0; q < 32; q += 8) tc::st_chunk8_hilo(tile, lo_tile, r, j + q, cols, v + q);
     }
 }
 
@@ -758,7 +777,7 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;
             v[0] = dcout[0] * DELTA_SCALE; v[1] = dcout[1] * DELTA_SCALE; v[2] = dcout[2] * DELTA_SCALE;
-            store_row<16>(tDC, 16, v);
+            store_row_hilo<16>(tDC, tDC + PL::DC_LO, 16, v);
             // colour-head bias gradient: a transposed warp butterfly, then three lanes add at once
             {
                 const float v4[4] = {v[0], v[1], v[2], 0.0f};
@@ -771,27 +790,31 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         handoff();
         if (tid == 0) {
             gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC), 16, true, 64, 16, 128, acc0);            // dWc_out^T
-            gemm(tmem + PL::ACC, G(PL::DC), 16, false, S(PL::W_HI + PL::W_COUT), 64, true, 128, 64, 16, 0);      // dC2
+            gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC) + PL::DC_LO, 16, true, 64, 16, 128, 1);
+            gemm_bwd3(tmem + PL::ACC, G(PL::DC), G(PL::DC) + PL::DC_LO, 16, S(PL::W_HI + PL::W_COUT),
+                      S(PL::W_LO + PL::W_COUT), 64, 64, 16);                                                       // dC2
         }
         sync_mma();
         {
-            epi_relu_mask(tmem, PL::ACC, 64, tC2, 64);
+            epi_relu_mask(tmem, PL::ACC, 64, tC2, tLO, 64);
         }
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_C01, G(PL::C2), 64, true, G(PL::C1), 64, true, 64, 64, 128, acc0);               // dWc_01
-            gemm(tmem + PL::B_C1, G(PL::C2), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbc_1
-            gemm(tmem + PL::ACC, G(PL::C2), 64, false, S(PL::W_HI + PL::W_C01), 64, true, 128, 64, 64, 0);       // dC1
+            gemm_wgrad2(tmem + PL::DW_C01, G(PL::C2), G(PL::LO), G(PL::C1), 64, 64, acc0);                      // dWc_01
+            gemm_wgrad2(tmem + PL::B_C1, G(PL::C2), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbc_1
+            gemm_bwd3(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_C01), S(PL::W_LO + PL::W_C01),
+                      64, 64, 64);                                                                                // dC1
         }
         sync_mma();
         {
-            epi_relu_mask(tmem, PL::ACC, 64, tC1, 64);
+            epi_relu_mask(tmem, PL::ACC, 64, tC1, tLO, 64);
         }
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_CIN, G(PL::C1), 64, true, G(PL::XC), 32, true, 64, 32, 128, acc0);               // dWc_in
-            gemm(tmem + PL::B_C0, G(PL::C1), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbc_0
-            gemm(tmem + PL::ACC, G(PL::C1), 64, false, S(PL::W_HI + PL::W_CIN), 32, true, 128, 16, 64, 0);       // dDout
+            gemm_wgrad2(tmem + PL::DW_CIN, G(PL::C1), G(PL::LO), G(PL::XC), 32, 32, acc0);                      // dWc_in
+            gemm_wgrad2(tmem + PL::B_C0, G(PL::C1), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbc_0
+            gemm_bwd3(tmem + PL::ACC, G(PL::C1), G(PL::LO), 64, S(PL::W_HI + PL::W_CIN), S(PL::W_LO + PL::W_CIN),
+                      32, 16, 64);                                                                                // dDout
         }
         sync_mma();
         {
@@ -800,7 +823,7 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
             v[0] += ddout0 * DELTA_SCALE;
             // delta at the density output replaces the colour input's first 16 columns
 #pragma unroll
-            for (int cc = 0; cc < 16; cc += 8) tc::st_chunk8(tXC, tid, cc, 32, v + cc);
+            for (int cc = 0; cc < 16; cc += 8) tc::st_chunk8_hilo(tXC, tLO, tid, cc, 32, v + cc);
             {
                 const float sum = warp_sum16(v);
                 if ((tid & 1) == 0) atomicAdd(bgrad + ((tid >> 1) & 15), sum);
@@ -810,27 +833,31 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         handoff();
         if (tid == 0) {
             gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::XC), 32, true, 64, 16, 128, acc0);               // dWd_out^T
-            gemm(tmem + PL::ACC, G(PL::XC), 32, false, S(PL::W_HI + PL::W_DOUT), 64, true, 128, 64, 16, 0);     // dH_last
+            gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::LO), 32, true, 64, 16, 128, 1);
+            gemm_bwd3(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_DOUT), S(PL::W_LO + PL::W_DOUT),
+                      64, 64, 16);                                                                                // dH_last
         }
         sync_mma();
         {
-            epi_relu_mask(tmem, PL::ACC, 64, tH(ND - 1), 64);
+            epi_relu_mask(tmem, PL::ACC, 64, tH(ND - 1), tLO, 64);
         }
         if (ND >= 2) {
             handoff();
             if (tid == 0) {
-                gemm(tmem + PL::DW_D01, hlast, 64, true, G(PL::HD), 64, true, 64, 64, 128, acc0);               // dWd_01
-                gemm(tmem + PL::B_D1, hlast, 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbd_1
-                gemm(tmem + PL::ACC, hlast, 64, false, S(PL::W_HI + PL::W_D01), 64, true, 128, 64, 64, 0);       // dH_0
+                gemm_wgrad2(tmem + PL::DW_D01, hlast, G(PL::LO), G(PL::HD), 64, 64, acc0);                      // dWd_01
+                gemm_wgrad2(tmem + PL::B_D1, hlast, G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbd_1
+                gemm_bwd3(tmem + PL::ACC, hlast, G(PL::LO), 64, S(PL::W_HI + PL::W_D01), S(PL::W_LO + PL::W_D01),
+                          64, 64, 64);                                                                            // dH_0
             }
             sync_mma();
-            epi_relu_mask(tmem, PL::ACC, 64, tH(0), 64);
+            epi_relu_mask(tmem, PL::ACC, 64, tH(0), tLO, 64);
         }
         handoff();
         if (tid == 0) {
-            gemm(tmem + PL::DW_DIN, G(PL::HD), 64, true, G(PL::X0), LPOS, true, 64, LPOS, 128, acc0);           // dWd_in
-            gemm(tmem + PL::B_D0, G(PL::HD), 64, true, S(PL::ONES), 8, true, 64, 8, 128, acc0);                 // dbd_0
-            gemm(tmem + PL::ACC, G(PL::HD), 64, false, S(PL::W_HI + PL::W_DIN), LPOS, true, 128, LPOS, 64, 0);   // hash grads
+            gemm_wgrad2(tmem + PL::DW_DIN, G(PL::HD), G(PL::LO), G(PL::X0), LPOS, LPOS, acc0);                  // dWd_in
+            gemm_wgrad2(tmem + PL::B_D0, G(PL::HD), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbd_0
+            gemm_bwd3(tmem + PL::ACC, G(PL::HD), G(PL::LO), 64, S(PL::W_HI + PL::W_DIN), S(PL::W_LO + PL::W_DIN),
+                      LPOS, LPOS, 64);                                                                            // hash grads
         }
         sync_mma();
         dw_started = true;

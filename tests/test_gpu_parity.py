@@ -365,8 +365,8 @@ def test_transfer_formats_match_oracle(oracle, fmt):
     the step's activations and deltas quantised.  fp32 MLP against the oracle (pinned against the
     reference kernels compiled with TRANSFER_FMT=16 / 8): MLP gradients within rel-L2 1e-4 (fp16) /
     1e-3 (fp8: a value within rounding of a 3-bit-mantissa step boundary may land on the other
-    step), the table gradient (not quantised) within 1e-4, and the quantisation must matter: the
-    fp32-transfer gradient differs from the quantised one."""
+    step), the table gradient (not quantised) within 1e-4, and the device's gradient is at least 5x
+    closer to the quantised oracle than to the unquantised one."""
     g = make_geometry(**GEOMS["cfg1"])
     ctx = fn.Context(g, transfer_fmt=fmt)
     blob, table, occ = init_blob(g, 7), init_table(g, 7), init_occ(g, 7)
@@ -389,8 +389,11 @@ def test_transfer_formats_match_oracle(oracle, fmt):
     tgo, mgo = res[fn.TRANSFER_FORMATS[fmt]]
     tol = 1e-4 if fmt == "fp16" else 1e-3
     assert rel_l2(grads[:table.size], tgo) < 1e-4
-    assert rel_l2(grads[table.size:], mgo) < tol, rel_l2(grads[table.size:], mgo)
-    assert rel_l2(mgo, res[32][1]) > 10 * tol          # the format changes the gradient
+    e_q = rel_l2(grads[table.size:], mgo)
+    assert e_q < tol, e_q
+    # the quantisation is what the device reproduces: it is much closer to the quantised oracle
+    # than to the unquantised one
+    assert 5 * e_q < rel_l2(grads[table.size:], res[32][1]), (e_q, rel_l2(grads[table.size:], res[32][1]))
     assert ctx.status() == 0
 
 
