@@ -1030,22 +1030,21 @@ __global__ void __launch_bounds__(256) encode_stage_kernel(const DevConfig c, co
         }
         unsigned char* tile = x0_out + (i >> 7) * (int64_t)(2 * HALF);
         const int r = (int)(i & 127);
-        __half hi[F], lo[F];
+        uint32_t hi[F / 2], lo[F / 2];
 #pragma unroll
-        for (int f = 0; f < F; ++f) {
-            const float x = v[f] * INPUT_SCALE;
-            hi[f] = tc::to_half_sat(x);
-            lo[f] = tc::to_half_sat(x - __half2float(hi[f]));
+        for (int f = 0; f < F; f += 2) {
+            const float x0 = v[f] * INPUT_SCALE, x1 = v[f + 1] * INPUT_SCALE;
+            hi[f / 2] = tc::pack_half2_sat(x0, x1);
+            const float2 b = tc::unpack_half2(hi[f / 2]);
+            lo[f / 2] = tc::pack_half2_sat(x0 - b.x, x1 - b.y);
         }
         const uint32_t off = tc::tile_off(r, lvl * F, LPOS);
         if constexpr (F == 2) {
-            *reinterpret_cast<__half2*>(tile + off) = __halves2half2(hi[0], hi[1]);
-            *reinterpret_cast<__half2*>(tile + HALF + off) = __halves2half2(lo[0], lo[1]);
+            *reinterpret_cast<uint32_t*>(tile + off) = hi[0];
+            *reinterpret_cast<uint32_t*>(tile + HALF + off) = lo[0];
         } else {
-            __half2 h[2] = {__halves2half2(hi[0], hi[1]), __halves2half2(hi[2], hi[3])};
-            __half2 l[2] = {__halves2half2(lo[0], lo[1]), __halves2half2(lo[2], lo[3])};
-            *reinterpret_cast<uint2*>(tile + off) = *reinterpret_cast<uint2*>(h);
-            *reinterpret_cast<uint2*>(tile + HALF + off) = *reinterpret_cast<uint2*>(l);
+            *reinterpret_cast<uint2*>(tile + off) = make_uint2(hi[0], hi[1]);
+            *reinterpret_cast<uint2*>(tile + HALF + off) = make_uint2(lo[0], lo[1]);
         }
     }
 }

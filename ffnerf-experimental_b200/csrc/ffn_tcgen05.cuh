@@ -117,12 +117,25 @@ __device__ __forceinline__ __half to_half_sat(float x) {
     return __float2half_rn(fminf(fmaxf(x, -65504.0f), 65504.0f));
 }
 
+// Two fp32 values -> one packed fp16 pair (x0 in the low half), rounded to nearest even; magnitudes
+// above 65504 saturate to +-65504, a NaN stays NaN.  One conversion instruction for both values.
+__device__ __forceinline__ uint32_t pack_half2_sat(float x0, float x1) {
+    uint32_t r;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+__device__ __forceinline__ float2 unpack_half2(uint32_t h) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
 // Stores 8 values as one 16-byte core-matrix row chunk.
 __device__ __forceinline__ void st_chunk8(unsigned char* tile, int r, int c0, int cols, const float* v) {
-    __half2 h[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = __halves2half2(to_half_sat(v[2 * i]), to_half_sat(v[2 * i + 1]));
-    *reinterpret_cast<uint4*>(tile + tile_off(r, c0, cols)) = *reinterpret_cast<uint4*>(h);
+    uint4 h;
+    h.x = pack_half2_sat(v[0], v[1]);
+    h.y = pack_half2_sat(v[2], v[3]);
+    h.z = pack_half2_sat(v[4], v[5]);
+    h.w = pack_half2_sat(v[6], v[7]);
+    *reinterpret_cast<uint4*>(tile + tile_off(r, c0, cols)) = h;
 }
 // Stores 8 values as a compensated pair of fp16 chunks: hi = fp16(x) into `hi_tile`, lo = fp16(x - hi)
 // into `lo_tile` (same position), so that hi + lo carries about 22 significant bits.  A product
@@ -132,16 +145,16 @@ __device__ __forceinline__ void st_chunk8(unsigned char* tile, int r, int c0, in
 // theoretical peak", IJHPCA 2022); the lo*lo' term is below fp32 rounding and is left out.
 __device__ __forceinline__ void st_chunk8_hilo(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
                                                const float* v) {
-    __half2 h[4], l[4];
+    uint32_t h[4], l[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const __half a = to_half_sat(v[2 * i]), b = to_half_sat(v[2 * i + 1]);
-        h[i] = __halves2half2(a, b);
-        l[i] = __halves2half2(to_half_sat(v[2 * i] - __half2float(a)), to_half_sat(v[2 * i + 1] - __half2float(b)));
+        h[i] = pack_half2_sat(v[2 * i], v[2 * i + 1]);
+        const float2 b = unpack_half2(h[i]);
+        l[i] = pack_half2_sat(v[2 * i] - b.x, v[2 * i + 1] - b.y);
     }
     const uint32_t off = tile_off(r, c0, cols);
-    *reinterpret_cast<uint4*>(hi_tile + off) = *reinterpret_cast<uint4*>(h);
-    *reinterpret_cast<uint4*>(lo_tile + off) = *reinterpret_cast<uint4*>(l);
+    *reinterpret_cast<uint4*>(hi_tile + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo_tile + off) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 __device__ __forceinline__ void ld_chunk8(const unsigned char* tile, int r, int c0, int cols, float* v) {
     uint4 u = *reinterpret_cast<const uint4*>(tile + tile_off(r, c0, cols));
