@@ -142,7 +142,7 @@ int check_config(const ffn_config* g, std::string* why) {
     for (int l = 0; l < FFN_N_LEVELS; ++l) {
         if (g->level_log2[l] < 1 || g->level_log2[l] > 24) { *why = "per-level table size must be 2^1..2^24"; return FFN_E_CONFIG; }
         if (g->level_offset[l] != expect) { *why = "level offsets must be the running sum of the level sizes"; return FFN_E_CONFIG; }
-        if (g->level_res[l] < 2) { *why = "level resolution must be >= 2"; return FFN_E_CONFIG; }
+        if (g->level_res[l] < 2 || g->level_res[l] > (1 << 20)) { *why = "level resolution must be 2..2^20"; return FFN_E_CONFIG; }
         expect += 1ull << g->level_log2[l];
     }
     if (expect * (uint64_t)g->F >= (1ull << 32)) { *why = "hash table too large (>= 2^32 floats)"; return FFN_E_CONFIG; }

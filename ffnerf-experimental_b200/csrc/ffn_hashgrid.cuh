@@ -47,14 +47,14 @@ __device__ __forceinline__ float sigmoid_soft(float x) {
 // Per-level trilinear corners (ffnerf_OG.cl:1308-1338)
 struct Corner8 { float w[8]; uint32_t base[8]; };
 template <int F>
-__device__ __forceinline__ void level_corners(const DevConfig& c, V3 p, int lvl, Corner8& k, uint32_t* cell_key = nullptr) {
+__device__ __forceinline__ void level_corners(const DevConfig& c, V3 p, int lvl, Corner8& k, uint64_t* cell_key = nullptr) {
     const int R = c.level_res[lvl];
     const float Rf = (float)R;
     const float ux = fm(p.x, Rf), uy = fm(p.y, Rf), uz = fm(p.z, Rf);
     const int ix0 = iclamp((int)floorf(ux), 0, R - 2);
     const int iy0 = iclamp((int)floorf(uy), 0, R - 2);
     const int iz0 = iclamp((int)floorf(uz), 0, R - 2);
-    if (cell_key) *cell_key = (uint32_t)ix0 | ((uint32_t)iy0 << 11) | ((uint32_t)iz0 << 22);   // R <= 2048
+    if (cell_key) *cell_key = (uint64_t)ix0 | ((uint64_t)iy0 << 21) | ((uint64_t)iz0 << 42);   // exact: R < 2^21
     const float fx = fs(ux, (float)ix0), fy = fs(uy, (float)iy0), fz = fs(uz, (float)iz0);
     const float wx[2] = {fs(1.0f, fx), fx}, wy[2] = {fs(1.0f, fy), fy}, wz[2] = {fs(1.0f, fz), fz};
     const uint32_t mask = (1u << c.level_log2[lvl]) - 1u;

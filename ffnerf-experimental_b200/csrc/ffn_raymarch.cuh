@@ -272,6 +272,8 @@ struct RayTile {
     bool valid, train, probe;
     V3 o, d, bmin, bmax, bsize, inv_box;
     float Gf, inv_n;
+    bool has_target;                 // `target` holds this ray's target (loaded ahead by the caller)
+    float4 target;
 };
 
 // Sampler (ffnerf_OG.cl:1002-1250): stratified candidates, occupancy weights, exact Blelloch
@@ -505,7 +507,8 @@ __device__ __forceinline__ void ray_composite(const StepArgs& a, const RayTile& 
         const float cf[3] = {fa(total.y, fm(T_final, bg[0])), fa(total.z, fm(T_final, bg[1])),
                              fa(total.w, fm(T_final, bg[2]))};
         float4 tg = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid && a.targets) tg = a.targets[ray_idx];
+        if (R.has_target) tg = R.target;
+        else if (valid && a.targets) tg = a.targets[ray_idx];
         const float tv[3] = {tg.x, tg.y, tg.z};
         float gr[3];
 #pragma unroll

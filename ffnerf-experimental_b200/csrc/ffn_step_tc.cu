@@ -118,17 +118,20 @@ __device__ __forceinline__ void stage_weight(unsigned char* hi, unsigned char* l
     }
 }
 
-// Issues ACC (+)= A * B for a K range in steps of 16 (one thread).
+// Issues ACC (+)= A * B for a K range in steps of 16 (one thread).  The descriptors are formed once:
+// the descriptor of the tile advanced by k steps is the first one plus (k * step) >> 4 in its start
+// field, which cannot carry out of its 14 bits (shared-memory addresses are below 2^18).
 __device__ __forceinline__ void gemm(uint32_t d, uint32_t a, int a_cols, bool a_mn, uint32_t b, int b_cols, bool b_mn,
                                      int M, int N, int K, uint32_t accumulate) {
     const uint32_t idesc = tc::idesc_f16(M, N, a_mn, b_mn);
     const uint32_t a_step = a_mn ? 2u * (uint32_t)(a_cols / 8) * 128u : 256u;
     const uint32_t b_step = b_mn ? 2u * (uint32_t)(b_cols / 8) * 128u : 256u;
-    for (int k = 0; k < K / 16; ++k) {
-        const uint64_t ad = a_mn ? tc::desc_mnmajor(a + k * a_step, a_cols) : tc::desc_kmajor(a + k * a_step, a_cols);
-        const uint64_t bd = b_mn ? tc::desc_mnmajor(b + k * b_step, b_cols) : tc::desc_kmajor(b + k * b_step, b_cols);
-        tc::mma_f16(d, ad, bd, idesc, (k > 0 || accumulate) ? 1u : 0u);
-    }
+    const uint64_t ad0 = a_mn ? tc::desc_mnmajor(a, a_cols) : tc::desc_kmajor(a, a_cols);
+    const uint64_t bd0 = b_mn ? tc::desc_mnmajor(b, b_cols) : tc::desc_kmajor(b, b_cols);
+#pragma unroll
+    for (int k = 0; k < K / 16; ++k)
+        tc::mma_f16(d, ad0 + (uint64_t)((k * a_step) >> 4), bd0 + (uint64_t)((k * b_step) >> 4), idesc,
+                    (k > 0 || accumulate) ? 1u : 0u);
 }
 
 // Forward layer with compensated operands: ACC = Ah*Wh^T + Ah*Wl^T + Al*Wh^T (both K-major; one
@@ -267,13 +270,16 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
 
 // Scatter of one level's hash-grid gradient (ffnerf_OG.cl:2090-2173): the thread's F raw feature
 // gradients `gl` become (coef_l * g) * w_c at the 8 trilinear corners, added with vector atomics.
-// On the coarse levels (lvl < DEDUP_LEVELS) the lanes of a warp -- consecutive samples of one ray --
-// often sit in the same grid cell and would add to the same 8 table entries: such lanes are grouped
-// (match on the cell) and the group's first lane adds the group's sums with one set of atomics.  The
-// sums are formed by shuffles when every group is a run of consecutive lanes, else through
-// `scratch` (each lane writes its 8 x F contributions to its shared-memory row, 8 F floats per
-// thread, and the first lane adds the other rows).  Finer levels add directly.
-constexpr int DEDUP_LEVELS = 10;
+// The lanes of a warp -- consecutive samples of one ray -- often sit in the same grid cell and would
+// add to the same 8 table entries (on the coarse levels nearly always; on the fine ones where the
+// occupancy-guided sampler packs samples densely): such lanes are grouped (match on the cell) and the
+// group's first lane adds the group's sums with one set of atomics.  The sums are formed by shuffles
+// when every group is a run of consecutive lanes, else through `scratch` (each lane writes its 8 x F
+// contributions to its shared-memory row, 8 F floats per thread, and the first lane adds the other
+// rows).  Levels from DEDUP_LEVELS up would add directly; merging on all 16 levels measured fastest
+// (cfg3 step 1.80 ms with the 10 coarsest, 1.74 ms with all 16, 1.86 ms with none): the reductions
+// themselves, not the matching, are the scatter's cost.
+constexpr int DEDUP_LEVELS = L;
 template <int F>
 __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restrict__ grad, V3 p, int lvl,
                                               const float* gl, const float* coef, float* scratch) {
@@ -289,7 +295,7 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
     }
     if (!any) return;
     Corner8 k;
-    uint32_t key;
+    uint64_t key;
     level_corners<F>(c, p, lvl, k, &key);
     unsigned grp = 1u << lid;
     if (lvl < DEDUP_LEVELS) {
@@ -593,17 +599,20 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
     float2 nx_tdt = make_float2(0.f, 0.f);
     uint4 nx_rst = make_uint4(0u, 0u, 0u, 0u);
     float4 nx_ro = make_float4(0.f, 0.f, 0.f, 0.f), nx_rd = make_float4(0.f, 0.f, 1.f, 0.f);
+    float4 nx_tg = make_float4(0.f, 0.f, 0.f, 0.f);
     auto prefetch = [&](int t) {
         const uint32_t ri = (uint32_t)t * rays_per_tile + rl;
         nx_tdt = make_float2(0.f, 0.f);
         nx_rst = make_uint4(0u, 0u, 0u, 0u);
         nx_ro = make_float4(0.f, 0.f, 0.f, 0.f);
         nx_rd = make_float4(0.f, 0.f, 1.f, 0.f);
+        nx_tg = make_float4(0.f, 0.f, 0.f, 0.f);
         if (!MLPB && ri < a.n_rays) {
             nx_tdt = a.tdt_stage[(size_t)t * 128 + tid];
             nx_rst = a.ray_stage[ri];
             nx_ro = a.rays[2 * ri];
             nx_rd = a.rays[2 * ri + 1];
+            if (lid == 0 && a.targets) nx_tg = a.targets[ri];   // read by the ray's lane 0 in the compositing
         }
         constexpr int HALF = 128 * LPOS * 2;   // bytes of the hi (and of the lo) tile
         const unsigned char* src = a.x0_stage + (size_t)t * PL::X0_STAGE_BYTES;
@@ -635,7 +644,8 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         }
         const V3 o = v3(ro.x, ro.y, ro.z), d = v3(rd.x, rd.y, rd.z);
         RayTile R{sCand, sCdf, sTs, sDTs, sTr, sKey, sSeg, sAffS, sAffE, sChg, sRay, tid, spr, rl, lid, rbase,
-                  ray_idx, ray_id, valid, train, probe, o, d, bmin, bmax, bsize, inv_box, (float)c.G, 1.0f / (float)spr};
+                  ray_idx, ray_id, valid, train, probe, o, d, bmin, bmax, bsize, inv_box, (float)c.G, 1.0f / (float)spr,
+                  STAGED, nx_tg};
         bool hit;
         int idx_sel = 0;
         if constexpr (STAGED) {

@@ -86,9 +86,13 @@ class Event:
         self._start = start
         self._end = torch.cuda.Event(enable_timing=start is not None)
         self._end.record(stream)
+        self._on_complete = None      # host work that completes the command (a staged copy's delivery)
 
     def wait(self):
         self._end.synchronize()
+        if self._on_complete is not None:
+            done, self._on_complete = self._on_complete, None
+            done()
 
     @property
     def command_execution_status(self):
@@ -142,9 +146,13 @@ class CommandQueue:
         self.context = ctx
         self.device = ctx.device
         self.stream = stream or torch.cuda.Stream(device=ctx.device.index)
+        self._pending = []            # events whose host-side delivery is still due
 
     def finish(self):
         self.stream.synchronize()
+        pending, self._pending = self._pending, []
+        for e in pending:
+            e.wait()
 
     def wait_for(self, events):
         for e in events or []:
@@ -320,13 +328,20 @@ class RayBatch:
         rb.rays_buf = torch.zeros((rb.num_rays, 8), dtype=torch.float32, device=dev)
         rb.targets_buf = torch.zeros((rb.num_rays, 4), dtype=torch.float32, device=dev)
         rb.out_buf = torch.zeros((rb.num_rays, 4), dtype=torch.float32, device=dev)
-        for k, w in (("rays", 8), ("targets", 4), ("out", 4)):
+        for k, w in (("rays", 8), ("targets", 4)):
             rb._stage[k] = torch.zeros((rb.num_rays, w), dtype=torch.float32).pin_memory()
             rb._stage[k + "_ev"] = None
+        # two pinned slots for read-backs into pageable arrays, so that a non-blocking download can be
+        # in flight while the next step runs
+        rb._stage["out"] = [torch.zeros((rb.num_rays, 4), dtype=torch.float32).pin_memory() for _ in range(2)]
+        rb._stage["out_ev"] = [None, None]
+        rb._stage["out_i"] = 0
         if with_host_arrays:
             rb.rays_host = np.empty((rb.num_rays,), dtype=rb.ray_dtype)
             rb.targets_host = np.empty((rb.num_rays, 4), dtype=np.float32)
-            rb.out_host = np.empty((rb.num_rays, 4), dtype=np.float32)
+            # pinned, so that a download into it is one asynchronous copy, as an OpenCL read is
+            rb._stage["out_host"] = torch.zeros((rb.num_rays, 4), dtype=torch.float32).pin_memory()
+            rb.out_host = rb._stage["out_host"].numpy()
         return rb
 
     def _h2d(self, key: str, arr: np.ndarray, dst, wait: bool, wait_for=None) -> Event:
@@ -373,12 +388,33 @@ class RayBatch:
             if out.shape != (self.num_rays, 4):
                 raise ValueError(f"out must be shape ({self.num_rays},4), got {out.shape}")
         self.queue.wait_for(wait_for)
-        stage = self._stage["out"]
-        with torch.cuda.stream(self.queue.stream):
-            stage.copy_(self.out_buf, non_blocking=True)
-            ev = Event(self.queue.stream)
-        ev.wait()     # the host array is only valid once the copy has landed
-        out[...] = stage.numpy()
+        # As with the reference's non-blocking read, `out` holds the colours once the returned event has
+        # completed (on return with wait=True).  A pinned `out` (out_host is) receives one asynchronous
+        # copy; a pageable one is staged through a pinned slot and filled when the event is waited on
+        # or the queue finishes.
+        dst = torch.from_numpy(out)
+        if dst.is_pinned():
+            with torch.cuda.stream(self.queue.stream):
+                dst.copy_(self.out_buf, non_blocking=True)
+                ev = Event(self.queue.stream)
+        else:
+            i = self._stage["out_i"]
+            self._stage["out_i"] = i ^ 1
+            prev = self._stage["out_ev"][i]
+            if prev is not None:
+                prev.wait()           # that slot's previous download has been delivered
+            stage = self._stage["out"][i]
+            with torch.cuda.stream(self.queue.stream):
+                stage.copy_(self.out_buf, non_blocking=True)
+                ev = Event(self.queue.stream)
+
+            def deliver(out=out, stage=stage):
+                out[...] = stage.numpy()
+            ev._on_complete = deliver
+            self._stage["out_ev"][i] = ev
+            self.queue._pending.append(ev)
+        if wait:
+            ev.wait()
         return out, ev
 
     def ensure_dummy_targets(self) -> np.ndarray:
@@ -1087,7 +1123,10 @@ class Nerf:
             print(f"[I]: ev_ff   do_train  [ms]: {event_ms(ev_ff):.3f}")
             print("          debug vals -", list(out[0:4, 3]))
         if return_output:
-            out, ev_dwn = io.download_out(wait=True, wait_for=[ev_last])
+            # the reference enqueues the read and returns (ffnerf_tools.py:1533-1540)
+            out, ev_dwn = io.download_out(wait=False, wait_for=[ev_last])
+            if wait:
+                ev_dwn.wait()
             return out, ev_dwn
         if wait:
             ev_last.wait()

@@ -4,9 +4,17 @@ same step read it (ffnerf_OG.cl:2155-2168) -- against the CPU oracle in sequenti
 (rays in order, each update applied at once: one legal schedule of the same race).
 
 Contracts:
-  * one step: the table change matches the oracle's within rel-L2 1e-3 (fp32 MLP) / 1e-2 (fp16
-    tensor-core MLP, the contract's gradient tolerance), the gradient buffer's table part stays zero;
+  * one step: the table change matches the oracle's within rel-L2 1e-3 (both MLP precisions), the
+    gradient buffer's table part stays zero;
   * an Adam table refuses immediate updates.
+The table starts at amplitude 1e-3 (the reference initialises at 1e-4).  At the helpers' usual 0.1
+the comparison measures float rounding, not the update: every one of a step's many small adds into
+an entry of size ~0.1 rounds to that entry's ulp, so the reference's per-sample adds (the oracle's
+sequential mode) and one exact sum of the same contributions (its deferred mode) end 1.2e-2 apart
+(rel-L2 of the change), and the device, which sums the contributions of a cell's samples before one
+add, sits between the two.  At 1e-3 that rounding is 1e-4 of the change and the remaining
+difference is the schedule's: which adds a gather sees (the oracle's sequential mode in forward and
+in reverse ray order: 4.8e-4 apart).
 (100-step training runs in this mode are in test_gpu_train100.py.)
 """
 import numpy as np
@@ -21,7 +29,7 @@ from oracle import OrcStep, make_orc_config
 import ffn_native as fn
 
 GEOM = dict(F=2, ND=1, NC=2, spr=64, G=64, log2_entries=14, rmax=512.0)
-TOL = {"fp32": (1e-3,), "fp16": (1e-2,)}
+TOL = {"fp32": (1e-3,), "fp16": (1e-3,)}
 MLP_GRAD_TOL = {"fp32": 1e-3, "fp16": 1e-2}
 
 
@@ -29,10 +37,10 @@ def _cuda(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def _make(prec, seed, n_rays):
+def _make(prec, seed, n_rays, table_amp=1e-1):
     g = make_geometry(**GEOM)
     ctx = fn.Context(g, mlp_precision=prec)
-    blob, table, occ = init_blob(g, seed), init_table(g, seed), init_occ(g, seed)
+    blob, table, occ = init_blob(g, seed), init_table(g, seed, table_amp), init_occ(g, seed)
     ctx.tensor(fn.BUF_PARAMS).copy_(_cuda(blob))
     ctx.tensor(fn.BUF_TABLE).copy_(_cuda(table))
     ctx.tensor(fn.BUF_OCC_IN).copy_(_cuda(occ.view(np.int32)))
@@ -43,7 +51,7 @@ def _make(prec, seed, n_rays):
 
 @pytest.mark.parametrize("prec", ["fp32", "fp16"])
 def test_immediate_one_step(oracle, prec):
-    g, ctx, blob, table, occ, rays, tg = _make(prec, 21, 128)
+    g, ctx, blob, table, occ, rays, tg = _make(prec, 21, 128, table_amp=1e-3)
     n, lr_f, seed = rays.shape[0], np.float32(1e-2), 4242
     cfg = make_orc_config(g, table_mode=1)
     tab_o = table.copy()

@@ -180,7 +180,9 @@ class OracleModel:
             mg += m_
         if occ_s > 0.0:                           # proposals are written only while updates are live
             for _, _, ost in res:
-                self.occ_st = nibble_max(self.occ_st, ost)
+                d = np.nonzero(ost != self.occ_st)[0]   # a step proposes into few words: merge those
+                if d.size:
+                    self.occ_st[d] = nibble_max(self.occ_st[d], ost[d])
         if h.maintenance_due(h.steps_trained, occ_s):
             self.o.decay(self.occ_in, self.occ_st, h.decay_q24(occ_s), seed)
         self.o.mlp_adam(self.cfg, self.blob, mg, self.m, self.v, float(h.lr_t(lr_f)), crl, float(h.ADAM_BETA1),
