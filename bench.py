@@ -641,6 +641,7 @@ def main():
         return
 
     import torch
+    import ffn_native
     import ffnerf_tools as ft
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -732,6 +733,30 @@ def main():
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b in pairs), outs
 
+    def exchange_alone(k: int):
+        """Device time of ffn_dp_reduce_apply with no forward/backward skew between the ranks (k
+        back-to-back calls between one event pair, max over ranks), and the bytes that cross NVLink per
+        direction per rank: peer form, its shard of every peer's gradients in and the updated shard
+        out to every peer, 2 (W - 1) / W of the buffer; NVSwitch form, the reduced shard in and every
+        peer's stored shard in, about the buffer once."""
+        nat = nerf.native
+        stp = ffn_native.make_step(lr_f=0.0, lr_t=0.0, rng_u32=1, spr=spr)
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(queue.stream)
+        for _ in range(k):
+            nat.dp_reduce_apply(stp, queue.stream)
+        b.record(queue.stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(a.elapsed_time(b) / k)
+        buf = nat.grad_buffer()[1] * 4          # bytes of [table | MLP] gradients
+        per_dir = buf if nerf.dp.nvls else 2.0 * (world - 1) / world * buf
+        return {"form": "nvls" if nerf.dp.nvls else "p2p", "alone_ms": ms, "in_step_ms": None,
+                "bytes_per_direction": per_dir, "gbs_per_direction": per_dir / (ms * 1e-3) / 1e9,
+                "link_gbs": 770.0, "frac_of_link": per_dir / (ms * 1e-3) / 1e9 / 770.0,
+                "note": "link_gbs: measured peer-copy rate per direction per GPU on this pool"}
+
     def e2e_steps(n_steps: int):
         """End to end through the public API, as a user pipelines it: per step the L2 flush, the
         pinned-host uploads of the step's rays and targets, Nerf.step and the non-blocking colour
@@ -788,6 +813,9 @@ def main():
         ms_warm, _ = timed_steps(args.steps, args.warmup, host=False, flush=False)
         barrier()
         ms_warm = max_over_ranks(ms_warm)
+        # (2b) the fused exchange alone: back-to-back calls, every rank arriving at once, with a zero
+        # learning rate (the table does not change; the gradients are recomputed by the next step)
+        ex_alone = exchange_alone(10) if (nerf.dp is not None and nerf.dp.fused) else None
         # (3) end to end through the public API: pinned-host uploads, Nerf.step, colour download
         if not args.no_e2e:
             io = ft.RayBatch.init(ctx, queue, n_loc, spr)
@@ -823,8 +851,8 @@ def main():
             print(json.dumps({"metric": METRIC, "value": n_glob * spr * args.steps / (ms_total * 1e-3),
                               "unit": "samples/s", "note": "profiling run (no e2e, no baseline)",
                               "gpu_launches": launches, "fused_ms": fb_ms, "exchange_ms": ex_ms,
-                              "exchange": ("nvls" if nerf.dp.nvls else "p2p" if nerf.dp.fused else "nccl")
-                              if nerf.dp is not None else None,
+                              "exchange": (dict(ex_alone, in_step_ms=ex_ms) if ex_alone else
+                                           "nccl" if nerf.dp is not None else None),
                               "host_ms_per_step": host_ms,
                               "ms_per_step": ms_total / args.steps}), flush=True)
         if dist is not None:
@@ -875,6 +903,7 @@ def main():
             "mlp_fp32": fp32_line,
             "host_ms_per_step": host_ms,
             "exchange_ms": ex_ms,
+            "exchange": dict(ex_alone, in_step_ms=ex_ms) if ex_alone else None,
             "roofline": {"bound": "hbm", "kernel": ("forward/backward group: sample_stage_kernel + encode_stage_kernel + "
                                                     "fused_step_tc_kernel<staged> + reduce_partials" if args.mlp == "fp16"
                                                     else "fused_step_kernel + reduce_partials"),

@@ -109,9 +109,11 @@ def synthetic_scene_views(workload: str = "cfg1", seed: int = 0, device: str = "
 
 
 def synthetic_nerf(workload: str = "cfg1", mlp_precision: str = "fp16", seed: int = 0,
-                   training_dir: str | None = None, table_update: str = "immediate", host_only: bool = False):
+                   training_dir: str | None = None, table_update: str = "immediate", host_only: bool = False,
+                   background: str = "random"):
     """A fresh ffnerf_tools.Nerf for the synthetic scene's geometry: hash L=16 F=2 (T and Rmax of
-    the workload), ND=1, NC=2, random background, box [-1, 1]^3, near clip 0.3, rng seed 777+seed.
+    the workload), ND=1, NC=2, `background` ("random" by default), box [-1, 1]^3, near clip 0.3, rng
+    seed 777+seed.
     host_only: no device or queue (the host state, seeds and schedules only)."""
     import tempfile
     import ffnerf_tools as ft
@@ -124,7 +126,7 @@ def synthetic_nerf(workload: str = "cfg1", mlp_precision: str = "fp16", seed: in
     tdir = training_dir or tempfile.mkdtemp(prefix="ffn_train_")
     return ft.Nerf(ctx, queue, training_dir=tdir, model_id=f"synthetic_{workload}", transfer_fmt="fp32",
                    table_size_entries=16 << wl["log2T"], f_per_level=2, occ=occ, rng_seed=777 + seed,
-                   background="random", finest_resolution=wl["rmax"], nd=1, nc=2, mlp_precision=mlp_precision,
+                   background=background, finest_resolution=wl["rmax"], nd=1, nc=2, mlp_precision=mlp_precision,
                    verbose=False, table_update=table_update)
 
 

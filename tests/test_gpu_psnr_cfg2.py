@@ -4,7 +4,9 @@ Protocol: the synthetic cfg2 scene (56 views at 450x800 from a camera ring, hash
 Rmax 2048, occupancy 128^3), 5,000 training steps of 512 rays x 64 samples from the same initial
 state (the reference's init draws from one seed), the same batches (uniformly drawn pixels, host
 rays of rays_targets_from_indices), the same schedules (run_ffnerf_OG.py:1356-1365: occupancy
-updates live after step 1,500, decay every 32nd step) and the same per-step seeds, trained by
+updates live after step 1,500, decay every 32nd step) and the same per-step seeds, a black
+background (the scene's images are rendered over black; with a random training background the
+model has to build black occluders and ends near the constant-colour baseline), trained by
   * the device through ffnerf_tools.Nerf.step with the tensor-core MLP (the configuration's fp16
     MLP: compensated fp16 operand pairs, fp32 accumulation) and the immediate table update;
   * the oracle with the deferred table update (OracleModel of test_gpu_psnr_reference.py).
@@ -12,7 +14,7 @@ Each model renders the same 2,048 seeded pixels of every view (114,688 rays; vie
 seed i) with its own inference path; the PSNR over those pixels is compared.
 Contract: |PSNR(device) - PSNR(oracle)| <= 0.2 dB.
 
-The oracle's 5,000 steps take 15-20 minutes of host-core time, so the test runs only with
+The oracle's 5,000 steps take 20-30 minutes of host-core time, so the test runs only with
 FFNERF_LONG_TESTS=1.  The two halves also run as separate commands, so that the device half runs
 on a GPU machine and the oracle half on any machine with the oracle built:
     python tests/test_gpu_psnr_cfg2.py device run.npz      # trains and evaluates on the GPU
@@ -87,7 +89,7 @@ def run_device(workdir, steps=STEPS_CFG2):
     from test_gpu_psnr_reference import train_device
     data = trainer.synthetic_scene_views("cfg2", 0)
     images, cams, K, W, H = data
-    nerf = trainer.synthetic_nerf("cfg2", "fp16", 0, str(Path(workdir) / "dev"))
+    nerf = trainer.synthetic_nerf("cfg2", "fp16", 0, str(Path(workdir) / "dev"), background="black")
     t0 = time.time()
     train_device(nerf, data, steps)
     assert nerf.native.status() == 0
@@ -102,8 +104,8 @@ def run_oracle(data, u, v, workdir, steps=STEPS_CFG2, threads=None):
     import trainer
     from test_gpu_psnr_reference import OracleModel, train_cpu
     images, cams, K, W, H = data
-    orc = OracleModel(trainer.synthetic_nerf("cfg2", "fp32", 0, str(Path(workdir) / "orc"), host_only=True),
-                      threads=threads)
+    orc = OracleModel(trainer.synthetic_nerf("cfg2", "fp32", 0, str(Path(workdir) / "orc"), host_only=True,
+                                             background="black"), threads=threads)
     t0 = time.time()
     train_cpu(orc, data, steps)
     p = subset_psnr(oracle_colours(orc, cams, K, W, H, u, v), images, u, v)
@@ -115,12 +117,12 @@ def run_oracle(data, u, v, workdir, steps=STEPS_CFG2, threads=None):
 def test_psnr_cfg2_matches_oracle(tmp_path):
     """|PSNR(device, fp16 tensor-core MLP) - PSNR(deferred oracle)| <= 0.2 dB after 5,000 cfg2 steps."""
     if os.environ.get("FFNERF_LONG_TESTS") != "1":
-        pytest.skip("long run (15-20 min of host-core time for the oracle): set FFNERF_LONG_TESTS=1")
+        pytest.skip("long run (20-30 min of host-core time for the oracle): set FFNERF_LONG_TESTS=1")
     pytest.importorskip("torch")
     data, u, v, p_dev = run_device(tmp_path)
     p_orc = run_oracle(data, u, v, tmp_path)
     print(f"PSNR after {STEPS_CFG2} cfg2 steps: device {p_dev:.3f} dB, deferred oracle {p_orc:.3f} dB")
-    assert p_orc > 12.0, p_orc                     # the scene was learned
+    assert p_orc > 15.0, p_orc          # the scene was learned (a constant colour scores 11.6 dB)
     assert abs(p_dev - p_orc) <= 0.2, (p_dev, p_orc)
 
 
