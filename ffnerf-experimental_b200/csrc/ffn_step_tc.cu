@@ -378,9 +378,13 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
 // by the row so that a warp's stores and loads spread over the banks), then the levels are scattered
 // one at a time by a single (not unrolled) copy of the level code: the kernel is large and its
 // instruction cache is a limit.
+// Every lane of the warp executes the TMEM loads (tcgen05.ld is warp-aligned: with fewer than 32
+// samples per ray a warp holds two or more rays, which may differ in hitting the box); only `live`
+// lanes (a sample of a hitting ray) scatter.
 template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
-                                                  V3 p, float unscale, const float* coef, float* scratch, float* gbuf) {
+                                                  V3 p, float unscale, const float* coef, float* scratch, float* gbuf,
+                                                  bool live) {
     constexpr int LPOS = L * F;
     const uint32_t lane = tlane();
     if constexpr (F != 2) {
@@ -390,6 +394,7 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
             float g[16];
             tc::tmem_ld16(tmem + lane + col + j, g);
             tc::tmem_wait_ld();
+            if (!live) continue;
 #pragma unroll
             for (int li = 0; li < 16 / F; ++li) {
                 float gl[F];
@@ -412,6 +417,7 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
             grow[((j + q) / 4) ^ (sw % (LPOS / 4))] =
                 make_float4(g[q] * unscale, g[q + 1] * unscale, g[q + 2] * unscale, g[q + 3] * unscale);
     }
+    if (!live) return;
 #pragma unroll 1
     for (int lvl = 0; lvl < L; ++lvl) {
         const float4 t = grow[((lvl * F) / 4) ^ (sw % (LPOS / 4))];
@@ -875,9 +881,9 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         prefetch_next();
         // the activation tiles are dead once the last MMAs completed: C1 holds the scatter's exchange
         // rows, C2 the parked gradients
-        if (!MLPB && hit && valid)
+        if (!MLPB)
             scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef,
-                                 reinterpret_cast<float*>(tC1), reinterpret_cast<float*>(tC2));
+                                 reinterpret_cast<float*>(tC1), reinterpret_cast<float*>(tC2), hit && valid);
         tc::fence_before_sync();
         tile_sync();
     }
