@@ -839,9 +839,13 @@ int ffn_dp_reduce_apply(ffn_ctx* c, const ffn_step_scalars* s, void* stream) {
         ffn::dp_reduce_apply_nvls_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, c->dp->mc_grads, c->dp->mc_table,
                                                                   c->table, table4, total4, lc, epoch, c->status,
                                                                   c->dp->done_counter, c->dp->wait_limit);
-    else
-        ffn::dp_reduce_apply_kernel<<<sms * 4, 256, 0, st>>>(c->dp->peers, table4, total4, lc, epoch, c->status,
-                                                             c->dp->done_counter, c->dp->wait_limit);
+    else {
+        // registers sized for the world: two float4 per thread and iteration up to 4 ranks, one at 8
+        auto kern = c->dp->peers.world <= 2 ? ffn::dp_reduce_apply_kernel<2, 2>
+                  : c->dp->peers.world <= 4 ? ffn::dp_reduce_apply_kernel<4, 2> : ffn::dp_reduce_apply_kernel<8, 1>;
+        kern<<<sms * 4, 256, 0, st>>>(c->dp->peers, table4, total4, lc, epoch, c->status, c->dp->done_counter,
+                                      c->dp->wait_limit);
+    }
     ++c->launches;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(c, e, "exchange launch");

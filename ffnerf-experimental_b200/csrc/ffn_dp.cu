@@ -57,9 +57,13 @@ __device__ __forceinline__ bool dp_wait(const uint32_t* flags, int first, int n,
     return false;
 }
 
-__global__ void __launch_bounds__(256) dp_reduce_apply_kernel(const DpPeers P, uint32_t table4, uint32_t total4,
-                                                              const LevelCoef lc, uint32_t epoch, int* status,
-                                                              unsigned int* done_counter, uint32_t wait_limit) {
+// U float4 of the shard per thread and iteration, all of their loads (every rank's gradients and
+// the local table) issued before any sum, so that U * (W + 1) loads are in flight per thread; WMAX
+// bounds the ranks the registers are sized for.
+template <int WMAX, int U>
+__global__ void __launch_bounds__(256, 4) dp_reduce_apply_kernel(const DpPeers P, uint32_t table4, uint32_t total4,
+                                                                 const LevelCoef lc, uint32_t epoch, int* status,
+                                                                 unsigned int* done_counter, uint32_t wait_limit) {
     __shared__ int ok;
     const int W = P.world, r = P.rank;
     if (threadIdx.x == 0) {
@@ -75,27 +79,42 @@ __global__ void __launch_bounds__(256) dp_reduce_apply_kernel(const DpPeers P, u
         const uint32_t per = (total4 + (uint32_t)W - 1) / (uint32_t)W;
         const uint32_t lo = (uint32_t)r * per;
         const uint32_t hi = lo + per < total4 ? lo + per : total4;
-        for (uint32_t i = lo + blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += gridDim.x * blockDim.x) {
-            float4 g[DP_MAX_RANKS];
+        const uint32_t S = gridDim.x * blockDim.x;
+        for (uint32_t i0 = lo + blockIdx.x * blockDim.x + threadIdx.x; i0 < hi; i0 += U * S) {
+            float4 g[U][WMAX], t[U];
+            bool has[U];
 #pragma unroll
-            for (int p = 0; p < DP_MAX_RANKS; ++p)
-                if (p < W) g[p] = reinterpret_cast<const float4*>(P.grads[p])[i];
-            float4 s = g[0];
+            for (int u = 0; u < U; ++u) {
+                const uint32_t i = i0 + (uint32_t)u * S;
+                has[u] = i < hi;
+                t[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (!has[u]) continue;
 #pragma unroll
-            for (int p = 1; p < DP_MAX_RANKS; ++p)
-                if (p < W) { s.x = fa(s.x, g[p].x); s.y = fa(s.y, g[p].y); s.z = fa(s.z, g[p].z); s.w = fa(s.w, g[p].w); }
-            if (i < table4) {
-                const float cf = lc.coef[level_of(lc, i * 4u)];
-                float4 t = reinterpret_cast<const float4*>(P.table[r])[i];
-                t.x = fa(t.x, fm(cf, s.x)); t.y = fa(t.y, fm(cf, s.y));
-                t.z = fa(t.z, fm(cf, s.z)); t.w = fa(t.w, fm(cf, s.w));
+                for (int p = 0; p < WMAX; ++p)
+                    if (p < W) g[u][p] = reinterpret_cast<const float4*>(P.grads[p])[i];
+                if (i < table4) t[u] = reinterpret_cast<const float4*>(P.table[r])[i];
+            }
 #pragma unroll
-                for (int p = 0; p < DP_MAX_RANKS; ++p)
-                    if (p < W) reinterpret_cast<float4*>(P.table[p])[i] = t;
-            } else {
+            for (int u = 0; u < U; ++u) {
+                if (!has[u]) continue;
+                const uint32_t i = i0 + (uint32_t)u * S;
+                float4 s = g[u][0];
 #pragma unroll
-                for (int p = 0; p < DP_MAX_RANKS; ++p)
-                    if (p < W) reinterpret_cast<float4*>(P.grads[p])[i] = s;
+                for (int p = 1; p < WMAX; ++p)
+                    if (p < W) { s.x = fa(s.x, g[u][p].x); s.y = fa(s.y, g[u][p].y); s.z = fa(s.z, g[u][p].z); s.w = fa(s.w, g[u][p].w); }
+                if (i < table4) {
+                    const float cf = lc.coef[level_of(lc, i * 4u)];
+                    float4 tv = t[u];
+                    tv.x = fa(tv.x, fm(cf, s.x)); tv.y = fa(tv.y, fm(cf, s.y));
+                    tv.z = fa(tv.z, fm(cf, s.z)); tv.w = fa(tv.w, fm(cf, s.w));
+#pragma unroll
+                    for (int p = 0; p < WMAX; ++p)
+                        if (p < W) reinterpret_cast<float4*>(P.table[p])[i] = tv;
+                } else {
+#pragma unroll
+                    for (int p = 0; p < WMAX; ++p)
+                        if (p < W) reinterpret_cast<float4*>(P.grads[p])[i] = s;
+                }
             }
         }
     }
@@ -148,16 +167,31 @@ __global__ void __launch_bounds__(256) dp_reduce_apply_nvls_kernel(const DpPeers
         const uint32_t per = (total4 + (uint32_t)W - 1) / (uint32_t)W;
         const uint32_t lo = (uint32_t)r * per;
         const uint32_t hi = lo + per < total4 ? lo + per : total4;
-        for (uint32_t i = lo + blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += gridDim.x * blockDim.x) {
-            const float4 s = mc_ld_reduce_add(mc_grads + 4 * (size_t)i);
-            if (i < table4) {
-                const float cf = lc.coef[level_of(lc, i * 4u)];
-                float4 t = reinterpret_cast<const float4*>(table)[i];
-                t.x = fa(t.x, fm(cf, s.x)); t.y = fa(t.y, fm(cf, s.y));
-                t.z = fa(t.z, fm(cf, s.z)); t.w = fa(t.w, fm(cf, s.w));
-                mc_st(mc_table + 4 * (size_t)i, t);
-            } else {
-                mc_st(mc_grads + 4 * (size_t)i, s);
+        // two float4 of the shard per thread and iteration, both reductions and table loads in flight
+        const uint32_t S = gridDim.x * blockDim.x;
+        for (uint32_t i0 = lo + blockIdx.x * blockDim.x + threadIdx.x; i0 < hi; i0 += 2 * S) {
+            float4 s[2], t[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const uint32_t i = i0 + (uint32_t)u * S;
+                s[u] = t[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (i >= hi) continue;
+                s[u] = mc_ld_reduce_add(mc_grads + 4 * (size_t)i);
+                if (i < table4) t[u] = reinterpret_cast<const float4*>(table)[i];
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const uint32_t i = i0 + (uint32_t)u * S;
+                if (i >= hi) continue;
+                if (i < table4) {
+                    const float cf = lc.coef[level_of(lc, i * 4u)];
+                    float4 tv = t[u];
+                    tv.x = fa(tv.x, fm(cf, s[u].x)); tv.y = fa(tv.y, fm(cf, s[u].y));
+                    tv.z = fa(tv.z, fm(cf, s[u].z)); tv.w = fa(tv.w, fm(cf, s[u].w));
+                    mc_st(mc_table + 4 * (size_t)i, tv);
+                } else {
+                    mc_st(mc_grads + 4 * (size_t)i, s[u]);
+                }
             }
         }
     }
