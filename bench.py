@@ -96,7 +96,10 @@ MLP_FLOP_PER_SAMPLE = 56448   # forward 18,816 (6,144 density + 12,672 colour) x
 
 
 def run_mlp_micro(args, wl, dev, st, gen, timed) -> dict:
-    """cfg5's MLP half on the tensor cores: ffn_mlp_bench over 2^22 packed fp16 inputs."""
+    """cfg5's MLP half on the tensor cores over 2^22 packed fp16 inputs: the headline is the plain
+    fp16-operand form (ffn_mlp_bench_f16: the configuration's fp16 inputs, fp32 accumulation, one MMA
+    per product); `compensated` is the training step's form (ffn_mlp_bench: every product from fp16
+    operand pairs), timed the same way."""
     import torch
     import ffn_native as fn
     from ffn_config import make_geometry, param_layout, param_shapes
@@ -116,10 +119,12 @@ def run_mlp_micro(args, wl, dev, st, gen, timed) -> dict:
     x16 = torch.randn((n, 32), device=dev, generator=gen).half()
     tiles = torch.empty(ctx.x0_tile_bytes(n), dtype=torch.uint8, device=dev)
     ctx.pack_x0(x16, tiles, n, stream=st)
-    step = lambda: ctx.mlp_bench(tiles, n, stream=st)           # noqa: E731
+    step = lambda: ctx.mlp_bench_f16(tiles, n, stream=st)       # noqa: E731
+    step_cp = lambda: ctx.mlp_bench(tiles, n, stream=st)        # noqa: E731
     for _ in range(args.warmup):
         with torch.cuda.stream(st):
             step()
+            step_cp()
     torch.cuda.synchronize()
     launches0 = ctx.launches
     with ClockSampler(0) as clk:
@@ -134,7 +139,10 @@ def run_mlp_micro(args, wl, dev, st, gen, timed) -> dict:
             step()
             h_g.copy_(ctx.tensor(fn.BUF_GRADS)[-total:], non_blocking=True)
         (t_e2e,) = timed([e2e], flush=False)
+        (t_cp,) = timed([step_cp], flush=False)
     ms = t / args.steps
+    ms_cp = t_cp / args.steps
+    tf_cp = MLP_FLOP_PER_SAMPLE * n / (ms_cp * 1e-3) / 1e12
     tf = MLP_FLOP_PER_SAMPLE * n / (ms * 1e-3) / 1e12
     # CPU: the same MLP forward/backward in fp32 with torch on the host cores, a bounded sample
     m = 1 << 16
@@ -161,7 +169,10 @@ def run_mlp_micro(args, wl, dev, st, gen, timed) -> dict:
         "e2e": {"value": MLP_FLOP_PER_SAMPLE * n / (t_e2e / args.steps * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": n * 64, "d2h_bytes_per_step": total * 4},
         "gpu_launches": launches,
-        "roofline": {"bound": "tensor", "kernel": "fused_step_tc_kernel<2,1,staged,mlp> + reduce_partials",
+        "compensated": {"value": tf_cp, "unit": "TFLOP/s", "ms_per_step": ms_cp, "frac": tf_cp / tflops_peak,
+                        "note": "the training step's form: every product from compensated fp16 operand pairs "
+                                "(three MMAs per counted product, lo tiles stored by every epilogue)"},
+        "roofline": {"bound": "tensor", "kernel": "fused_step_tc_kernel<2,1,staged,mlp,plain> + reduce_partials",
                      "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s", "frac": tf / tflops_peak,
                      "traffic": None, "peak_source": peak_kind,
                      "note": "peak = measured cuBLAS bf16 burst; the MLP is 128-row tiles of 32-64 wide layers"},

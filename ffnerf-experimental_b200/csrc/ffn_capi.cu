@@ -275,6 +275,38 @@ int forward_backward_staged(ffn_ctx* c, const void* rays, const void* targets, v
     return FFN_OK;
 }
 
+// The MLP microbenchmark launch: compensated operand pairs (the step's form) or plain fp16.
+template <bool PLAIN>
+int mlp_bench(ffn_ctx* c, const void* tiles, int64_t n, void* stream) {
+    if (!c || (n > 0 && !tiles)) return fail(c, FFN_E_CONFIG, "null argument");
+    if (n <= 0) return FFN_OK;
+    if (c->cfg.mlp_precision != 1 || c->cfg.F != 2 || c->cfg.ND != 1)
+        return fail(c, FFN_E_CONFIG, "the MLP microbenchmark is compiled for the tensor-core MLP with F=2, ND=1");
+    if (n % 128 != 0 || (uint64_t)n / (uint64_t)c->cfg.spr > 0xFFFFFFFFull || 128 % c->cfg.spr != 0)
+        return fail(c, FFN_E_CONFIG, "n must be a multiple of 128 and the configured samples per ray divide 128");
+    if (!aligned16(tiles)) return fail(c, FFN_E_CONFIG, "tiles must be 16-byte aligned");
+    DeviceGuard guard(c->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    using PL = TcPlan<2, 1>;
+    auto kfn = fused_step_tc_kernel<2, 1, true, true, PLAIN>;
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::BYTES);
+    if (e != cudaSuccess) return cuda_fail(c, e, "MLP microbenchmark kernel attribute");
+    ffn_step_scalars s{};
+    s.sh_mult = 1.0f;
+    s.spr = (uint32_t)c->cfg.spr;
+    StepArgs a = base_args(c, nullptr, nullptr, nullptr, (uint32_t)(n / c->cfg.spr), &s);
+    a.do_train = 1;
+    a.x0_stage = static_cast<const unsigned char*>(tiles);
+    const int grid = fused_grid(c, (int)(n / 128));
+    kfn<<<grid, PL::THREADS, PL::BYTES, st>>>(a);
+    ++c->launches;
+    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid * PL::GROUPS, c->Pw,
+                                                        c->grads + c->table_floats, c->status);
+    ++c->launches;
+    e = cudaGetLastError();
+    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "MLP microbenchmark launch");
+}
+
 }  // namespace
 
 extern "C" {
@@ -626,35 +658,8 @@ int ffn_pack_x0(ffn_ctx* c, const void* x16, void* tiles, int64_t n, void* strea
     return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "pack launch");
 }
 
-int ffn_mlp_bench(ffn_ctx* c, const void* tiles, int64_t n, void* stream) {
-    if (!c || (n > 0 && !tiles)) return fail(c, FFN_E_CONFIG, "null argument");
-    if (n <= 0) return FFN_OK;
-    if (c->cfg.mlp_precision != 1 || c->cfg.F != 2 || c->cfg.ND != 1)
-        return fail(c, FFN_E_CONFIG, "the MLP microbenchmark is compiled for the tensor-core MLP with F=2, ND=1");
-    if (n % 128 != 0 || (uint64_t)n / (uint64_t)c->cfg.spr > 0xFFFFFFFFull || 128 % c->cfg.spr != 0)
-        return fail(c, FFN_E_CONFIG, "n must be a multiple of 128 and the configured samples per ray divide 128");
-    if (!aligned16(tiles)) return fail(c, FFN_E_CONFIG, "tiles must be 16-byte aligned");
-    DeviceGuard guard(c->device);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    using PL = TcPlan<2, 1>;
-    auto kfn = fused_step_tc_kernel<2, 1, true, true>;
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::BYTES);
-    if (e != cudaSuccess) return cuda_fail(c, e, "MLP microbenchmark kernel attribute");
-    ffn_step_scalars s{};
-    s.sh_mult = 1.0f;
-    s.spr = (uint32_t)c->cfg.spr;
-    StepArgs a = base_args(c, nullptr, nullptr, nullptr, (uint32_t)(n / c->cfg.spr), &s);
-    a.do_train = 1;
-    a.x0_stage = static_cast<const unsigned char*>(tiles);
-    const int grid = fused_grid(c, (int)(n / 128));
-    kfn<<<grid, PL::THREADS, PL::BYTES, st>>>(a);
-    ++c->launches;
-    reduce_partials<<<(c->Pw + 255) / 256, 256, 0, st>>>(c->partials, grid * PL::GROUPS, c->Pw,
-                                                        c->grads + c->table_floats, c->status);
-    ++c->launches;
-    e = cudaGetLastError();
-    return e == cudaSuccess ? FFN_OK : cuda_fail(c, e, "MLP microbenchmark launch");
-}
+int ffn_mlp_bench(ffn_ctx* c, const void* tiles, int64_t n, void* stream) { return mlp_bench<false>(c, tiles, n, stream); }
+int ffn_mlp_bench_f16(ffn_ctx* c, const void* tiles, int64_t n, void* stream) { return mlp_bench<true>(c, tiles, n, stream); }
 
 uint64_t ffn_kernel_launches(const ffn_ctx* c) { return c ? c->launches : 0u; }
 

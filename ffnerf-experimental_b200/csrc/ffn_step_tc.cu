@@ -134,30 +134,48 @@ __device__ __forceinline__ void gemm(uint32_t d, uint32_t a, int a_cols, bool a_
                     (k > 0 || accumulate) ? 1u : 0u);
 }
 
+// The helpers below take CP (compensated): true forms every product from fp16 operand pairs, the
+// training step's form; false multiplies the hi tiles alone and stores no lo tiles (plain fp16
+// operands, fp32 accumulation: the MLP microbenchmark's plain form).
+//
 // Forward layer with compensated operands: ACC = Ah*Wh^T + Ah*Wl^T + Al*Wh^T (both K-major; one
 // thread).  The large term first, then the two corrections into the same fp32 accumulator.
+template <bool CP = true>
 __device__ __forceinline__ void gemm_fwd3(uint32_t d, uint32_t a_hi, uint32_t a_lo, int a_cols, uint32_t w_hi,
                                          uint32_t w_lo, int N, int K) {
     gemm(d, a_hi, a_cols, false, w_hi, a_cols, false, 128, N, K, 0);
-    gemm(d, a_hi, a_cols, false, w_lo, a_cols, false, 128, N, K, 1);
-    gemm(d, a_lo, a_cols, false, w_hi, a_cols, false, 128, N, K, 1);
+    if constexpr (CP) {
+        gemm(d, a_hi, a_cols, false, w_lo, a_cols, false, 128, N, K, 1);
+        gemm(d, a_lo, a_cols, false, w_hi, a_cols, false, 128, N, K, 1);
+    }
 }
 
 // Backward-data layer with compensated operands: ACC = Dh*Wh + Dl*Wh + Dh*Wl, D [128 x K] K-major
 // (d_cols columns), W [K x N] read MN-major (w_cols columns).  One thread.
+template <bool CP = true>
 __device__ __forceinline__ void gemm_bwd3(uint32_t d, uint32_t d_hi, uint32_t d_lo, int d_cols, uint32_t w_hi,
                                          uint32_t w_lo, int w_cols, int N, int K) {
     gemm(d, d_hi, d_cols, false, w_hi, w_cols, true, 128, N, K, 0);
-    gemm(d, d_lo, d_cols, false, w_hi, w_cols, true, 128, N, K, 1);
-    gemm(d, d_hi, d_cols, false, w_lo, w_cols, true, 128, N, K, 1);
+    if constexpr (CP) {
+        gemm(d, d_lo, d_cols, false, w_hi, w_cols, true, 128, N, K, 1);
+        gemm(d, d_hi, d_cols, false, w_lo, w_cols, true, 128, N, K, 1);
+    }
 }
 
 // Weight (or bias, with the one-hot tile) gradient with a compensated delta: ACC (+)= Dh^T X + Dl^T X,
 // D [128 x 64] and X [128 x N] both read MN-major (the activation X stays a single fp16 tile).
+template <bool CP = true>
 __device__ __forceinline__ void gemm_wgrad2(uint32_t d, uint32_t d_hi, uint32_t d_lo, uint32_t x, int x_cols, int N,
                                            uint32_t accumulate) {
     gemm(d, d_hi, 64, true, x, x_cols, true, 64, N, 128, accumulate);
-    gemm(d, d_lo, 64, true, x, x_cols, true, 64, N, 128, 1);
+    if constexpr (CP) gemm(d, d_lo, 64, true, x, x_cols, true, 64, N, 128, 1);
+}
+
+// One 8-value chunk as the operand pair (CP) or as the hi tile alone.
+template <bool CP = true>
+__device__ __forceinline__ void st_pair8(unsigned char* hi, unsigned char* lo, int r, int c0, int cols, const float* v) {
+    if constexpr (CP) tc::st_chunk8_hilo(hi, lo, r, c0, cols, v);
+    else tc::st_chunk8(hi, r, c0, cols, v);
 }
 
 // One row (this thread's sample) of an ACC region into registers.
@@ -179,15 +197,16 @@ __device__ __forceinline__ void store_row(unsigned char* tile, int cols, const f
 #pragma unroll
     for (int c = 0; c < N; c += 8) tc::st_chunk8(tile, trow(), c, cols, v + c);
 }
-template <int N>
+template <int N, bool CP = true>
 __device__ __forceinline__ void store_row_hilo(unsigned char* hi, unsigned char* lo, int cols, const float (&v)[N]) {
 #pragma unroll
-    for (int c = 0; c < N; c += 8) tc::st_chunk8_hilo(hi, lo, trow(), c, cols, v + c);
+    for (int c = 0; c < N; c += 8) st_pair8<CP>(hi, lo, trow(), c, cols, v + c);
 }
 
 // Epilogue of a forward layer: row = relu(ACC * in_scale + bias) for N columns, 32 at a time (two
 // TMEM loads per wait; one copy of the loop body, to keep the kernel's code small), stored as the
 // (hi, lo) pair that the next forward layer multiplies.
+template <bool CP = true>
 __device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N, const float* bias, unsigned char* tile,
                                               unsigned char* lo_tile, int cols, float in_scale = 1.0f) {
     const uint32_t lane = tlane();
@@ -201,13 +220,14 @@ __device__ __forceinline__ void epi_bias_relu(uint32_t tmem, uint32_t col, int N
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = fmaxf(fmaf(v[i], in_scale, bias[j + i]), 0.0f);
 #pragma unroll
-        for (int q = 0; q < 32; q += 8) tc::st_chunk8_hilo(tile, lo_tile, r, j + q, cols, v + q);
+        for (int q = 0; q < 32; q += 8) st_pair8<CP>(tile, lo_tile, r, j + q, cols, v + q);
     }
 }
 
 // Epilogue of a backward layer: row = ACC masked by (activation in `tile` > 0), written in place,
 // 32 columns at a time.  The mask reads the hi copy of the activation, which is > 0 whenever the
 // activation is, except below fp16's smallest subnormal (2^-24), where the delta's share is negligible.
+template <bool CP = true>
 __device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N, unsigned char* tile,
                                               unsigned char* lo_tile, int cols) {
     const uint32_t lane = tlane();
@@ -223,7 +243,7 @@ __device__ __forceinline__ void epi_relu_mask(uint32_t tmem, uint32_t col, int N
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = act[i] > 0.0f ? v[i] : 0.0f;
 #pragma unroll
-        for (int q = 0; q < 32; q += 8) tc::st_chunk8_hilo(tile, lo_tile, r, j + q, cols, v + q);
+        for (int q = 0; q < 32; q += 8) st_pair8<CP>(tile, lo_tile, r, j + q, cols, v + q);
     }
 }
 
@@ -480,9 +500,11 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // Work split: tile g of the CTA's groups takes tiles blockIdx.x * GROUPS + g, advancing by
 // gridDim.x * GROUPS; each group writes its own row of weight-gradient partials
 // (a.partials[(blockIdx.x * GROUPS + g) * P]).
-template <int F, int ND, bool STAGED = false, bool MLPB = false>
+template <int F, int ND, bool STAGED = false, bool MLPB = false, bool PLAIN = false>
 __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kernel(const StepArgs a) {
     static_assert(!MLPB || STAGED, "the MLP microbenchmark runs the staged form");
+    static_assert(!PLAIN || MLPB, "plain fp16 operands are the MLP microbenchmark's form only");
+    constexpr bool CP = !PLAIN;     // compensated operand pairs
     using PL = TcPlan<F, ND>;
     constexpr int LPOS = PL::LPOS;
     extern __shared__ __align__(1024) unsigned char smem_tc[];
@@ -689,18 +711,18 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         } else {
             if constexpr (!STAGED) encode_rows<F>(c, a.table, pn, hit, tX0, tLO);
             handoff();
-            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::X0), G(PL::LO), LPOS, S(PL::W_HI + PL::W_DIN), S(PL::W_LO + PL::W_DIN), 64, LPOS);
+            if (tid == 0) gemm_fwd3<CP>(tmem + PL::ACC, G(PL::X0), G(PL::LO), LPOS, S(PL::W_HI + PL::W_DIN), S(PL::W_LO + PL::W_DIN), 64, LPOS);
             sync_mma();
-            epi_bias_relu(tmem, PL::ACC, 64, bias, tH(0), tLO, 64, 1.0f / INPUT_SCALE);
+            epi_bias_relu<CP>(tmem, PL::ACC, 64, bias, tH(0), tLO, 64, 1.0f / INPUT_SCALE);
             if (ND >= 2) {
                 handoff();
-                if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::HD), G(PL::LO), 64, S(PL::W_HI + PL::W_D01), S(PL::W_LO + PL::W_D01), 64, 64);
+                if (tid == 0) gemm_fwd3<CP>(tmem + PL::ACC, G(PL::HD), G(PL::LO), 64, S(PL::W_HI + PL::W_D01), S(PL::W_LO + PL::W_D01), 64, 64);
                 sync_mma();
-                epi_bias_relu(tmem, PL::ACC, 64, bias + 64, tH(ND - 1), tLO, 64);
+                epi_bias_relu<CP>(tmem, PL::ACC, 64, bias + 64, tH(ND - 1), tLO, 64);
             }
             handoff();
             if (tid == 0)
-                gemm_fwd3(tmem + PL::ACC, G(PL::HD + (ND - 1) * 128 * 64 * 2), G(PL::LO), 64, S(PL::W_HI + PL::W_DOUT),
+                gemm_fwd3<CP>(tmem + PL::ACC, G(PL::HD + (ND - 1) * 128 * 64 * 2), G(PL::LO), 64, S(PL::W_HI + PL::W_DOUT),
                           S(PL::W_LO + PL::W_DOUT), 16, 64);
             sync_mma();
             {
@@ -715,18 +737,18 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
                 sh16(d.x, d.y, d.z, sh);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[16 + j] = sh[j] * a.sh_mult;
-                store_row_hilo<32>(tXC, tLO, 32, v);
+                store_row_hilo<32, CP>(tXC, tLO, 32, v);
             }
             handoff();
-            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_CIN), S(PL::W_LO + PL::W_CIN), 64, 32);
+            if (tid == 0) gemm_fwd3<CP>(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_CIN), S(PL::W_LO + PL::W_CIN), 64, 32);
             sync_mma();
-            epi_bias_relu(tmem, PL::ACC, 64, bias + 144, tC1, tLO, 64);
+            epi_bias_relu<CP>(tmem, PL::ACC, 64, bias + 144, tC1, tLO, 64);
             handoff();
-            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::C1), G(PL::LO), 64, S(PL::W_HI + PL::W_C01), S(PL::W_LO + PL::W_C01), 64, 64);
+            if (tid == 0) gemm_fwd3<CP>(tmem + PL::ACC, G(PL::C1), G(PL::LO), 64, S(PL::W_HI + PL::W_C01), S(PL::W_LO + PL::W_C01), 64, 64);
             sync_mma();
-            epi_bias_relu(tmem, PL::ACC, 64, bias + 208, tC2, tLO, 64);
+            epi_bias_relu<CP>(tmem, PL::ACC, 64, bias + 208, tC2, tLO, 64);
             handoff();
-            if (tid == 0) gemm_fwd3(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_COUT), S(PL::W_LO + PL::W_COUT), 16, 64);
+            if (tid == 0) gemm_fwd3<CP>(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_COUT), S(PL::W_LO + PL::W_COUT), 16, 64);
             sync_mma();
             {
                 float v[16];
@@ -793,7 +815,7 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;
             v[0] = dcout[0] * DELTA_SCALE; v[1] = dcout[1] * DELTA_SCALE; v[2] = dcout[2] * DELTA_SCALE;
-            store_row_hilo<16>(tDC, tDC + PL::DC_LO, 16, v);
+            store_row_hilo<16, CP>(tDC, tDC + PL::DC_LO, 16, v);
             // colour-head bias gradient: a transposed warp butterfly, then three lanes add at once
             {
                 const float v4[4] = {v[0], v[1], v[2], 0.0f};
@@ -806,30 +828,30 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         handoff();
         if (tid == 0) {
             gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC), 16, true, 64, 16, 128, acc0);            // dWc_out^T
-            gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC) + PL::DC_LO, 16, true, 64, 16, 128, 1);
-            gemm_bwd3(tmem + PL::ACC, G(PL::DC), G(PL::DC) + PL::DC_LO, 16, S(PL::W_HI + PL::W_COUT),
+            if constexpr (CP) gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC) + PL::DC_LO, 16, true, 64, 16, 128, 1);
+            gemm_bwd3<CP>(tmem + PL::ACC, G(PL::DC), G(PL::DC) + PL::DC_LO, 16, S(PL::W_HI + PL::W_COUT),
                       S(PL::W_LO + PL::W_COUT), 64, 64, 16);                                                       // dC2
         }
         sync_mma();
         {
-            epi_relu_mask(tmem, PL::ACC, 64, tC2, tLO, 64);
+            epi_relu_mask<CP>(tmem, PL::ACC, 64, tC2, tLO, 64);
         }
         handoff();
         if (tid == 0) {
-            gemm_wgrad2(tmem + PL::DW_C01, G(PL::C2), G(PL::LO), G(PL::C1), 64, 64, acc0);                      // dWc_01
-            gemm_wgrad2(tmem + PL::B_C1, G(PL::C2), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbc_1
-            gemm_bwd3(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_C01), S(PL::W_LO + PL::W_C01),
+            gemm_wgrad2<CP>(tmem + PL::DW_C01, G(PL::C2), G(PL::LO), G(PL::C1), 64, 64, acc0);                      // dWc_01
+            gemm_wgrad2<CP>(tmem + PL::B_C1, G(PL::C2), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbc_1
+            gemm_bwd3<CP>(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_C01), S(PL::W_LO + PL::W_C01),
                       64, 64, 64);                                                                                // dC1
         }
         sync_mma();
         {
-            epi_relu_mask(tmem, PL::ACC, 64, tC1, tLO, 64);
+            epi_relu_mask<CP>(tmem, PL::ACC, 64, tC1, tLO, 64);
         }
         handoff();
         if (tid == 0) {
-            gemm_wgrad2(tmem + PL::DW_CIN, G(PL::C1), G(PL::LO), G(PL::XC), 32, 32, acc0);                      // dWc_in
-            gemm_wgrad2(tmem + PL::B_C0, G(PL::C1), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbc_0
-            gemm_bwd3(tmem + PL::ACC, G(PL::C1), G(PL::LO), 64, S(PL::W_HI + PL::W_CIN), S(PL::W_LO + PL::W_CIN),
+            gemm_wgrad2<CP>(tmem + PL::DW_CIN, G(PL::C1), G(PL::LO), G(PL::XC), 32, 32, acc0);                      // dWc_in
+            gemm_wgrad2<CP>(tmem + PL::B_C0, G(PL::C1), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbc_0
+            gemm_bwd3<CP>(tmem + PL::ACC, G(PL::C1), G(PL::LO), 64, S(PL::W_HI + PL::W_CIN), S(PL::W_LO + PL::W_CIN),
                       32, 16, 64);                                                                                // dDout
         }
         sync_mma();
@@ -839,7 +861,7 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
             v[0] += ddout0 * DELTA_SCALE;
             // delta at the density output replaces the colour input's first 16 columns
 #pragma unroll
-            for (int cc = 0; cc < 16; cc += 8) tc::st_chunk8_hilo(tXC, tLO, tid, cc, 32, v + cc);
+            for (int cc = 0; cc < 16; cc += 8) st_pair8<CP>(tXC, tLO, tid, cc, 32, v + cc);
             {
                 const float sum = warp_sum16(v);
                 if ((tid & 1) == 0) atomicAdd(bgrad + ((tid >> 1) & 15), sum);
@@ -849,30 +871,30 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         handoff();
         if (tid == 0) {
             gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::XC), 32, true, 64, 16, 128, acc0);               // dWd_out^T
-            gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::LO), 32, true, 64, 16, 128, 1);
-            gemm_bwd3(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_DOUT), S(PL::W_LO + PL::W_DOUT),
+            if constexpr (CP) gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::LO), 32, true, 64, 16, 128, 1);
+            gemm_bwd3<CP>(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_DOUT), S(PL::W_LO + PL::W_DOUT),
                       64, 64, 16);                                                                                // dH_last
         }
         sync_mma();
         {
-            epi_relu_mask(tmem, PL::ACC, 64, tH(ND - 1), tLO, 64);
+            epi_relu_mask<CP>(tmem, PL::ACC, 64, tH(ND - 1), tLO, 64);
         }
         if (ND >= 2) {
             handoff();
             if (tid == 0) {
-                gemm_wgrad2(tmem + PL::DW_D01, hlast, G(PL::LO), G(PL::HD), 64, 64, acc0);                      // dWd_01
-                gemm_wgrad2(tmem + PL::B_D1, hlast, G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbd_1
-                gemm_bwd3(tmem + PL::ACC, hlast, G(PL::LO), 64, S(PL::W_HI + PL::W_D01), S(PL::W_LO + PL::W_D01),
+                gemm_wgrad2<CP>(tmem + PL::DW_D01, hlast, G(PL::LO), G(PL::HD), 64, 64, acc0);                      // dWd_01
+                gemm_wgrad2<CP>(tmem + PL::B_D1, hlast, G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbd_1
+                gemm_bwd3<CP>(tmem + PL::ACC, hlast, G(PL::LO), 64, S(PL::W_HI + PL::W_D01), S(PL::W_LO + PL::W_D01),
                           64, 64, 64);                                                                            // dH_0
             }
             sync_mma();
-            epi_relu_mask(tmem, PL::ACC, 64, tH(0), tLO, 64);
+            epi_relu_mask<CP>(tmem, PL::ACC, 64, tH(0), tLO, 64);
         }
         handoff();
         if (tid == 0) {
-            gemm_wgrad2(tmem + PL::DW_DIN, G(PL::HD), G(PL::LO), G(PL::X0), LPOS, LPOS, acc0);                  // dWd_in
-            gemm_wgrad2(tmem + PL::B_D0, G(PL::HD), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbd_0
-            gemm_bwd3(tmem + PL::ACC, G(PL::HD), G(PL::LO), 64, S(PL::W_HI + PL::W_DIN), S(PL::W_LO + PL::W_DIN),
+            gemm_wgrad2<CP>(tmem + PL::DW_DIN, G(PL::HD), G(PL::LO), G(PL::X0), LPOS, LPOS, acc0);                  // dWd_in
+            gemm_wgrad2<CP>(tmem + PL::B_D0, G(PL::HD), G(PL::LO), S(PL::ONES), 8, 8, acc0);                        // dbd_0
+            gemm_bwd3<CP>(tmem + PL::ACC, G(PL::HD), G(PL::LO), 64, S(PL::W_HI + PL::W_DIN), S(PL::W_LO + PL::W_DIN),
                       LPOS, LPOS, 64);                                                                            // hash grads
         }
         sync_mma();

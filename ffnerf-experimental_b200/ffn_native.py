@@ -47,7 +47,7 @@ STEP_TABLE_IMMEDIATE = 1
 STEP_TABLE_APPLIED = 2
 STATUS_NONFINITE, STATUS_TC_TIMEOUT, STATUS_DP_TIMEOUT = 1, 4, 8   # ffn_status bits
 STAGE_SAMPLES = 1 << 20   # samples per group of the split tensor-core step (ffn_capi.cu)
-ABI_VERSION = 5          # include/ffnerf.h FFN_ABI_VERSION
+ABI_VERSION = 6          # include/ffnerf.h FFN_ABI_VERSION
 
 
 _VP = C.c_void_p
@@ -71,6 +71,7 @@ _SIGS = {
     "ffn_hash_encode_f16": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_pack_x0": (C.c_int, [_VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_mlp_bench": (C.c_int, [_VP, _VP, C.c_int64, _VP]),
+    "ffn_mlp_bench_f16": (C.c_int, [_VP, _VP, C.c_int64, _VP]),
     "ffn_hash_encode_bwd_f16": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, _VP]),
     "ffn_adam": (C.c_int, [_VP, _VP, _VP, _VP, C.c_int64, C.c_float, C.c_float, C.c_float, C.c_float, _VP]),
     "ffn_status": (C.c_int, [_VP, C.POINTER(C.c_uint32)]),
@@ -343,6 +344,12 @@ class Context:
         MLP part of BUF_GRADS (view direction (0.36, 0.48, 0.8), sh multiplier 1)."""
         self._check_tiles(None, tiles, n)
         self._check(self.lib.ffn_mlp_bench(self.h, _ptr(tiles), int(n), self._stream(stream)), "ffn_mlp_bench")
+
+    def mlp_bench_f16(self, tiles, n: int, stream=None):
+        """mlp_bench with plain fp16 operands (one MMA per product, no compensation)."""
+        self._check_tiles(None, tiles, n)
+        self._check(self.lib.ffn_mlp_bench_f16(self.h, _ptr(tiles), int(n), self._stream(stream)),
+                    "ffn_mlp_bench_f16")
 
     def hash_encode_bwd_f16(self, grad16, pts, denc, n: int, stream=None):
         """Scatter-adds fp32 upstream gradients denc [n, 16F] into the caller-owned fp16 table grad16."""

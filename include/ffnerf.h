@@ -38,9 +38,10 @@ extern "C" {
 #endif
 
 #define FFN_N_LEVELS 16
-#define FFN_ABI_VERSION 5   /* 2: ffn_step_scalars.flags; 3: batch/exchange entry points;
+#define FFN_ABI_VERSION 6   /* 2: ffn_step_scalars.flags; 3: batch/exchange entry points;
                                    4: fp16-table hash and MLP microbenchmark entry points;
-                                   5: ffn_dp_set_wait_limit, ffn_config.transfer_fmt */
+                                   5: ffn_dp_set_wait_limit, ffn_config.transfer_fmt,
+                                      ffn_probe_random_access; 6: ffn_mlp_bench_f16 */
 
 enum {
     FFN_OK = 0,
@@ -182,6 +183,9 @@ int ffn_hash_encode_bwd_f16(ffn_ctx* ctx, void* grad16, const float* pts, const 
  * part of FFN_BUF_GRADS.  The table and its gradients are not touched. */
 int ffn_pack_x0(ffn_ctx* ctx, const void* x16, void* tiles, int64_t n, void* stream);
 int ffn_mlp_bench(ffn_ctx* ctx, const void* tiles, int64_t n, void* stream);
+/* The same with plain fp16 operands: one MMA per product from the hi tiles, no lo tiles stored
+ * (the training step forms every product from compensated fp16 pairs, as ffn_mlp_bench does). */
+int ffn_mlp_bench_f16(ffn_ctx* ctx, const void* tiles, int64_t n, void* stream);
 /* Ceiling probe (no reference counterpart): n_ops fully random 8-byte accesses (mode 0: float2
  * loads through the read-only path, as the hash encoders do; mode 1: red.global.add.v2.f32
  * reductions, as the gradient scatter does; both adding a negligible value) over the largest
