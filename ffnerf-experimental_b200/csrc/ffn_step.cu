@@ -86,9 +86,10 @@ __device__ __forceinline__ void dense_bwd(const float (&d)[OUT], const float* W,
 // gb[o] += sum_r D[r][o]  (update_layer_tile_adam_i32's reduction, weight_update.cl:260-314), with
 // D and A read in the transfer format `tq` (32: as they are; 16 / 8: quantised as the reference's
 // weight update reads its staged buffers).  D may have a zero pad column (OUT = 3 is read as 4).
-template <int ROWS>
-__device__ __forceinline__ void coop_wgrad(const float* D, int ldd, int OUT, const float* A, int lda,
-                                           int IN, float* gW, float* gb, int tq) {
+template <int ROWS, int TQ>
+__device__ __forceinline__ void coop_wgrad_fmt(const float* D, int ldd, int OUT, const float* A, int lda,
+                                               int IN, float* gW, float* gb) {
+    constexpr int tq = TQ;
     const int nib = IN >> 2, nob = (OUT + 3) >> 2;
     for (int b = threadIdx.x; b < nib * nob; b += ROWS) {
         const int ob = b / nib, ib = b - ob * nib;
@@ -103,7 +104,7 @@ __device__ __forceinline__ void coop_wgrad(const float* D, int ldd, int OUT, con
             const float4 av = *reinterpret_cast<const float4*>(A + r * lda + ib * 4);
             float dd[4] = {dv.x, dv.y, dv.z, dv.w};
             float aa[4] = {av.x, av.y, av.z, av.w};
-            if (tq != 32) {
+            if constexpr (tq != 32) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) { dd[i] = transfer_q(dd[i], tq); aa[i] = transfer_q(aa[i], tq); }
             }
@@ -128,6 +129,14 @@ __device__ __forceinline__ void coop_wgrad(const float* D, int ldd, int OUT, con
         for (int r = 0; r < ROWS; ++r) s += transfer_q(D[r * ldd + o], tq);
         gb[o] += s;
     }
+}
+// The format is fixed per launch: one branch here keeps the quantisation out of the fp32 loop.
+template <int ROWS>
+__device__ __forceinline__ void coop_wgrad(const float* D, int ldd, int OUT, const float* A, int lda,
+                                           int IN, float* gW, float* gb, int tq) {
+    if (tq == 16) coop_wgrad_fmt<ROWS, 16>(D, ldd, OUT, A, lda, IN, gW, gb);
+    else if (tq == 8) coop_wgrad_fmt<ROWS, 8>(D, ldd, OUT, A, lda, IN, gW, gb);
+    else coop_wgrad_fmt<ROWS, 32>(D, ldd, OUT, A, lda, IN, gW, gb);
 }
 
 // ---------------------------------------------------------------------------- fused kernel
