@@ -5,8 +5,10 @@ wait=True).
 
 Contracts, on the same rays and seeds: the pipelined form (step i+1 enqueued before step i's colours
 are taken; two pinned host arrays) returns the colours of the blocking form, step for step (within
-1e-5: the table's float atomics add in a different order from run to run, while the rays of
-consecutive steps differ completely); a pageable array passed as `out` is filled when its event is
+1e-3 absolute: the Hogwild table update adds its float atomics in a different order from run to
+run, and after five training steps at lr 5e-2 the two runs' colours drift apart by up to ~2e-4,
+while the rays of consecutive steps differ completely, so their colours differ by more than
+1e-2); a pageable array passed as `out` is filled when its event is
 waited on, or when the queue finishes.
 """
 import numpy as np
@@ -60,7 +62,7 @@ def test_pipelined_readback_matches_blocking(tmp_path):
     pending[1].wait()
     pipelined.append(pending[0].copy())
     for k in range(steps):
-        np.testing.assert_allclose(pipelined[k], blocking[k], rtol=1e-5, atol=1e-5, err_msg=f"step {k}")
+        np.testing.assert_allclose(pipelined[k], blocking[k], rtol=0, atol=1e-3, err_msg=f"step {k}")
         if k:
             assert np.abs(blocking[k] - blocking[k - 1]).max() > 1e-2   # consecutive steps are told apart
     assert np.isfinite(blocking[-1]).all() and np.abs(blocking[-1][:, :3]).sum() > 0
