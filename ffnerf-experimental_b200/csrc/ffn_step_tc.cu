@@ -290,21 +290,20 @@ __device__ __forceinline__ void encode_rows(const DevConfig& c, const float* __r
 
 // Scatter of one level's hash-grid gradient (ffnerf_OG.cl:2090-2173): the thread's F raw feature
 // gradients `gl` become (coef_l * g) * w_c at the 8 trilinear corners, added with vector atomics.
-// The lanes of a warp -- consecutive samples of one ray -- often sit in the same grid cell and would
-// add to the same 8 table entries (on the coarse levels nearly always; on the fine ones where the
-// occupancy-guided sampler packs samples densely): such lanes are grouped (match on the cell) and the
-// group's first lane adds the group's sums with one set of atomics.  The sums are formed by shuffles
-// when every group is a run of consecutive lanes, else through `scratch` (each lane writes its 8 x F
-// contributions to its shared-memory row, 8 F floats per thread, and the first lane adds the other
-// rows).  Levels from DEDUP_LEVELS up would add directly; merging on all 16 levels measured fastest
-// (cfg3 step 1.80 ms with the 10 coarsest, 1.74 ms with all 16, 1.86 ms with none): the reductions
-// themselves, not the matching, are the scatter's cost.
-constexpr int DEDUP_LEVELS = L;
+// The lanes of a warp -- consecutive samples of a ray, in ray order (of two or more rays below 32
+// samples per ray) -- often sit in the same grid cell and would add to the same 8 table entries (on
+// the coarse levels nearly always; on the fine ones where the occupancy-guided sampler packs samples
+// densely).  A ray leaves a (convex) cell only once, so a ray's lanes in one cell form a run: a lane starts a run when the lane before it is not scattering this
+// level or holds another cell (one shuffle of the 64-bit cell key, one ballot).  A segmented suffix
+// sum by shuffles leaves each run's total in its first lane, in log2(longest run) steps, and that lane
+// adds the run's sums with one set of atomics.  Merging on all 16 levels measured fastest (cfg3 step
+// 1.80 ms with the 10 coarsest, 1.74 ms with all 16, 1.86 ms with none, when the runs were found by
+// a match on the key; finding them from the neighbour's key took the step from 1.729 to 1.711 ms):
+// the reductions themselves are the scatter's cost.
 template <int F>
 __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restrict__ grad, V3 p, int lvl,
-                                              const float* gl, const float* coef, float* scratch) {
+                                              const float* gl, const float* coef) {
     const int lid = threadIdx.x & 31;
-    float* row = scratch + trow() * (8 * F);
     float gf[F];
     bool any = false;
 #pragma unroll
@@ -317,41 +316,17 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
     Corner8 k;
     uint64_t key;
     level_corners<F>(c, p, lvl, k, &key);
-    unsigned grp = 1u << lid;
-    if (lvl < DEDUP_LEVELS) {
-        const unsigned act = __activemask();
-        grp = __match_any_sync(act, key);
-        // Groups of consecutive lanes (always, when a warp holds samples of one ray): a segmented
-        // suffix sum by shuffles leaves each group's total in its first lane, in log2(group) steps.
-        const int first = __ffs(grp) - 1, last = 31 - __clz(grp);
-        const bool contiguous = (grp >> first) == (0xffffffffu >> (31 - (last - first)));
-        if (__all_sync(act, contiguous)) {
-            const int span = (int)__reduce_max_sync(act, (unsigned)(last - first + 1));
-            if (span > 1) {
-                float v[8 * F];
-#pragma unroll
-                for (int cc = 0; cc < 8; ++cc)
-#pragma unroll
-                    for (int f = 0; f < F; ++f) v[cc * F + f] = gf[f] * k.w[cc];
-                for (int off = 1; off < span; off <<= 1) {
-#pragma unroll
-                    for (int q = 0; q < 8 * F; ++q) {
-                        const float t = __shfl_down_sync(act, v[q], off);
-                        if (lid + off <= last) v[q] += t;
-                    }
-                }
-                if (lid == first) {
-#pragma unroll
-                    for (int cc = 0; cc < 8; ++cc) {
-                        if constexpr (F == 2) red_add2(grad + k.base[cc], v[2 * cc], v[2 * cc + 1]);
-                        else red_add4(grad + k.base[cc], v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
-                    }
-                }
-                return;
-            }
-        }
-    }
-    if (grp == (1u << lid)) {
+    const unsigned act = __activemask();
+    const unsigned klo = (unsigned)key, khi = (unsigned)(key >> 32);
+    const unsigned plo = __shfl_up_sync(act, klo, 1), phi = __shfl_up_sync(act, khi, 1);
+    const bool prev_in = lid > 0 && ((act >> (lid - 1)) & 1u);
+    const unsigned heads = __ballot_sync(act, !prev_in || plo != klo || phi != khi);
+    const unsigned upto = (2u << lid) - 1u;                 // lanes 0..lid (all 32 for lane 31)
+    const unsigned after = (heads | ~act) & ~upto;         // later lanes that end this lane's run
+    const int last = after ? __ffs(after) - 2 : 31;         // the run's last lane
+    const int first = 31 - __clz(heads & upto);             // the run's first lane
+    const int span = (int)__reduce_max_sync(act, (unsigned)(last - first + 1));
+    if (span == 1) {
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
             const float w = k.w[cc];
@@ -367,30 +342,21 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
     for (int cc = 0; cc < 8; ++cc)
 #pragma unroll
         for (int f = 0; f < F; ++f) v[cc * F + f] = gf[f] * k.w[cc];
+    // every lane of [first, last] is active, so the shuffles below read live values only
+    for (int off = 1; off < span; off <<= 1) {
 #pragma unroll
-    for (int q = 0; q < 8 * F; q += 4) *reinterpret_cast<float4*>(row + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-    __syncwarp(grp);
-    if (lid == __ffs(grp) - 1) {
-        unsigned rest = grp & (grp - 1u);   // the other members
-        while (rest) {
-            const int m = __ffs(rest) - 1;
-            rest &= rest - 1u;
-            const float* r = scratch + ((trow() & ~31) + m) * (8 * F);
-#pragma unroll
-            for (int q = 0; q < 8 * F; q += 4) {
-                const float4 t = *reinterpret_cast<const float4*>(r + q);
-                v[q] += t.x; v[q + 1] += t.y; v[q + 2] += t.z; v[q + 3] += t.w;
-            }
-        }
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-            if constexpr (F == 2)
-                red_add2(grad + k.base[cc], v[2 * cc], v[2 * cc + 1]);
-            else
-                red_add4(grad + k.base[cc], v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+        for (int q = 0; q < 8 * F; ++q) {
+            const float t = __shfl_down_sync(act, v[q], off);
+            if (lid + off <= last) v[q] += t;
         }
     }
-    __syncwarp(grp);
+    if (lid == first) {
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            if constexpr (F == 2) red_add2(grad + k.base[cc], v[2 * cc], v[2 * cc + 1]);
+            else red_add4(grad + k.base[cc], v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+        }
+    }
 }
 
 // Hash-grid gradient from the ACC region (scaled deltas times Wd_in).  F = 2: the thread's 32 values are
@@ -403,7 +369,7 @@ __device__ __forceinline__ void scatter_level(const DevConfig& c, float* __restr
 // lanes (a sample of a hitting ray) scatter.
 template <int F>
 __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t tmem, uint32_t col, float* __restrict__ grad,
-                                                  V3 p, float unscale, const float* coef, float* scratch, float* gbuf,
+                                                  V3 p, float unscale, const float* coef, float* gbuf,
                                                   bool live) {
     constexpr int LPOS = L * F;
     const uint32_t lane = tlane();
@@ -420,7 +386,7 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
                 float gl[F];
 #pragma unroll
                 for (int f = 0; f < F; ++f) gl[f] = g[li * F + f] * unscale;
-                scatter_level<F>(c, grad, p, j / F + li, gl, coef, scratch);
+                scatter_level<F>(c, grad, p, j / F + li, gl, coef);
             }
         }
         return;
@@ -449,7 +415,7 @@ __device__ __forceinline__ void scatter_from_tmem(const DevConfig& c, uint32_t t
         } else {
             gl[0] = t.x; gl[1] = t.y; gl[2] = t.z; gl[3] = t.w;
         }
-        scatter_level<F>(c, grad, p, lvl, gl, coef, scratch);
+        scatter_level<F>(c, grad, p, lvl, gl, coef);
     }
 }
 
@@ -901,11 +867,10 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         dw_started = true;
         // X0 and LO are dead: the next tile's pair lands while this tile scatters
         prefetch_next();
-        // the activation tiles are dead once the last MMAs completed: C1 holds the scatter's exchange
-        // rows, C2 the parked gradients
+        // the activation tiles are dead once the last MMAs completed: C2 holds the parked gradients
         if (!MLPB)
             scatter_from_tmem<F>(c, tmem, PL::ACC, a.grad_table, pn, 1.0f / DELTA_SCALE, a.hash_coef,
-                                 reinterpret_cast<float*>(tC1), reinterpret_cast<float*>(tC2), hit && valid);
+                                 reinterpret_cast<float*>(tC2), hit && valid);
         tc::fence_before_sync();
         tile_sync();
     }
