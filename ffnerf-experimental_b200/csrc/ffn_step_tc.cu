@@ -474,7 +474,11 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
     using PL = TcPlan<F, ND>;
     constexpr int LPOS = PL::LPOS;
     extern __shared__ __align__(1024) unsigned char smem_tc[];
-    const int grp = PL::GROUPS == 1 ? 0 : (int)(threadIdx.x >> 7);
+    // The group index and the tensor-memory base are broadcast from lane 0 (every lane holds the same
+    // value): the compiler then treats them, and every shared-memory and tensor-memory address and MMA
+    // descriptor formed from them, as warp-uniform, and the issuing thread forms its descriptors in
+    // uniform registers instead of converting each one (cfg3 step 1.723 -> 1.652 ms).
+    const int grp = PL::GROUPS == 1 ? 0 : __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 7), 0);
     unsigned char* gsm = smem_tc + PL::SHARED_BYTES + grp * PL::GROUP_BYTES;   // this group's tiles
     const DevConfig& c = a.c;
     const ParamLayout& lo = a.lo;
@@ -539,7 +543,7 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tmem_base = __shfl_sync(0xffffffffu, *tmem_slot, 0);
     const uint32_t tmem = tmem_base + (uint32_t)grp * PL::TMEM_GROUP;   // this group's columns
     uint32_t phase = 0;
     bool dw_started = false;
@@ -790,7 +794,8 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
                 if ((tid & 7) == 0 && k < 3) atomicAdd(bgrad + 16 + k, sum);
             }
         }
-        const uint32_t acc0 = dw_started ? 1u : 0u;
+        // every tile runs the backward: the weight-gradient accumulators start on the group's first tile
+        const uint32_t acc0 = tile != first_tile ? 1u : 0u;
         handoff();
         if (tid == 0) {
             gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC), 16, true, 64, 16, 128, acc0);            // dWc_out^T

@@ -22,6 +22,10 @@ mode (rays applied in order) ends 0.29 dB above its deferred mode on this protoc
 contract therefore compares the device with the reference kernels under the device's schedule (the
 lockstep run; tests/test_oracle_pin.py shows that one lockstep step is bit-identical to the deferred
 oracle's), and with the deferred oracle; the near-sequential run is reported and held to 1 dB.
+
+The device's side is the median of three runs: the immediate table update adds its float atomics in
+a different order from run to run, and single device runs of this protocol have ended anywhere in
+21.20-21.45 dB on B200s, which alone spans more than the contract's 0.2 dB.
 """
 import os
 from concurrent.futures import ThreadPoolExecutor
@@ -38,6 +42,7 @@ from ffn_config import param_layout, param_shapes
 from oracle import Oracle, OrcStep, RefKernels, make_orc_config
 
 STEPS, RAYS, SPR = 1600, 512, 64
+DEVICE_RUNS = 3
 
 
 def psnr(frames, images):
@@ -221,7 +226,8 @@ def train_cpu(model, data, steps=STEPS, seed=2024):
 
 @pytest.mark.gpu
 def test_psnr_matches_reference_after_training(tmp_path):
-    """Contracts: |PSNR(device) - PSNR(reference kernels, lockstep)| <= 0.2 dB and
+    """Contracts (PSNR(device) = the median of the device runs): |PSNR(device) - PSNR(reference
+    kernels, lockstep)| <= 0.2 dB and
     |PSNR(device) - PSNR(deferred oracle)| <= 0.2 dB; the reference kernels' near-sequential run within
     1 dB of the device (see the module docstring); the device's renderer and the reference's renderer
     agree on the device's model within 0.05 dB."""
@@ -231,11 +237,17 @@ def test_psnr_matches_reference_after_training(tmp_path):
         pytest.skip(f"reference kernels for the CPU not built: {e}")
     data = trainer.synthetic_scene_views("cfg1", 0)
     images, cams, K, W, H = data
-    dev = trainer.synthetic_nerf("cfg1", "fp32", 0, str(tmp_path / "dev"))
-    train_device(dev, data)
-    assert dev.native.status() == 0
     from render_gpu import render_frame
-    p_dev = psnr([render_frame(dev, c, K, W, H, rng_u32=i).cpu().numpy() for i, c in enumerate(cams)], images)
+    p_devs = []
+    for k in range(DEVICE_RUNS):
+        if k:
+            dev.native.close()
+        dev = trainer.synthetic_nerf("cfg1", "fp32", 0, str(tmp_path / f"dev{k}"))
+        train_device(dev, data)
+        assert dev.native.status() == 0
+        p_devs.append(psnr([render_frame(dev, c, K, W, H, rng_u32=i).cpu().numpy() for i, c in enumerate(cams)],
+                           images))
+    p_dev = float(np.median(p_devs))
     orc = OracleModel(trainer.synthetic_nerf("cfg1", "fp32", 0, str(tmp_path / "orc"), host_only=True))
     train_cpu(orc, data)
     p_orc = psnr(orc.render(cams, K, W, H), images)
@@ -248,10 +260,11 @@ def test_psnr_matches_reference_after_training(tmp_path):
     cross = RefModel(trainer.synthetic_nerf("cfg1", "fp32", 0, str(tmp_path / "x"), host_only=True))
     cross.load_from(dev)
     p_dev_refrender = psnr(cross.render(cams, K, W, H), images)
-    print(f"PSNR after {STEPS} steps: device {p_dev:.3f} dB (reference renderer {p_dev_refrender:.3f}), "
+    print(f"PSNR after {STEPS} steps: device {p_dev:.3f} dB (runs {', '.join(f'{p:.3f}' for p in p_devs)}; the last "
+          f"one {p_devs[-1]:.3f} dB with the reference renderer {p_dev_refrender:.3f}), "
           f"reference kernels lockstep {p_lock:.3f} dB / near-sequential {p_ref:.3f} dB, deferred oracle {p_orc:.3f} dB")
     assert p_ref > 12.0 and p_orc > 12.0 and p_lock > 12.0, (p_ref, p_orc, p_lock)   # the scene was learned
     assert abs(p_dev - p_lock) <= 0.2, (p_dev, p_lock)
     assert abs(p_dev - p_orc) <= 0.2, (p_dev, p_orc)
     assert abs(p_dev - p_ref) <= 1.0, (p_dev, p_ref)
-    assert abs(p_dev - p_dev_refrender) <= 0.05, (p_dev, p_dev_refrender)
+    assert abs(p_devs[-1] - p_dev_refrender) <= 0.05, (p_devs[-1], p_dev_refrender)
