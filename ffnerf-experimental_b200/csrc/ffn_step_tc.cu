@@ -48,18 +48,22 @@ struct TcPlan {
     // tiles side by side per CTA: two where both groups' tiles and tensor memory fit one SM
     static constexpr int GROUPS = (F == 2 && ND == 1) ? 2 : 1;
     static constexpr int THREADS = ROWS * GROUPS;
-    // ---- per CTA, shared by the groups: fp16 weights (rows = outputs, columns = inputs), hi copy
-    // at W_HI, lo copy at W_LO, then the one-hot tile and the fp32 biases
+    // ---- per CTA, shared by the groups: fp16 weights (rows = outputs, columns = inputs).  The
+    // 64-row weights have their hi copy at W_HI and their lo copy at W_LO (same offsets in both sets);
+    // each 16-row weight has its hi copy at W_DOUT / W_COUT (offsets from W_HI = 0) and its lo copy
+    // right behind it, W16_LO bytes on, so that the pair is one [32 x 64] operand and hi*Wh + hi*Wl is
+    // one N = 32 MMA per K step.  Then the one-hot tile and the fp32 biases.
     static constexpr int W_DIN = 0;                           // [64 x LPOS]
     static constexpr int W_D01 = W_DIN + 64 * LPOS * 2;       // [64 x 64] (ND = 2)
-    static constexpr int W_DOUT = W_D01 + (ND >= 2 ? 64 * 64 * 2 : 0);   // [16 x 64]
-    static constexpr int W_CIN = W_DOUT + 16 * 64 * 2;        // [64 x 32]
+    static constexpr int W_CIN = W_D01 + (ND >= 2 ? 64 * 64 * 2 : 0);   // [64 x 32]
     static constexpr int W_C01 = W_CIN + 64 * 32 * 2;         // [64 x 64]
-    static constexpr int W_COUT = W_C01 + 64 * 64 * 2;        // [16 x 64], rows 3..15 zero
-    static constexpr int W_SET = W_COUT + 16 * 64 * 2;        // bytes of one copy
+    static constexpr int W_SET = W_C01 + 64 * 64 * 2;         // bytes of one set
     static constexpr int W_HI = 0;
     static constexpr int W_LO = W_SET;
-    static constexpr int ONES = 2 * W_SET;                    // one-hot [128 x 8]
+    static constexpr int W16_LO = 16 * 64 * 2;
+    static constexpr int W_DOUT = 2 * W_SET;                  // [16 x 64], then its lo copy
+    static constexpr int W_COUT = W_DOUT + 2 * W16_LO;        // [16 x 64], rows 3..15 zero, then its lo copy
+    static constexpr int ONES = W_COUT + 2 * W16_LO;          // one-hot [128 x 8]
     static constexpr int BIAS = ONES + ROWS * 8 * 2;          // bd_0[64] bd_1[64] bd_out[16] bc_0[64] bc_1[64] bc_out[16]
     static constexpr int SHARED_BYTES = round_up_1k(BIAS + (64 * 2 + 16 + 64 * 2 + 16) * 4);
     // ---- per group, at SHARED_BYTES + group * GROUP_BYTES: fp16 operand tiles
@@ -150,6 +154,16 @@ __device__ __forceinline__ void gemm_fwd3(uint32_t d, uint32_t a_hi, uint32_t a_
     }
 }
 
+// Forward layer with 16 outputs and compensated operands, its weight pair stored as one [32 x 64]
+// tile (hi rows, then lo rows): ACC[:, 0:16] = Ah*Wh^T + Al*Wh^T and ACC[:, 16:32] = Ah*Wl^T, two MMAs
+// per K step instead of three (the issuing thread's time per MMA, not the tensor pipe, sets the
+// pace of these small GEMMs); acc_row16_pair adds the halves.  Plain operands: ACC = Ah*Wh^T.
+template <bool CP = true>
+__device__ __forceinline__ void gemm_fwd16(uint32_t d, uint32_t a_hi, uint32_t a_lo, int a_cols, uint32_t w_pair, int K) {
+    gemm(d, a_hi, a_cols, false, w_pair, a_cols, false, 128, CP ? 32 : 16, K, 0);
+    if constexpr (CP) gemm(d, a_lo, a_cols, false, w_pair, a_cols, false, 128, 16, K, 1);
+}
+
 // Backward-data layer with compensated operands: ACC = Dh*Wh + Dl*Wh + Dh*Wl, D [128 x K] K-major
 // (d_cols columns), W [K x N] read MN-major (w_cols columns).  One thread.
 template <bool CP = true>
@@ -190,6 +204,19 @@ __device__ __forceinline__ void acc_row(uint32_t tmem, uint32_t col, float (&v)[
         for (int i = 0; i < 16; ++i) v[j + i] = t[i];
     }
     tc::tmem_wait_ld();
+}
+
+// The 16 outputs of a gemm_fwd16 layer: the two accumulator halves added (compensated form).
+template <bool CP = true>
+__device__ __forceinline__ void acc_row16_pair(uint32_t tmem, uint32_t col, float (&v)[16]) {
+    if constexpr (CP) {
+        float t[32];
+        acc_row<32>(tmem, col, t);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = t[j] + t[16 + j];
+    } else {
+        acc_row<16>(tmem, col, v);
+    }
 }
 
 template <int N>
@@ -517,10 +544,10 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
     unsigned char* wl = smem_tc + PL::W_LO;
     stage_weight(wh + PL::W_DIN, wl + PL::W_DIN, P + lo.off[P_WD_IN], 64, 64, LPOS);
     if (ND >= 2) stage_weight(wh + PL::W_D01, wl + PL::W_D01, P + lo.off[P_WD_01], 64, 64, 64);
-    stage_weight(wh + PL::W_DOUT, wl + PL::W_DOUT, P + lo.off[P_WD_OUT], 16, 16, 64);
+    stage_weight(wh + PL::W_DOUT, wh + PL::W_DOUT + PL::W16_LO, P + lo.off[P_WD_OUT], 16, 16, 64);
     stage_weight(wh + PL::W_CIN, wl + PL::W_CIN, P + lo.off[P_WC_IN], 64, 64, 32);
     stage_weight(wh + PL::W_C01, wl + PL::W_C01, P + lo.off[P_WC_01], 64, 64, 64);
-    stage_weight(wh + PL::W_COUT, wl + PL::W_COUT, P + lo.off[P_WC_OUT], 3, 16, 64);
+    stage_weight(wh + PL::W_COUT, wh + PL::W_COUT + PL::W16_LO, P + lo.off[P_WC_OUT], 3, 16, 64);
     {
         float* sb = reinterpret_cast<float*>(smem_tc + PL::BIAS);
         for (int i = threadIdx.x; i < 64; i += blockDim.x) {
@@ -692,13 +719,12 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
             }
             handoff();
             if (tid == 0)
-                gemm_fwd3<CP>(tmem + PL::ACC, G(PL::HD + (ND - 1) * 128 * 64 * 2), G(PL::LO), 64, S(PL::W_HI + PL::W_DOUT),
-                          S(PL::W_LO + PL::W_DOUT), 16, 64);
+                gemm_fwd16<CP>(tmem + PL::ACC, G(PL::HD + (ND - 1) * 128 * 64 * 2), G(PL::LO), 64, S(PL::W_HI + PL::W_DOUT), 64);
             sync_mma();
             {
                 float v[32];
                 float dv[16];
-                acc_row<16>(tmem, PL::ACC, dv);
+                acc_row16_pair<CP>(tmem, PL::ACC, dv);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = dv[j] + bias[128 + j];
                 dout0 = v[0];
@@ -718,11 +744,11 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
             sync_mma();
             epi_bias_relu<CP>(tmem, PL::ACC, 64, bias + 208, tC2, tLO, 64);
             handoff();
-            if (tid == 0) gemm_fwd3<CP>(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_COUT), S(PL::W_LO + PL::W_COUT), 16, 64);
+            if (tid == 0) gemm_fwd16<CP>(tmem + PL::ACC, G(PL::C2), G(PL::LO), 64, S(PL::W_HI + PL::W_COUT), 64);
             sync_mma();
             {
                 float v[16];
-                acc_row<16>(tmem, PL::ACC, v);
+                acc_row16_pair<CP>(tmem, PL::ACC, v);
 #pragma unroll
                 for (int k = 0; k < 3; ++k) rgb[k] = sigmoid_soft(v[k] + bias[272 + k]);
             }
@@ -801,7 +827,7 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
             gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC), 16, true, 64, 16, 128, acc0);            // dWc_out^T
             if constexpr (CP) gemm(tmem + PL::DW_COUT_T, G(PL::C2), 64, true, G(PL::DC) + PL::DC_LO, 16, true, 64, 16, 128, 1);
             gemm_bwd3<CP>(tmem + PL::ACC, G(PL::DC), G(PL::DC) + PL::DC_LO, 16, S(PL::W_HI + PL::W_COUT),
-                      S(PL::W_LO + PL::W_COUT), 64, 64, 16);                                                       // dC2
+                      S(PL::W_HI + PL::W_COUT + PL::W16_LO), 64, 64, 16);                                                       // dC2
         }
         sync_mma();
         {
@@ -843,7 +869,7 @@ __global__ void __launch_bounds__(TcPlan<F, ND>::THREADS, 1) fused_step_tc_kerne
         if (tid == 0) {
             gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::XC), 32, true, 64, 16, 128, acc0);               // dWd_out^T
             if constexpr (CP) gemm(tmem + PL::DW_DOUT_T, hlast, 64, true, G(PL::LO), 32, true, 64, 16, 128, 1);
-            gemm_bwd3<CP>(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_DOUT), S(PL::W_LO + PL::W_DOUT),
+            gemm_bwd3<CP>(tmem + PL::ACC, G(PL::XC), G(PL::LO), 32, S(PL::W_HI + PL::W_DOUT), S(PL::W_HI + PL::W_DOUT + PL::W16_LO),
                       64, 64, 16);                                                                                // dH_last
         }
         sync_mma();
